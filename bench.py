@@ -1,0 +1,384 @@
+"""Benchmark of the W4A8 quantized linear (BASELINE north-star workload) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload w4a8|w4a4]
+
+One step = one pass of the hot path over one synthetic batch: activation rotation (ConvRot g256) + per-token
+int8 quantization, then the packed-int4 x int8 tcgen05 GEMM with the per-group affine epilogue, bf16 out.
+Workload (BASELINE north-star target T): M=4096 tokens, K=3072, N=12288, awq-layout weights with group 128.
+
+Timing: W warm-up steps, then K steps each bracketed by CUDA events on the launching stream; L2 is flushed
+(256 MiB memset, outside the events) before every step so every step reads its inputs from HBM.  The K step
+times are summed; the whole timed loop is bracketed by a barrier + synchronize; the max over ranks is taken.
+N > 1 runs N data-parallel replicas (sampler batches, one process per GPU, no collective in the step:
+"scaling": "weak"); ``--mode tp`` instead shards N column-parallel with an NCCL all-gather of the output.
+
+``--impl reference`` times the reference's CPU path (dequantize-and-matmul, oracle port) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (M, K, N, rot, description)
+    "w4a8": (4096, 3072, 12288, 256, "W4A8 linear, affine int4 g128 weights (bf16 scale/zero), ConvRot g256, "
+                                     "per-token int8 acts, bf16 out"),
+    "w4a4": (4096, 3072, 12288, 256, "ConvRot W4A4 linear, per-row int4 weights, per-token int4 acts, bf16 out"),
+}
+
+
+def _peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thr is not None:
+            self._thr.join()
+
+    def summary(self) -> dict:
+        if self._nv is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        nv = self._nv
+        names = {
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        seen = set()
+        for _, r in self.samples:
+            for k, bit in names.items():
+                if r & bit:
+                    seen.add(k)
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(seen), "samples": len(self.samples)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() and args.impl == "ours" else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allreduce_max(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" else torch.device("cpu")
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_problem(workload: str, seed: int, dev):
+    from oracle import ref  # synthetic inputs only (seeded generators with the BASELINE value distributions)
+    from comfy_quant_bench_b200 import ops
+    m, k, n, rot, _ = WORKLOADS[workload]
+    x_bits = ref.synth_activations(m, k, seed=seed)
+    x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16).to(dev)
+    w = torch.from_numpy(ref.synth_weight(n, k, seed=seed + 1)).to(dev)
+    bias = torch.from_numpy(ref.synth_bias(n, seed=seed + 2).view(np.int16)).view(torch.bfloat16).to(dev)
+    if workload == "w4a8":
+        qw, s, z = ops.quantize_affine_w4_weight(w, group_size=128, convrot_groupsize=rot)
+        weights = (qw, s, z)
+    else:
+        qw, sw = ops.quantize_convrot_w4a4_weight(w, convrot_groupsize=rot)
+        weights = (qw, sw)
+    del w
+    return x, x_bits, weights, bias
+
+
+def cpu_baseline(workload: str, rows: int, steps: int) -> dict:
+    """The reference CPU path (oracle port) on a bounded row-slice of the workload, all host threads."""
+    from oracle import cpu_path, ref
+    m, k, n, rot, _ = WORKLOADS[workload]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x_bits = ref.synth_activations(rows, k, seed=0)
+    w = ref.synth_weight(n, k, seed=1)
+    qr, sr, zr = ref.weight_quant_affine(w, rot, 128)
+    qw = torch.from_numpy(ref.pack_int4(qr))
+    s = torch.from_numpy(sr)
+    z = torch.from_numpy(zr)
+    bias = torch.from_numpy(ref.bf16_bits_to_f32(ref.synth_bias(n, seed=2)))
+    cpu_path.w4a8_affine_step(x_bits, rot, qw, s, z, bias)   # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_path.w4a8_affine_step(x_bits, rot, qw, s, z, bias)
+    dt = (time.perf_counter() - t0) / steps
+    tops = 2.0 * rows * n * k / dt / 1e12
+    return {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {m} tokens x N={n} x K={k} per step (activation quant + weight dequant + fp32 "
+                      f"F.linear, torch CPU), {steps} steps, {dt * 1e3:.1f} ms/step"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    m, k, n, rot, desc = WORKLOADS["w4a8"]
+    rows = args.cpu_rows
+    cb = cpu_baseline("w4a8", rows, max(1, args.steps))
+    line = {
+        "metric": "W4A8 linear INT8-TOPS", "value": cb["value"], "unit": "TOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2.0 * rows * n * k / cb["value"] / 1e9,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "w4a8_affine_linear", "desc": desc, "M": m, "K": k, "N": n, "convrot_groupsize": rot,
+                   "group_size": 128, "cpu_rows_per_step": rows},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    from comfy_quant_bench_b200 import ops, _lib
+    dev = torch.device("cuda", local)
+    m, k, n, rot, desc = WORKLOADS[args.workload]
+    x, x_bits, weights, bias = make_problem(args.workload, seed=rank, dev=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # stage buffers for the kernel-level timing (same kernels the fused call enqueues)
+    mp = (m + 15) // 16 * 16
+    if args.workload == "w4a8":
+        qw, s, z = weights
+
+        def stage1():
+            return ops.rotquant(x, rot, _lib.CQ_ACT_INT8_ROW, m_pad=mp, group_sums=True)
+
+        def stage2(a):
+            q, sx, gs = a
+            return ops.gemm_affine(q[:m], sx[:m], gs, qw, s, z, bias)
+
+        def public(xin):
+            return ops.w4a8_affine_linear(xin, qw, s, z, bias, group_size=128, convrot_groupsize=rot)
+    else:
+        qw, sw = weights
+
+        def stage1():
+            return ops.rotquant(x, rot, _lib.CQ_ACT_INT4_ROW, m_pad=mp, int4_as_int8=True)
+
+        def stage2(a):
+            q, sx, _ = a
+            return ops.gemm_rowcol(q[:m], sx[:m], qw, sw, bias)
+
+        def public(xin):
+            return ops.convrot_w4a4_linear(xin, qw, sw, bias, convrot_groupsize=rot)
+
+    def one_step(ev):
+        ev[0].record(stream)
+        a = stage1()
+        ev[1].record(stream)
+        stage2(a)
+        ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        one_step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    _lib.take_device_status()
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            one_step(evs[i])
+        torch.cuda.synchronize()
+    barrier(world)
+    st = _lib.take_device_status()
+    if st != (0, 0):
+        raise RuntimeError(f"device status {st}")
+    t_quant = [e[0].elapsed_time(e[1]) for e in evs]
+    t_gemm = [e[1].elapsed_time(e[2]) for e in evs]
+    total_ms = sum(a + b for a, b in zip(t_quant, t_gemm))
+    total_ms = allreduce_max(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    ops_per_step = 2.0 * m * n * k
+    value = ops_per_step * args.steps * world / (total_ms / 1e3) / 1e12
+
+    # e2e through the public API with host buffers: H2D of x from pinned memory, the op, D2H of the output
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    xin = torch.empty_like(x)
+    e2e_steps = max(3, min(args.steps, 50))
+    for _ in range(2):
+        xin.copy_(x_host, non_blocking=True)
+        y_host.copy_(public(xin), non_blocking=True)
+    torch.cuda.synchronize()
+    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(e2e_steps)]
+    barrier(world)
+    for i in range(e2e_steps):
+        flush.zero_()
+        ee[i][0].record(stream)
+        xin.copy_(x_host, non_blocking=True)
+        y_host.copy_(public(xin), non_blocking=True)
+        ee[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in ee), world) / e2e_steps
+    e2e_val = ops_per_step * world / (e2e_ms / 1e3) / 1e12
+
+    # library int8 GEMM on the same shape, for context (cuBLASLt through torch._int_mm)
+    lib_int8 = None
+    try:
+        a8 = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev)
+        b8 = torch.randint(-127, 128, (k, n), dtype=torch.int8, device=dev)
+        for _ in range(3):
+            torch._int_mm(a8, b8)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ts = []
+        for _ in range(10):
+            flush.zero_()
+            e0.record(stream)
+            torch._int_mm(a8, b8)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        lib_int8 = {"kernel": "torch._int_mm (cuBLASLt int8, no dequant epilogue)", "ms": statistics.median(ts),
+                    "tops": ops_per_step / (statistics.median(ts) / 1e3) / 1e12}
+    except Exception as exc:  # noqa: BLE001
+        lib_int8 = {"unavailable": str(exc).splitlines()[0][:200]}
+
+    if rank != 0:
+        return
+    peaks = _peaks()
+    gemm_ms = statistics.mean(t_gemm)
+    quant_ms = statistics.mean(t_quant)
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    achieved = ops_per_step / (gemm_ms / 1e3) / 1e12
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", f"gemm_{args.workload}_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    act_bytes = m * k * 2 + m * k * 1 + m * 4 + (k // 128) * mp * 4
+    line = {
+        "metric": "W4A8 linear INT8-TOPS" if args.workload == "w4a8" else "W4A4 linear INT8-TOPS",
+        "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{args.workload}_linear", "desc": desc, "M": m, "K": k, "N": n,
+                   "convrot_groupsize": rot, "group_size": 128 if args.workload == "w4a8" else None,
+                   "parallelism": f"dp{world}", "l2": "flushed before every step (256 MiB memset outside the events)",
+                   "inputs": "x ~ N(0,1) bf16 with 1% outlier channels x20, W ~ N(0,0.02), bias ~ N(0,0.01), seeded"},
+        "breakdown_ms": {"rotquant": quant_ms, "gemm": gemm_ms},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<affine>" if args.workload == "w4a8" else "gemm_kernel<rowcol>",
+                     "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
+                     "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16_tflops']} TFLOP/s; B200 int8 "
+                                    "dense rate is twice bf16)",
+                     "traffic": traffic,
+                     "algorithmic": f"2*M*N*K = {ops_per_step:.4g} int-ops per launch"},
+        "rotquant_roofline": {"bound": "hbm", "achieved": act_bytes / (quant_ms / 1e3) / 1e9,
+                              "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                              "frac": act_bytes / (quant_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                              "algorithmic_bytes": act_bytes},
+        "library_int8_gemm": lib_int8,
+        "e2e": {"value": e2e_val, "unit": "TOPS", "ms_per_step": e2e_ms, "h2d_bytes_per_step": m * k * 2,
+                "d2h_bytes_per_step": m * n * 2,
+                "path": "ops.w4a8_affine_linear (C ABI cq_linear_w4a8_affine) with pinned host buffers"
+                        if args.workload == "w4a8" else "ops.convrot_w4a4_linear (C ABI cq_linear_convrot_w4a4)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload if args.workload == "w4a8" else "w4a8", args.cpu_rows,
+                                            args.cpu_steps)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="w4a8")
+    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--cpu-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

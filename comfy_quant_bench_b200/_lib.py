@@ -1,0 +1,117 @@
+"""ctypes binding of libcq_b200.so (the C ABI declared in include/cq_b200.h).
+
+The library is the only implementation of the hot path: there is no CPU or eager fallback.  Loading fails
+with an exception when the shared object is missing, and every entry point raises on a nonzero status.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcq_b200.so")
+
+CQ_OK = 0
+CQ_ERR_ARG = 1
+CQ_ERR_SHAPE = 2
+CQ_ERR_ALIGN = 3
+CQ_ERR_CUDA = 4
+CQ_ERR_TIMEOUT = 5
+CQ_ERR_UNSUPPORTED = 6
+CQ_ERR_CAPACITY = 7
+
+CQ_ACT_INT8_ROW = 0
+CQ_ACT_INT4_ROW = 1
+CQ_ACT_INT4_GROUP = 2
+
+CQ_W_INT4_ROW = 0
+CQ_W_INT8_ROW = 1
+CQ_W_AFFINE_INT4_GROUP = 2
+CQ_W_INT4_GROUP_BF16UP = 3
+
+CQ_B_INT4_SIGNED = 0
+CQ_B_INT8 = 1
+
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes), one line per declaration of include/cq_b200.h
+SIGNATURES = {
+    "cq_version": (ctypes.c_char_p, []),
+    "cq_status_string": (ctypes.c_char_p, [_int]),
+    "cq_take_device_status": (_int, [ctypes.POINTER(_int), _vp]),
+    "cq_rotquant": (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _i64, _int, _vp, _vp, _vp, _vp]),
+    "cq_weight_rotquant": (_int, [_vp, _int, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp]),
+    "cq_unpack_int4": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "cq_gemm_rowcol": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "cq_gemm_affine": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "cq_linear_workspace_bytes": (_i64, [_i64, _i64]),
+    "cq_linear_convrot_w4a4": (_int, [_vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "cq_linear_w4a8_affine": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64,
+                                     _vp]),
+    "cq_linear_w8a8": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
+}
+
+
+class CQError(RuntimeError):
+    """A nonzero cq_status from the native library."""
+
+    def __init__(self, fn: str, status: int, message: str):
+        super().__init__(f"{fn} failed: {message} (status {status})")
+        self.status = status
+
+
+class CQShapeError(CQError, ValueError):
+    """Shape / argument rejected by the native library (mirrors the reference's ValueError / TORCH_CHECK)."""
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and type the shared library.  Raises if it is absent: there is no fallback path."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(f"{LIB_PATH} is missing: build it with `python -m comfy_quant_bench_b200.build` "
+                                  "(the quantized-linear path has no CPU fallback)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return load().cq_status_string(status).decode()
+
+
+def check(fn: str, status: int) -> None:
+    if status == CQ_OK:
+        return
+    msg = status_string(status)
+    if status in (CQ_ERR_ARG, CQ_ERR_SHAPE, CQ_ERR_ALIGN):
+        raise CQShapeError(fn, status, msg)
+    raise CQError(fn, status, msg)
+
+
+def call(name: str, *args) -> None:
+    check(name, getattr(load(), name)(*args))
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def take_device_status(stream=None) -> tuple[int, int]:
+    st = (ctypes.c_int * 2)()
+    call("cq_take_device_status", st, stream)
+    return int(st[0]), int(st[1])

@@ -1,0 +1,215 @@
+// extern "C" entry points of libcq_b200.so (declared in include/cq_b200.h): argument checks on the host,
+// then kernel launches on the caller's stream.  No entry point here allocates device memory.
+#include <cstdint>
+
+#include "kernels.cuh"
+
+
+namespace {
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int check_device() {
+  static int cached = -1;
+  if (cached < 0) {
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CQ_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return CQ_ERR_CUDA;
+    cached = (major == 10) ? CQ_OK : CQ_ERR_UNSUPPORTED;
+  }
+  return cached;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? CQ_OK : CQ_ERR_CUDA; }
+
+bool valid_rot(int r) { return r == 0 || r == 16 || r == 64 || r == 256; }
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+constexpr int64_t kMaxK = 32768;
+constexpr int64_t kMaxRows = 0x7FFFFFFF;
+
+}  // namespace
+
+extern "C" {
+
+const char* cq_version(void) { return "cq_b200 0.1.0 sm_100a"; }
+
+const char* cq_status_string(int status) {
+  switch (status) {
+    case CQ_OK: return "ok";
+    case CQ_ERR_ARG: return "invalid argument";
+    case CQ_ERR_SHAPE: return "unsupported shape";
+    case CQ_ERR_ALIGN: return "misaligned pointer";
+    case CQ_ERR_CUDA: return "CUDA error";
+    case CQ_ERR_TIMEOUT: return "device wait timed out";
+    case CQ_ERR_UNSUPPORTED: return "device is not sm_100";
+    case CQ_ERR_CAPACITY: return "problem exceeds a fixed internal limit";
+    default: return "unknown status";
+  }
+}
+
+int cq_take_device_status(int* status, void* stream) {
+  if (status == nullptr) return CQ_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int host[2] = {0, 0};
+  const int zero[2] = {0, 0};
+  if (cudaMemcpyFromSymbolAsync(host, cq::g_device_status, sizeof(host), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return CQ_ERR_CUDA;
+  if (cudaMemcpyToSymbolAsync(cq::g_device_status, zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return CQ_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return CQ_ERR_CUDA;
+  status[0] = host[0];
+  status[1] = host[1];
+  return CQ_OK;
+}
+
+int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, int mode, int act_group,
+                int64_t M_pad, int int4_as_int8, void* q, float* scale, float* group_sums, void* stream) {
+  if (M < 0 || M_pad < M || M_pad > kMaxRows) return CQ_ERR_SHAPE;
+  if (K < 256 || K % 256 != 0 || K > kMaxK) return CQ_ERR_SHAPE;
+  if (!valid_rot(rot_group)) return CQ_ERR_ARG;
+  if (mode != CQ_ACT_INT8_ROW && mode != CQ_ACT_INT4_ROW && mode != CQ_ACT_INT4_GROUP) return CQ_ERR_ARG;
+  if (mode == CQ_ACT_INT4_GROUP && act_group != 64 && act_group != 128) return CQ_ERR_ARG;
+  if (M_pad == 0) return CQ_OK;
+  if ((M > 0 && x == nullptr) || q == nullptr || scale == nullptr) return CQ_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(group_sums, 4)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), act_group, int4_as_int8, q, scale, nullptr, group_sums};
+  return cuda_status(cq::launch_act_rotquant(rot_group, swiglu != 0, mode, a, static_cast<cudaStream_t>(stream)));
+}
+
+int cq_weight_rotquant(const void* w, int w_is_bf16, int64_t N, int64_t K, int rot_group, int mode, int group,
+                       void* q, void* scale, void* zeros, void* stream) {
+  if (N < 0 || N > kMaxRows) return CQ_ERR_SHAPE;
+  if (K < 256 || K % 256 != 0 || K > kMaxK) return CQ_ERR_SHAPE;
+  if (!valid_rot(rot_group)) return CQ_ERR_ARG;
+  int kmode;
+  switch (mode) {
+    case CQ_W_INT4_ROW: kmode = 10; break;
+    case CQ_W_INT8_ROW: kmode = 11; break;
+    case CQ_W_AFFINE_INT4_GROUP: kmode = 12; break;
+    case CQ_W_INT4_GROUP_BF16UP: kmode = 13; break;
+    default: return CQ_ERR_ARG;
+  }
+  const bool grouped = mode == CQ_W_AFFINE_INT4_GROUP || mode == CQ_W_INT4_GROUP_BF16UP;
+  if (grouped && group != 64 && group != 128) return CQ_ERR_ARG;
+  if (N == 0) return CQ_OK;
+  if (w == nullptr || q == nullptr || scale == nullptr || (mode == CQ_W_AFFINE_INT4_GROUP && zeros == nullptr))
+    return CQ_ERR_ARG;
+  if (!aligned(w, 16) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(zeros, 2)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::RotQuantArgs a{w, N, N, static_cast<int>(K), grouped ? group : 0, 0, q, scale, zeros, nullptr};
+  return cuda_status(cq::launch_weight_rotquant(rot_group, w_is_bf16 != 0, kmode, a, static_cast<cudaStream_t>(stream)));
+}
+
+int cq_unpack_int4(const void* src, int64_t R, int64_t C, void* dst, void* stream) {
+  if (R < 0 || C < 0 || C % 16 != 0) return CQ_ERR_SHAPE;
+  if (R == 0 || C == 0) return CQ_OK;
+  if (src == nullptr || dst == nullptr) return CQ_ERR_ARG;
+  if (!aligned(src, 8) || !aligned(dst, 16)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  return cuda_status(cq::launch_unpack_int4(src, R * C / 2, dst, static_cast<cudaStream_t>(stream)));
+}
+
+static int check_gemm(const void* a, const void* b, const void* out, int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N <= 0 || M > kMaxRows || N > kMaxRows) return CQ_ERR_SHAPE;
+  if (K < 128 || K % 128 != 0 || K > (int64_t(1) << 17)) return CQ_ERR_SHAPE;
+  if (M == 0) return CQ_OK;
+  if (a == nullptr || b == nullptr || out == nullptr) return CQ_ERR_ARG;
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(out, 2)) return CQ_ERR_ALIGN;
+  return CQ_OK;
+}
+
+int cq_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_format, const float* sb,
+                   const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (b_format != CQ_B_INT4_SIGNED && b_format != CQ_B_INT8) return CQ_ERR_ARG;
+  if (int e = check_gemm(a, b, out, M, N, K)) return e;
+  if (M == 0) return CQ_OK;
+  if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
+  if (int dv = check_device()) return dv;
+  return cq::launch_gemm_rowcol(a, sa, b, b_format, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
+                                static_cast<int>(K), static_cast<cudaStream_t>(stream));
+}
+
+int cq_gemm_affine(const int8_t* a, const float* sa, const float* gsum, int64_t gsum_ld, const void* b_packed,
+                   const void* s_bf16, const void* z_bf16, const void* bias, void* out, int64_t M, int64_t N,
+                   int64_t K, int group, void* stream) {
+  if (group != 128) return CQ_ERR_ARG;
+  if (int e = check_gemm(a, b_packed, out, M, N, K)) return e;
+  if (M == 0) return CQ_OK;
+  if (sa == nullptr || gsum == nullptr || s_bf16 == nullptr || z_bf16 == nullptr) return CQ_ERR_ARG;
+  if (gsum_ld < round_up(M, 4) || gsum_ld % 4 != 0) return CQ_ERR_SHAPE;
+  if (!aligned(gsum, 16)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  return cq::launch_gemm_affine(a, sa, gsum, gsum_ld, b_packed, s_bf16, z_bf16, bias, out, static_cast<int>(M),
+                                static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------------------------
+// fused linears: activation stage into the caller's workspace, then the GEMM
+// ---------------------------------------------------------------------------------------------
+static int64_t ws_mpad(int64_t M) { return round_up(M > 0 ? M : 1, 16); }
+
+int64_t cq_linear_workspace_bytes(int64_t M, int64_t K) {
+  if (M < 0 || K <= 0) return -1;
+  const int64_t mp = ws_mpad(M);
+  return round_up(mp * K, 256) + round_up(mp * 4, 256) + round_up((K / 128 + 1) * mp * 4, 256);
+}
+
+struct Workspace {
+  int8_t* xq;
+  float* sx;
+  float* gsum;
+  int64_t mpad;
+};
+
+static int carve(void* ws, int64_t ws_bytes, int64_t M, int64_t K, Workspace* w) {
+  const int64_t need = cq_linear_workspace_bytes(M, K);
+  if (ws == nullptr || ws_bytes < need) return CQ_ERR_ARG;
+  if (!aligned(ws, 256)) return CQ_ERR_ALIGN;
+  w->mpad = ws_mpad(M);
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  w->xq = reinterpret_cast<int8_t*>(p);
+  p += round_up(w->mpad * K, 256);
+  w->sx = reinterpret_cast<float*>(p);
+  p += round_up(w->mpad * 4, 256);
+  w->gsum = reinterpret_cast<float*>(p);
+  return CQ_OK;
+}
+
+int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, int act_bits,
+                           const void* qweight, const float* wscale, const void* bias, void* out, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  if (act_bits != 4 && act_bits != 8) return CQ_ERR_ARG;
+  if (M == 0) return CQ_OK;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  const int mode = act_bits == 4 ? CQ_ACT_INT4_ROW : CQ_ACT_INT8_ROW;
+  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, mode, 0, w.mpad, 1, w.xq, w.sx, nullptr, stream)) return e;
+  return cq_gemm_rowcol(w.xq, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream);
+}
+
+int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
+                          const void* qweight, const void* s_bf16, const void* z_bf16, int group, const void* bias,
+                          void* out, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (M == 0) return CQ_OK;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, 0, w.xq, w.sx, w.gsum, stream))
+    return e;
+  return cq_gemm_affine(w.xq, w.sx, w.gsum, w.mpad, qweight, s_bf16, z_bf16, bias, out, M, N, K, group, stream);
+}
+
+int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,
+                   const float* wscale, const void* bias, void* out, void* workspace, int64_t workspace_bytes,
+                   void* stream) {
+  if (M == 0) return CQ_OK;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, 0, w.xq, w.sx, nullptr, stream))
+    return e;
+  return cq_gemm_rowcol(w.xq, w.sx, weight, CQ_B_INT8, wscale, bias, out, M, N, K, stream);
+}
+
+}  // extern "C"

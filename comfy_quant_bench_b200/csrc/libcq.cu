@@ -1,0 +1,5 @@
+// Unity build of libcq_b200.so: one translation unit, so the device status word and every kernel live in the
+// same module (no relocatable device code needed).
+#include "rotquant.cu"
+#include "gemm_sm100.cu"
+#include "capi.cu"

@@ -1,0 +1,339 @@
+"""Torch-level operators of the quantized-linear hot path, mirroring comfy-kitchen's CUDA backend API.
+
+Names, argument meaning and error behaviour follow the call sites in comfy-quant-bench:
+
+* ``quantize_int4_rowwise_convrot64(x, convrot_groupsize)`` (``g64_quant_test.py:105-112``,
+  ``node/__init__.py:148``) and ``swiglu_quantize_int4_rowwise_convrot64(h)`` (``tools/ck_swiglu/swiglu_quant.cu:111-137``);
+* ``quant(x, group, swiglu, pad)``: the reference's own per-group activation quantizer
+  (``experiments/qwen21-kernel/kernels/g64_quant.cu:113-130``);
+* ``quantize_convrot_w4a4_weight`` / ``quantize_int8_convrot_weight`` (``tools/_formats.py:72-76, 149-156``) and
+  ``quantize_affine_w4_weight`` (the awq_w4a16 layout, ``tools/_formats.py:191-212``) - the converter kernels;
+* ``int4_linear`` (``g64_bench6.py:109``), ``convrot_w4a4_linear`` (``patches/comfy_kitchen_swiglu_w4a4_fused.patch:41-95``),
+  ``int8_linear`` (``tools/_native_probe.py:234-255``) and ``w4a8_affine_linear`` (the BASELINE W4A8 linear).
+
+Every op runs the CUDA kernels of libcq_b200.so on the input's device and the current torch stream.  Inputs
+on the CPU or on a non-sm_100 device are rejected: there is no eager fallback.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+ROT_GROUPS = (0, 16, 64, 256)
+INT4_GROUP_SIZE = 64          # comfy-kitchen's loader constant (tools/_formats.py:57-59)
+
+
+def _stream(dev: torch.device):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("comfy_quant_bench_b200 ops run on CUDA tensors only (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _check_rot(g: int) -> int:
+    g = int(g)
+    if g not in ROT_GROUPS:
+        raise ValueError(f"convrot_groupsize must be one of {ROT_GROUPS[1:]} (or 0 for none), got {g}")
+    return g
+
+
+def _as2d(x: torch.Tensor) -> torch.Tensor:
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(torch.bfloat16)
+    return x2.contiguous()
+
+
+def _bias_bf16(bias: torch.Tensor | None) -> torch.Tensor | None:
+    if bias is None:
+        return None
+    return bias.to(torch.bfloat16).contiguous()
+
+
+# --------------------------------------------------------------------------------------------------
+# activation quantizers
+# --------------------------------------------------------------------------------------------------
+
+def rotquant(x: torch.Tensor, rot_group: int, mode: int, *, swiglu: bool = False, act_group: int = 0,
+             m_pad: int | None = None, int4_as_int8: bool = False, group_sums: bool = False):
+    """Raw activation stage: returns (q, scale, gsum or None).  See cq_rotquant in include/cq_b200.h."""
+    dev = _require_cuda(x)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    k = x2.shape[1] // 2 if swiglu else x2.shape[1]
+    mp = m if m_pad is None else int(m_pad)
+    if mode == _lib.CQ_ACT_INT8_ROW or int4_as_int8:
+        q = torch.empty(mp, k, dtype=torch.int8, device=dev)
+    else:
+        q = torch.empty(mp, k // 2, dtype=torch.int8, device=dev)
+    if mode == _lib.CQ_ACT_INT4_GROUP:
+        scale = torch.empty(k // act_group, mp, dtype=torch.float32, device=dev)
+    else:
+        scale = torch.empty(mp, dtype=torch.float32, device=dev)
+    gs = torch.empty(k // 128, mp, dtype=torch.float32, device=dev) if group_sums else None
+    _lib.call("cq_rotquant", _ptr(x2), m, k, _check_rot(rot_group), int(bool(swiglu)), int(mode), int(act_group), mp,
+              int(bool(int4_as_int8)), _ptr(q), _ptr(scale), _ptr(gs), _stream(dev))
+    return q, scale, gs
+
+
+def quantize_int4_rowwise_convrot64(x: torch.Tensor, convrot_groupsize: int = 256):
+    """Rotate (block Hadamard) + per-token int4: (q [M, K/2] int8 packed, scale [M] f32)."""
+    q, s, _ = rotquant(x, convrot_groupsize, _lib.CQ_ACT_INT4_ROW)
+    return q, s
+
+
+def swiglu_quantize_int4_rowwise_convrot64(h: torch.Tensor):
+    """silu(gate)*up (fp32, rounded once to bf16) + ConvRot-256 + per-token int4 from h = [gate | up]."""
+    if h.shape[-1] % 2:
+        raise ValueError("h must hold gate | up halves")
+    k = h.shape[-1] // 2
+    if k % 256 or k > 16384:
+        raise ValueError("K must be a multiple of 256 and <= 16384")
+    q, s, _ = rotquant(h, 256, _lib.CQ_ACT_INT4_ROW, swiglu=True)
+    return q, s
+
+
+def quantize_int8_rowwise_convrot(x: torch.Tensor, convrot_groupsize: int = 256, *, swiglu: bool = False):
+    """Rotate + per-token int8: (q [M, K] int8, scale [M] f32)."""
+    q, s, _ = rotquant(x, convrot_groupsize, _lib.CQ_ACT_INT8_ROW, swiglu=swiglu)
+    return q, s
+
+
+def quant(x: torch.Tensor, group: int, swiglu: bool = False, pad: int = 128):
+    """The reference's per-group quantizer: ConvRot-256, int4 per (token, group) with bf16-up scales.
+
+    Returns q [M_pad, K/2] packed and s [K/group, M_pad] f32; rows M..M_pad-1 are zero.
+    """
+    if group not in (64, 128):
+        raise ValueError("group 64 or 128")
+    m = x.reshape(-1, x.shape[-1]).shape[0]
+    mp = (m + pad - 1) // pad * pad
+    q, s, _ = rotquant(x, 256, _lib.CQ_ACT_INT4_GROUP, swiglu=swiglu, act_group=group, m_pad=mp)
+    return q, s
+
+
+# --------------------------------------------------------------------------------------------------
+# weight quantizers (the converter's rotate-and-quantize step)
+# --------------------------------------------------------------------------------------------------
+
+def _weight_in(weight: torch.Tensor):
+    _require_cuda(weight)
+    if weight.dim() != 2:
+        raise ValueError("weight must be 2-D [N, K]")
+    if weight.dtype == torch.bfloat16:
+        return weight.contiguous(), 1
+    return weight.to(torch.float32).contiguous(), 0
+
+
+def quantize_convrot_w4a4_weight(weight: torch.Tensor, convrot_groupsize: int = 256,
+                                 quant_group_size: int = INT4_GROUP_SIZE, stochastic_rounding: int = 0):
+    """ConvRot W4A4 weight: (qdata [N, K/2] int8 packed signed int4, scale [N] f32)."""
+    if quant_group_size != INT4_GROUP_SIZE:
+        raise ValueError(f"int4 MMA kernel requires quant_group_size {INT4_GROUP_SIZE}")
+    if stochastic_rounding:
+        raise ValueError("stochastic_rounding is not supported (the converters always pass 0)")
+    w, is_bf16 = _weight_in(weight)
+    n, k = w.shape
+    q = torch.empty(n, k // 2, dtype=torch.int8, device=w.device)
+    s = torch.empty(n, dtype=torch.float32, device=w.device)
+    _lib.call("cq_weight_rotquant", _ptr(w), is_bf16, n, k, _check_rot(convrot_groupsize), _lib.CQ_W_INT4_ROW, 0,
+              _ptr(q), _ptr(s), None, _stream(w.device))
+    return q, s
+
+
+def quantize_int8_convrot_weight(weight: torch.Tensor, group_size: int = 256):
+    """int8_tensorwise (ConvRot when group_size > 0): (qdata [N, K] int8, scale [N, 1] f32)."""
+    w, is_bf16 = _weight_in(weight)
+    n, k = w.shape
+    q = torch.empty(n, k, dtype=torch.int8, device=w.device)
+    s = torch.empty(n, 1, dtype=torch.float32, device=w.device)
+    _lib.call("cq_weight_rotquant", _ptr(w), is_bf16, n, k, _check_rot(group_size), _lib.CQ_W_INT8_ROW, 0,
+              _ptr(q), _ptr(s), None, _stream(w.device))
+    return q, s
+
+
+def quantize_affine_w4_weight(weight: torch.Tensor, group_size: int = 128, convrot_groupsize: int = 0):
+    """Asymmetric per-group int4 in the awq_w4a16 layout: W ~ (q - 8) * scale + zeros.
+
+    Returns (qweight [N, K/2] int8 packed uint4, scale bf16 [K/G, N], zeros bf16 [K/G, N]).
+    """
+    w, is_bf16 = _weight_in(weight)
+    n, k = w.shape
+    q = torch.empty(n, k // 2, dtype=torch.int8, device=w.device)
+    s = torch.empty(k // group_size, n, dtype=torch.bfloat16, device=w.device)
+    z = torch.empty(k // group_size, n, dtype=torch.bfloat16, device=w.device)
+    _lib.call("cq_weight_rotquant", _ptr(w), is_bf16, n, k, _check_rot(convrot_groupsize),
+              _lib.CQ_W_AFFINE_INT4_GROUP, int(group_size), _ptr(q), _ptr(s), _ptr(z), _stream(w.device))
+    return q, s, z
+
+
+def quantize_int4_groupwise_weight(weight: torch.Tensor, group_size: int = 128, convrot_groupsize: int = 256):
+    """Per-group symmetric int4 with bf16-up scales (the reference's pol 1/3/4 weights): (q packed, s [K/G, N])."""
+    w, is_bf16 = _weight_in(weight)
+    n, k = w.shape
+    q = torch.empty(n, k // 2, dtype=torch.int8, device=w.device)
+    s = torch.empty(k // group_size, n, dtype=torch.float32, device=w.device)
+    _lib.call("cq_weight_rotquant", _ptr(w), is_bf16, n, k, _check_rot(convrot_groupsize),
+              _lib.CQ_W_INT4_GROUP_BF16UP, int(group_size), _ptr(q), _ptr(s), None, _stream(w.device))
+    return q, s
+
+
+# --------------------------------------------------------------------------------------------------
+# GEMMs and fused linears
+# --------------------------------------------------------------------------------------------------
+
+def gemm_rowcol(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, bias=None, *,
+                b_int8: bool = False) -> torch.Tensor:
+    """out = (a @ b^T) * sa[:, None] * sb[None, :] + bias -> bf16.  a int8 codes [M, K]; b packed int4 or int8."""
+    dev = _require_cuda(a, sa, b, sb, bias)
+    m, k = a.shape
+    n = b.shape[0]
+    if (b.shape[1] if b_int8 else 2 * b.shape[1]) != k:
+        raise ValueError(f"Input K={k} does not match weight K={b.shape[1] * (1 if b_int8 else 2)}")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    bias = _bias_bf16(bias)
+    _lib.call("cq_gemm_rowcol", _ptr(a), _ptr(sa.float().contiguous()), _ptr(b),
+              _lib.CQ_B_INT8 if b_int8 else _lib.CQ_B_INT4_SIGNED, _ptr(sb.float().contiguous()), _ptr(bias),
+              _ptr(out), m, n, k, _stream(dev))
+    return out
+
+
+def int4_linear(qact: torch.Tensor, qweight: torch.Tensor, x_scale: torch.Tensor, wscales: torch.Tensor,
+                bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Packed int4 activations x packed int4 weights, row x column scales (comfy-kitchen int4_linear)."""
+    dev = _require_cuda(qact, qweight, x_scale, wscales, bias)
+    m, kh = qact.shape
+    a8 = torch.empty(m, 2 * kh, dtype=torch.int8, device=dev)
+    _lib.call("cq_unpack_int4", _ptr(qact.contiguous()), m, 2 * kh, _ptr(a8), _stream(dev))
+    out = gemm_rowcol(a8, x_scale.reshape(-1), qweight.contiguous(), wscales.reshape(-1), bias)
+    return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
+
+
+def _workspace(m: int, k: int, dev) -> torch.Tensor:
+    nbytes = int(_lib.load().cq_linear_workspace_bytes(m, k))
+    return torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+
+
+def _ws_ptr(ws: torch.Tensor) -> tuple[int, int]:
+    p = ws.data_ptr()
+    aligned = (p + 255) // 256 * 256
+    return aligned, ws.numel() - (aligned - p)
+
+
+def convrot_w4a4_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, bias: torch.Tensor | None = None,
+                        convrot_groupsize: int = 256, quant_group_size: int = INT4_GROUP_SIZE,
+                        linear_dtype: str = "int4", input_act: str | None = None) -> torch.Tensor:
+    """act(x) @ W^T + bias with ConvRot W4A4 weights (rotated per-row int4) and int4 or int8 activations."""
+    if linear_dtype not in {"int4", "int8"}:
+        raise ValueError(f"ConvRot W4A4 linear_dtype must be 'int4' or 'int8', got {linear_dtype!r}")
+    if quant_group_size != INT4_GROUP_SIZE:
+        raise ValueError(f"int4 MMA kernel requires quant_group_size {INT4_GROUP_SIZE}")
+    if input_act not in (None, "swiglu"):
+        raise ValueError(f"input_act {input_act!r} is not fused; apply it before the call")
+    swiglu = input_act == "swiglu"
+    k = x.shape[-1] // 2 if swiglu else x.shape[-1]
+    if k != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
+    if k % max(int(convrot_groupsize), 1) != 0:
+        raise ValueError(f"Input K={k} is not divisible by convrot_groupsize={convrot_groupsize}")
+    dev = _require_cuda(x, qweight, wscales, bias)
+    x2 = _as2d(x)
+    m, n = x2.shape[0], qweight.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    bias = _bias_bf16(bias)
+    _lib.call("cq_linear_convrot_w4a4", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), int(swiglu),
+              4 if linear_dtype == "int4" else 8, _ptr(qweight.contiguous()),
+              _ptr(wscales.float().reshape(-1).contiguous()), _ptr(bias), _ptr(out), wp, wn, _stream(dev))
+    out = out.reshape(*x.shape[:-1], n)
+    return out if x.dtype == torch.bfloat16 else out.to(x.dtype)
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None, convrot: bool = False, convrot_groupsize: int = 256,
+                input_act: str | None = None) -> torch.Tensor:
+    """W8A8 (int8_tensorwise) linear with optional ConvRot rotation and per-token int8 activations."""
+    if input_act not in (None, "swiglu"):
+        raise ValueError(f"input_act {input_act!r} is not fused; apply it before the call")
+    swiglu = input_act == "swiglu"
+    k = x.shape[-1] // 2 if swiglu else x.shape[-1]
+    if weight.dtype != torch.int8 or weight.shape[-1] != k:
+        raise ValueError(f"weight must be int8 [N, {k}]")
+    dev = _require_cuda(x, weight, weight_scale, bias)
+    x2 = _as2d(x)
+    m, n = x2.shape[0], weight.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    bias = _bias_bf16(bias)
+    _lib.call("cq_linear_w8a8", _ptr(x2), m, k, n, _check_rot(convrot_groupsize if convrot else 0), int(swiglu),
+              _ptr(weight.contiguous()), _ptr(weight_scale.float().reshape(-1).contiguous()), _ptr(bias), _ptr(out),
+              wp, wn, _stream(dev))
+    out = out.reshape(*x.shape[:-1], n)
+    dt = out_dtype or x.dtype
+    return out if dt == torch.bfloat16 else out.to(dt)
+
+
+def w4a8_affine_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, zeros: torch.Tensor,
+                       bias: torch.Tensor | None = None, group_size: int = 128, convrot_groupsize: int = 0,
+                       input_act: str | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """W4A8 linear with awq-layout weights (W = (q - 8) * scale + zeros, scale/zeros [K/G, N] bf16).
+
+    Activations are (optionally rotated and) quantized per token to int8; the GEMM accumulates int8 x int4
+    products per 128-group in int32 and applies scale, zero-point, activation scale and bias in fp32.
+    """
+    if group_size != 128:
+        raise ValueError("the W4A8 affine kernel supports group_size 128")
+    if input_act not in (None, "swiglu"):
+        raise ValueError(f"input_act {input_act!r} is not fused; apply it before the call")
+    swiglu = input_act == "swiglu"
+    k = x.shape[-1] // 2 if swiglu else x.shape[-1]
+    if k != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
+    n = qweight.shape[0]
+    if tuple(scale.shape) != (k // group_size, n) or tuple(zeros.shape) != (k // group_size, n):
+        raise ValueError(f"scale/zeros must be [{k // group_size}, {n}]")
+    dev = _require_cuda(x, qweight, scale, zeros, bias)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    bias = _bias_bf16(bias)
+    _lib.call("cq_linear_w4a8_affine", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), int(swiglu),
+              _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()),
+              _ptr(zeros.to(torch.bfloat16).contiguous()), int(group_size), _ptr(bias), _ptr(out), wp, wn,
+              _stream(dev))
+    out = out.reshape(*x.shape[:-1], n)
+    dt = out_dtype or x.dtype
+    return out if dt == torch.bfloat16 else out.to(dt)
+
+
+def gemm_affine(a: torch.Tensor, sa: torch.Tensor, gsum: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
+                zeros: torch.Tensor, bias=None) -> torch.Tensor:
+    """The affine GEMM alone on pre-quantized activations (a int8 [M, K], sa [M], gsum [K/128, M_pad])."""
+    dev = _require_cuda(a, sa, gsum, qweight, scale, zeros, bias)
+    m, k = a.shape
+    n = qweight.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    bias = _bias_bf16(bias)
+    _lib.call("cq_gemm_affine", _ptr(a), _ptr(sa), _ptr(gsum), gsum.shape[1], _ptr(qweight),
+              _ptr(scale.contiguous()), _ptr(zeros.contiguous()), _ptr(bias), _ptr(out), m, n, k, 128, _stream(dev))
+    return out

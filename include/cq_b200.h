@@ -1,0 +1,179 @@
+/*
+ * comfy-quant-bench B200 hot path: C ABI of libcq_b200.so.
+ *
+ * The quantized-linear path that comfy-quant-bench's formats execute inside ComfyUI, rebuilt for sm_100a:
+ *   1. activation rotation (block Hadamard, groups 256/64/16) fused with dynamic quantization (+ SwiGLU);
+ *   2. packed-int4-weight x int8/int4-activation GEMM on tcgen05 kind::i8 tensor cores (TMEM accumulators);
+ *   3. fused dequant epilogue back to bf16 (per-group affine weight scale/zero, per-token activation scale,
+ *      bias);
+ * plus the converter's weight rotate-and-quantize step as a kernel.
+ *
+ * Conventions
+ *   - All tensor arguments are raw DEVICE pointers to contiguous row-major arrays owned by the caller;
+ *     sizes are element counts.  bf16 data is passed as `const void*` / `void*` (2 bytes per element).
+ *   - Packed int4 stores two codes per byte, the low nibble holding the even column (the layout of
+ *     comfy-kitchen's int4 tensors and of tools/_formats.py in comfy-quant-bench).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are asynchronous: they enqueue
+ *     kernels and return.  Nothing here allocates device memory except where noted.
+ *   - Return value: CQ_OK (0) or a cq_status code.  Argument errors are detected on the host before any
+ *     launch.  Device-side failures (a bounded wait that ran out) are recorded in a device status word read
+ *     by cq_take_device_status().
+ */
+#ifndef CQ_B200_H
+#define CQ_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CQ_API __attribute__((visibility("default")))
+#else
+#define CQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  CQ_OK = 0,
+  CQ_ERR_ARG = 1,          /* null pointer, bad enum value */
+  CQ_ERR_SHAPE = 2,        /* size / divisibility constraint violated */
+  CQ_ERR_ALIGN = 3,        /* pointer not 16-byte aligned where TMA or vector access needs it */
+  CQ_ERR_CUDA = 4,         /* a CUDA runtime / driver call failed */
+  CQ_ERR_TIMEOUT = 5,      /* device: a bounded wait ran out (recorded in the device status word) */
+  CQ_ERR_UNSUPPORTED = 6,  /* device is not sm_100 */
+  CQ_ERR_CAPACITY = 7      /* problem larger than a fixed internal limit */
+} cq_status;
+
+/* Activation quantization modes (cq_rotquant). */
+typedef enum {
+  CQ_ACT_INT8_ROW = 0,   /* per token, symmetric int8 (int8_linear / W4A8): scale = max(absmax/127, 1e-10)   */
+  CQ_ACT_INT4_ROW = 1,   /* per token, symmetric int4 (ConvRot W4A4):        scale = max(absmax/7, 1e-10)     */
+  CQ_ACT_INT4_GROUP = 2  /* per (token, act_group) int4, scale rounded UP to bf16; scales laid out [K/G, M_pad] */
+} cq_act_mode;
+
+/* Weight quantization modes (cq_weight_rotquant). */
+typedef enum {
+  CQ_W_INT4_ROW = 0,          /* ConvRot W4A4: s[n] = max(amax/7, 1e-12), signed int4 packed [N, K/2]        */
+  CQ_W_INT8_ROW = 1,          /* int8_tensorwise: s[n] = max(amax/127, 1e-12), int8 [N, K]                   */
+  CQ_W_AFFINE_INT4_GROUP = 2, /* awq layout: W = (q - 8) * s + z, q uint4 packed [N, K/2], s/z bf16 [K/G, N]    */
+  CQ_W_INT4_GROUP_BF16UP = 3  /* per-group symmetric int4, s = bf16_up(amax/7) f32 [K/G, N]                    */
+} cq_weight_mode;
+
+/* Weight operand encodings accepted by the GEMMs. */
+typedef enum {
+  CQ_B_INT4_SIGNED = 0,  /* packed signed int4 [N, K/2] (ConvRot W4A4)             */
+  CQ_B_INT8 = 1          /* int8 [N, K] (int8_tensorwise, decoded W4A8)           */
+} cq_b_format;
+
+/* Library version string, e.g. "cq_b200 0.1.0 sm_100a". */
+CQ_API const char* cq_version(void);
+/* Human-readable name of a cq_status code. */
+CQ_API const char* cq_status_string(int status);
+
+/* Copy the device status word of the current device into status[0..1] (code, site) and clear it.
+ * Synchronizes `stream`.  Returns CQ_OK or CQ_ERR_CUDA. */
+CQ_API int cq_take_device_status(int* status, void* stream);
+
+/*
+ * Activation rotation + dynamic quantization.
+ * Replaces comfy-kitchen's quantize_int4_rowwise_convrot64(x, 256) (called at
+ * experiments/qwen21-kernel/kernels/g64_quant_test.py:105-112, experiments/qwen21-kernel/node/__init__.py:148),
+ * the fused swiglu_quantize_int4_rowwise_convrot64(h) (tools/ck_swiglu/swiglu_quant.cu:111-137), the per-group
+ * quant(x, group, swiglu, pad) (experiments/qwen21-kernel/kernels/g64_quant.cu:113-130) and the int8 activation
+ * quantization inside w4a8_int8_linear / int8_linear (tools/_native_probe.py:201-255).
+ *
+ *   x          bf16 [M, K], or [M, 2K] = [gate | up] when swiglu != 0 (the product silu(gate)*up is quantized)
+ *   rot_group  0 (no rotation), 16, 64 or 256; K % max(rot_group, 256 if swiglu) == 0 ... see DESIGN notes
+ *   mode       cq_act_mode
+ *   act_group  64 or 128 for CQ_ACT_INT4_GROUP, else ignored
+ *   M_pad      >= M; rows M..M_pad-1 of q (and of scale for CQ_ACT_INT4_GROUP) are written as 0
+ *   q          int8 [M_pad, K] for CQ_ACT_INT8_ROW; packed int4 [M_pad, K/2] for the int4 modes,
+ *              or int8 codes [M_pad, K] when int4_as_int8 != 0 (what the fused linears feed the GEMM)
+ *   scale      f32 [M_pad] for the per-token modes, f32 [K/act_group, M_pad] for CQ_ACT_INT4_GROUP
+ *   group_sums NULL, or f32 [K/128, M_pad]: sum of the codes of each token over each 128-wide K group
+ *              (the affine zero-point term of cq_gemm_affine)
+ * Constraints: K % 512 == 0 or K % 256 == 0 (multiple of 256), K <= 32768; M >= 0.
+ */
+CQ_API int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, int mode, int act_group,
+                int64_t M_pad, int int4_as_int8, void* q, float* scale, float* group_sums, void* stream);
+
+/*
+ * Weight rotate-and-quantize (the converter kernel).
+ * Replaces comfy-kitchen's quantize_convrot_w4a4_weight(w, convrot_groupsize, quant_group_size=64, 0)
+ * (tools/_formats.py:72-76; restated at experiments/qwen21-kernel/node/__init__.py:89-126),
+ * quantize_int8_convrot_weight (tools/_formats.py:149-156) and produces the awq_w4a16 affine layout
+ * (tools/_formats.py:191-212, patches/comfyui_awq_w4a16_format.patch:79-80) used by the W4A8 linear.
+ *
+ *   w        f32 [N, K] (w_is_bf16 == 0) or bf16 [N, K]
+ *   q        packed int4 [N, K/2] (modes INT4_ROW, AFFINE, INT4_GROUP_BF16UP) or int8 [N, K] (INT8_ROW)
+ *   scale    f32 [N] (INT4_ROW, INT8_ROW), bf16 [K/group, N] (AFFINE), f32 [K/group, N] (INT4_GROUP_BF16UP)
+ *   zeros    bf16 [K/group, N] for AFFINE, else NULL
+ */
+CQ_API int cq_weight_rotquant(const void* w, int w_is_bf16, int64_t N, int64_t K, int rot_group, int mode, int group,
+                       void* q, void* scale, void* zeros, void* stream);
+
+/*
+ * Unpack int4 codes to int8 codes: src packed [R, C/2] -> dst int8 [R, C] (signed nibbles).
+ * Lets a caller holding comfy-kitchen-style packed int4 activations feed cq_gemm_rowcol.
+ */
+CQ_API int cq_unpack_int4(const void* src, int64_t R, int64_t C, void* dst, void* stream);
+
+/*
+ * out[m, n] = bf16( (sum_k a[m,k] * b[n,k]) * sa[m] * sb[n] + bias[n] )
+ * Replaces comfy-kitchen's int4_linear(qact, qweight, x_scale, wscales, bias, out_dtype)
+ * (experiments/qwen21-kernel/kernels/g64_bench6.py:109, patches/comfy_kitchen_swiglu_w4a4_fused.patch:37)
+ * and the int8 GEMM of int8_linear (tools/_native_probe.py:234-255), and the reference's own scale policy 0
+ * of g64_gemm6.gemm (experiments/qwen21-kernel/kernels/g64_gemm6.cu:383-411).
+ *
+ *   a      int8 codes [M, K] (int8, or int4 values held in int8)
+ *   sa     f32 [M]
+ *   b      CQ_B_INT4_SIGNED: packed [N, K/2]; CQ_B_INT8: int8 [N, K]
+ *   sb     f32 [N]
+ *   bias   bf16 [N] or NULL
+ *   out    bf16 [M, N]
+ * Constraints: K % 128 == 0; N % 16 == 0; pointers 16-byte aligned.
+ */
+CQ_API int cq_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_format, const float* sb,
+                   const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream);
+
+/*
+ * W4A8 affine linear, the BASELINE north-star GEMM:
+ *   out[m, n] = bf16( sa[m] * sum_g ( s[g,n] * sum_{k in g} a[m,k]*(q[n,k]-8) + z[g,n] * gsum[g,m] ) + bias[n] )
+ * with q the awq_w4a16 uint4 codes (packed [N, K/2]) and s/z bf16 [K/group, N]
+ * (patches/comfyui_awq_w4a16_format.patch:79-80; the int8 x int4 policy family of
+ * experiments/qwen21-kernel/kernels/g64_gemm6.cu:5-11, 93-343).
+ *   a      int8 [M, K];  sa f32 [M];  gsum f32 [K/128, M_pad>=M] from cq_rotquant (sum of a over each group)
+ *   group  128
+ */
+CQ_API int cq_gemm_affine(const int8_t* a, const float* sa, const float* gsum, int64_t gsum_ld, const void* b_packed,
+                   const void* s_bf16, const void* z_bf16, const void* bias, void* out, int64_t M, int64_t N,
+                   int64_t K, int group, void* stream);
+
+/*
+ * Fused linears (activation stage + GEMM) with caller-provided scratch.  `workspace` must hold at least
+ * cq_linear_workspace_bytes(M, K) bytes of device memory (16-byte aligned).
+ *
+ * cq_linear_convrot_w4a4: comfy-kitchen convrot_w4a4_linear(x, qweight, wscales, bias, convrot_groupsize,
+ *   quant_group_size=64, linear_dtype, input_act) (signature: patches/comfy_kitchen_swiglu_w4a4_fused.patch:41-50,
+ *   compile_support.py:84-113).  act_bits 4 or 8 (linear_dtype "int4" / "int8"); swiglu: x is [M, 2K].
+ * cq_linear_w4a8_affine: the affine W4A8 linear (rotation optional, per-token int8 activations).
+ * cq_linear_w8a8: comfy-kitchen int8_linear(x, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize,
+ *   input_act) (tools/_native_probe.py:234-255).
+ */
+CQ_API int64_t cq_linear_workspace_bytes(int64_t M, int64_t K);
+CQ_API int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, int act_bits,
+                           const void* qweight, const float* wscale, const void* bias, void* out, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+CQ_API int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
+                          const void* qweight, const void* s_bf16, const void* z_bf16, int group, const void* bias,
+                          void* out, void* workspace, int64_t workspace_bytes, void* stream);
+CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,
+                   const float* wscale, const void* bias, void* out, void* workspace, int64_t workspace_bytes,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CQ_B200_H */

@@ -1,0 +1,78 @@
+"""CPU-side checks of the C ABI: the library loads without a GPU, exports every symbol include/cq_b200.h
+declares, and rejects bad arguments on the host before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "cq_b200.h"), encoding="utf-8").read()
+    return sorted(set(re.findall(r"CQ_API\s+[\w\s\*]+?\b(cq_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from comfy_quant_bench_b200 import _lib
+    return _lib.load()
+
+
+def test_header_and_binding_agree():
+    from comfy_quant_bench_b200 import _lib
+    assert _declared() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in _declared():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_status_strings(lib):
+    assert b"sm_100a" in lib.cq_version()
+    assert lib.cq_status_string(0) == b"ok"
+    assert lib.cq_status_string(2) == b"unsupported shape"
+
+
+def test_host_side_argument_checks_need_no_device(lib):
+    from comfy_quant_bench_b200 import _lib
+    vp = ctypes.c_void_p(16)
+    # K not a multiple of 256
+    assert lib.cq_rotquant(vp, 4, 300, 256, 0, 0, 0, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_SHAPE
+    # bad rotation group
+    assert lib.cq_rotquant(vp, 4, 512, 32, 0, 0, 0, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_ARG
+    # M_pad < M
+    assert lib.cq_rotquant(vp, 8, 512, 256, 0, 0, 0, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_SHAPE
+    # per-group mode needs act_group 64/128
+    assert lib.cq_rotquant(vp, 4, 512, 256, 0, 2, 32, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_ARG
+    # GEMM: K must be a multiple of 128; bad weight format
+    assert lib.cq_gemm_rowcol(vp, vp, vp, 0, vp, None, vp, 4, 8, 100, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_gemm_rowcol(vp, vp, vp, 7, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ARG
+    # affine: only group 128, gsum leading dimension >= M rounded to 4
+    assert lib.cq_gemm_affine(vp, vp, vp, 4, vp, vp, vp, None, vp, 4, 8, 128, 64, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_gemm_affine(vp, vp, vp, 2, vp, vp, vp, None, vp, 4, 8, 128, 128, None) == _lib.CQ_ERR_SHAPE
+    # misaligned pointer
+    assert lib.cq_gemm_rowcol(ctypes.c_void_p(17), vp, vp, 0, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ALIGN
+    # empty problems are no-ops
+    assert lib.cq_gemm_rowcol(None, None, None, 0, None, None, None, 0, 8, 128, None) == _lib.CQ_OK
+    # workspace sizing is pure arithmetic
+    assert lib.cq_linear_workspace_bytes(4096, 3072) >= 4096 * 3072 + 4096 * 4
+    assert lib.cq_linear_workspace_bytes(-1, 3072) == -1
+
+
+def test_python_errors_map_to_exceptions():
+    from comfy_quant_bench_b200 import _lib
+    with pytest.raises(_lib.CQShapeError):
+        _lib.check("cq_rotquant", _lib.CQ_ERR_SHAPE)
+    with pytest.raises(_lib.CQError):
+        _lib.check("cq_gemm_rowcol", _lib.CQ_ERR_TIMEOUT)
+    _lib.check("x", _lib.CQ_OK)
+
+
+def test_ops_reject_cpu_tensors():
+    import torch
+    from comfy_quant_bench_b200 import ops
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.quantize_int4_rowwise_convrot64(torch.zeros(2, 256, dtype=torch.bfloat16))

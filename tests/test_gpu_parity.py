@@ -1,0 +1,362 @@
+"""GPU parity: the CUDA path (through the C ABI, via comfy_quant_bench_b200.ops) against the CPU oracle.
+
+Bars (the north star's): integer and byte outputs bit-exact (codes, packed nibbles, group sums, int32
+accumulators); scales bit-exact; bf16 outputs within rel-L2 <= 1e-3 of the oracle's float64 result rounded to
+bf16, with at most 1e-3 of the elements off by more than one bf16 rounding.  The SwiGLU prologue calls the
+device expf, so its codes may differ by 1 at rounding ties (<= 0.1 % of codes), the reference's own rule.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from comfy_quant_bench_b200 import ops as _ops, _lib
+    _lib.load()
+    return _ops
+
+
+def bf16_dev(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def bits_of(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def f32_of(t: torch.Tensor) -> np.ndarray:
+    return ref.bf16_bits_to_f32(bits_of(t))
+
+
+def assert_bf16_close(got: torch.Tensor, want: np.ndarray, rel=REL_L2):
+    g = f32_of(got).astype(np.float64)
+    w = ref.bf16_round(np.asarray(want, np.float32)).astype(np.float64)
+    r = ref.rel_l2(want, g)
+    assert r <= rel, f"rel-L2 {r:.3e}"
+    # one bf16 rounding step of slack per element
+    ulp = np.abs(w) * 2.0 ** -7 + 1e-30
+    off = np.abs(g - w) > ulp
+    assert off.mean() <= 1e-3, f"{off.mean():.2e} of elements beyond one bf16 ulp"
+
+
+def codes_within_ties(got, want, frac=1e-3):
+    d = np.abs(np.asarray(got, np.int32) - np.asarray(want, np.int32))
+    assert d.max() <= 1
+    assert (d > 0).mean() <= frac
+
+
+def _check_status():
+    from comfy_quant_bench_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.take_device_status() == (0, 0)
+
+
+# ----------------------------------------------------------------------------------------------
+# activation rotation + quantization
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,k", [(1, 256), (37, 768), (64, 3072), (5, 16384), (3, 20480)])
+@pytest.mark.parametrize("rot", [0, 16, 64, 256])
+def test_rotquant_int8_rowwise_bit_exact(ops, m, k, rot):
+    x = ref.synth_activations(m, k, seed=m + k + rot)
+    q, s, gs = ops.rotquant(bf16_dev(x), rot, 0, group_sums=True)
+    qr, sr = ref.rotquant(x, rot, "int8")
+    assert np.array_equal(q.cpu().numpy(), qr.astype(np.int8))
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+    assert np.array_equal(gs.cpu().numpy().T, ref.group_sums(qr, 128).astype(np.float32))
+    _check_status()
+
+
+@pytest.mark.parametrize("m,k,rot", [(19, 1024, 256), (64, 3072, 64), (7, 512, 16), (3, 768, 0)])
+def test_rotquant_int4_rowwise_packed_bit_exact(ops, m, k, rot):
+    x = ref.synth_activations(m, k, seed=7 + k)
+    q, s = ops.quantize_int4_rowwise_convrot64(bf16_dev(x), rot)
+    qr, sr = ref.rotquant(x, rot, "int4")
+    assert np.array_equal(q.cpu().numpy(), ref.pack_int4(qr))
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+    q8, s8, _ = ops.rotquant(bf16_dev(x), rot, 1, int4_as_int8=True)
+    assert np.array_equal(q8.cpu().numpy(), qr.astype(np.int8))
+
+
+@pytest.mark.parametrize("group", [64, 128])
+@pytest.mark.parametrize("m,k", [(300, 4096), (77, 1024)])
+def test_groupwise_quant_matches_oracle_and_pads(ops, group, m, k):
+    x = ref.synth_activations(m, k, seed=group + m)
+    q, s = ops.quant(bf16_dev(x), group, False, 128)
+    mp = (m + 127) // 128 * 128
+    assert q.shape == (mp, k // 2) and s.shape == (k // group, mp)
+    qr, sr = ref.rotquant(x, 256, "int4_group", act_group=group)
+    assert np.array_equal(q[:m].cpu().numpy(), ref.pack_int4(qr))
+    assert np.array_equal(s[:, :m].cpu().numpy().view(np.uint32), sr.view(np.uint32))
+    assert (q[m:] == 0).all() and (s[:, m:] == 0).all()
+
+
+def test_groupwise_quant_matches_reference_golden(ops):
+    """The reference's own quantizer reference (g64_quant_test.ref), with its acceptance rule."""
+    import os
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_golden.npz")))
+    for tag, swiglu in (("act_m37_k1024_plain", False), ("act_m19_k512_swiglu", True)):
+        for grp in (64, 128):
+            q, s = ops.quant(bf16_dev(g[f"{tag}_x"]), grp, swiglu, 128)
+            m = g[f"{tag}_x"].shape[0]
+            codes_within_ties(ref.unpack_int4_signed(q[:m].cpu().numpy()), g[f"{tag}_g{grp}_q"])
+            ss = s[:, :m].cpu().numpy()
+            diff = ss != g[f"{tag}_g{grp}_s"]
+            assert diff.mean() <= 1e-3
+
+
+@pytest.mark.parametrize("mode,name", [(1, "int4"), (0, "int8")])
+def test_swiglu_rotquant_within_ties(ops, mode, name):
+    m, k = 48, 3072
+    h = ref.synth_activations(m, 2 * k, seed=11)
+    q, s, _ = ops.rotquant(bf16_dev(h), 256, mode, swiglu=True, int4_as_int8=True)
+    qr, sr = ref.rotquant(h, 256, name, swiglu=True)
+    codes_within_ties(q.cpu().numpy(), qr)
+    assert np.allclose(s.cpu().numpy(), sr, rtol=1e-5)
+
+
+def test_swiglu_fused_equals_quantizer_of_rounded_product(ops):
+    """test_comfyui_fase4_dispatch.py:108-110: the fused SwiGLU quantizer equals the plain quantizer fed
+    silu(gate)*up rounded once to bf16 (same device arithmetic on both sides)."""
+    m, k = 64, 1024
+    h = bf16_dev(ref.synth_activations(m, 2 * k, seed=5))
+    qf, sf = ops.swiglu_quantize_int4_rowwise_convrot64(h)
+    prod = (torch.nn.functional.silu(h[:, :k].float()) * h[:, k:].float()).to(torch.bfloat16)
+    qc, sc = ops.quantize_int4_rowwise_convrot64(prod, 256)
+    codes_within_ties(ref.unpack_int4_signed(qf.cpu().numpy()), ref.unpack_int4_signed(qc.cpu().numpy()), 2e-3)
+    assert torch.allclose(sf, sc, rtol=1e-5)
+
+
+# ----------------------------------------------------------------------------------------------
+# weight rotate-and-quantize
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("rot", [0, 64, 256])
+@pytest.mark.parametrize("bf16_in", [False, True])
+def test_weight_quantizers_bit_exact(ops, rot, bf16_in):
+    n, k = 96, 1536
+    w = ref.synth_weight(n, k, seed=rot + 3)
+    if bf16_in:
+        w = ref.bf16_round(w)
+    wt = torch.from_numpy(w).cuda()
+    wt = wt.to(torch.bfloat16) if bf16_in else wt
+    q, s = ops.quantize_convrot_w4a4_weight(wt, convrot_groupsize=rot) if rot else (None, None)
+    if rot:
+        qr, sr = ref.weight_quant_convrot_rowwise(w, rot)
+        assert np.array_equal(q.cpu().numpy(), ref.pack_int4(qr))
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+    q8, s8 = ops.quantize_int8_convrot_weight(wt, group_size=rot)
+    qr8, sr8 = ref.weight_quant_int8_rowwise(w, rot)
+    assert np.array_equal(q8.cpu().numpy(), qr8.astype(np.int8))
+    assert np.array_equal(s8.cpu().numpy().view(np.uint32), sr8.view(np.uint32))
+    qa, sa, za = ops.quantize_affine_w4_weight(wt, group_size=128, convrot_groupsize=rot)
+    qra, sra, zra = ref.weight_quant_affine(w, rot, 128)
+    assert np.array_equal(ref.unpack_uint4(qa.cpu().numpy()), qra)
+    assert np.array_equal(f32_of(sa), sra) and np.array_equal(f32_of(za), zra)
+    qg, sg = ops.quantize_int4_groupwise_weight(wt, group_size=128, convrot_groupsize=rot)
+    qrg, srg = ref.weight_quant_groupwise_bf16up(w, rot, 128)
+    assert np.array_equal(ref.unpack_int4_signed(qg.cpu().numpy()), qrg)
+    assert np.array_equal(sg.cpu().numpy(), srg)
+
+
+def test_weight_quant_matches_reference_golden(ops):
+    import os
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_golden.npz")))
+    w = torch.from_numpy(g["wq_in"]).cuda()
+    q, s = ops.quantize_convrot_w4a4_weight(w, 256)
+    codes_within_ties(ref.unpack_int4_signed(q.cpu().numpy()), ref.unpack_int4_signed(g["wq_p0_packed"]))
+    assert np.allclose(s.cpu().numpy(), g["wq_p0_scale"], rtol=1e-6)
+
+
+# ----------------------------------------------------------------------------------------------
+# GEMMs
+# ----------------------------------------------------------------------------------------------
+
+def _sparse_codes(rng, shape, density, lo, hi):
+    c = rng.integers(lo, hi + 1, size=shape)
+    return np.where(rng.random(shape) < density, c, 0)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 128, 128), (300, 200, 3072), (1000, 640, 1024)])
+def test_int32_accumulators_bit_exact_rowcol(ops, m, n, k):
+    """Unit scales and sparse +-1 codes keep |acc| <= 256, exactly representable in bf16: out == acc."""
+    rng = np.random.default_rng(m + n)
+    a = _sparse_codes(rng, (m, k), 0.05, -1, 1).astype(np.int8)
+    b = _sparse_codes(rng, (n, k), 0.05, -1, 1).astype(np.int8)
+    acc = ref.int_gemm(a, b)
+    assert np.abs(acc).max() <= 256
+    ones_m = torch.ones(m, device="cuda")
+    ones_n = torch.ones(n, device="cuda")
+    out4 = ops.gemm_rowcol(torch.from_numpy(a).cuda(), ones_m, torch.from_numpy(ref.pack_int4(b)).cuda(), ones_n)
+    assert np.array_equal(f32_of(out4), acc.astype(np.float32))
+    out8 = ops.gemm_rowcol(torch.from_numpy(a).cuda(), ones_m, torch.from_numpy(b).cuda(), ones_n, b_int8=True)
+    assert np.array_equal(f32_of(out8), acc.astype(np.float32))
+    _check_status()
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 128, 128), (300, 200, 3072)])
+def test_int32_accumulators_bit_exact_affine(ops, m, n, k):
+    """scale 1, zero 0: out == sum over groups of the exact int32 partials."""
+    rng = np.random.default_rng(m * 3 + n)
+    a = _sparse_codes(rng, (m, k), 0.05, -1, 1).astype(np.int8)
+    q = (8 + _sparse_codes(rng, (n, k), 0.05, -1, 1)).astype(np.int16)
+    acc = ref.int_gemm(a, q - 8)
+    s = torch.ones(k // 128, n, dtype=torch.bfloat16, device="cuda")
+    z = torch.zeros_like(s)
+    gsum = torch.from_numpy(ref.group_sums(a, 128).T.astype(np.float32).copy()).cuda()
+    out = ops.gemm_affine(torch.from_numpy(a).cuda(), torch.ones(m, device="cuda"), gsum,
+                          torch.from_numpy(ref.pack_int4(q)).cuda(), s, z)
+    assert np.array_equal(f32_of(out), acc.astype(np.float32))
+
+
+@pytest.mark.parametrize("m,n,k,bias", [(300, 200, 768, True), (512, 1024, 3072, True), (64, 384, 2048, False)])
+def test_gemm_rowcol_random_scales(ops, m, n, k, bias):
+    rng = np.random.default_rng(k + m)
+    a = rng.integers(-127, 128, size=(m, k)).astype(np.int8)
+    b = rng.integers(-7, 8, size=(n, k)).astype(np.int8)
+    sa = (rng.random(m) * 0.01 + 0.005).astype(np.float32)
+    sb = (rng.random(n) * 0.01 + 0.005).astype(np.float32)
+    bb = ref.synth_bias(n, seed=k) if bias else None
+    want = ref.linear_rowcol(a, sa, b, sb, None if bb is None else ref.bf16_bits_to_f32(bb))
+    out = ops.gemm_rowcol(torch.from_numpy(a).cuda(), torch.from_numpy(sa).cuda(),
+                          torch.from_numpy(ref.pack_int4(b)).cuda(), torch.from_numpy(sb).cuda(),
+                          None if bb is None else bf16_dev(bb))
+    assert_bf16_close(out, want)
+
+
+def test_int4_linear_matches_reference_policy0_golden(ops):
+    import os
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_golden.npz")))
+    out = ops.int4_linear(torch.from_numpy(g["gemm_a_packed"]).cuda(), torch.from_numpy(g["gemm_p0_sa"]).cuda(),
+                          torch.from_numpy(ref.pack_int4(g["gemm_b"])).cuda(), torch.from_numpy(g["gemm_p0_sb"]).cuda(),
+                          bf16_dev(g["gemm_bias"]))
+    assert_bf16_close(out, g["gemm_p0_out"].astype(np.float64))
+
+
+# ----------------------------------------------------------------------------------------------
+# fused linears (activation stage + GEMM) against the oracle pipeline
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,n,k,rot", [(300, 384, 1024, 256), (256, 3072, 3072, 0), (129, 256, 3072, 64)])
+def test_w4a8_affine_linear_vs_oracle(ops, m, n, k, rot):
+    x = ref.synth_activations(m, k, seed=m)
+    w = ref.synth_weight(n, k, seed=n)
+    bb = ref.synth_bias(n, seed=3)
+    qw, sw, zw = ops.quantize_affine_w4_weight(torch.from_numpy(w).cuda(), 128, rot)
+    out = ops.w4a8_affine_linear(bf16_dev(x), qw, sw, zw, bf16_dev(bb), group_size=128, convrot_groupsize=rot)
+    qx, sx = ref.rotquant(x, rot, "int8")
+    qr, sr, zr = ref.weight_quant_affine(w, rot, 128)
+    want = ref.linear_affine(qx, sx, qr, sr, zr, ref.bf16_bits_to_f32(bb), 128)
+    assert_bf16_close(out, want)
+    # the dequantize-and-matmul path (patches/tests/test_comfyui_fase4_dispatch.py:98) gives the same numbers
+    deq = ref.dequant_matmul(qx * sx[:, None].astype(np.float64), ref.dequant_affine(qr, sr, zr),
+                             ref.bf16_bits_to_f32(bb))
+    assert ref.rel_l2(deq, want) < 1e-6
+    # and the quantized linear tracks the full-precision one (liveness, cf. tools/verify_w4a4.py:32-38)
+    full = ref.bf16_bits_to_f32(x).astype(np.float64) @ w.astype(np.float64).T + ref.bf16_bits_to_f32(bb)
+    assert ref.rel_l2(full, f32_of(out)) < 0.15
+    _check_status()
+
+
+@pytest.mark.parametrize("m,n,k,rot,dtype", [(300, 384, 1024, 256, "int4"), (64, 512, 3072, 64, "int8"),
+                                             (200, 256, 768, 16, "int4")])
+def test_convrot_w4a4_linear_vs_oracle(ops, m, n, k, rot, dtype):
+    x = ref.synth_activations(m, k, seed=k)
+    w = ref.synth_weight(n, k, seed=m)
+    bb = ref.synth_bias(n, seed=5)
+    qw, sw = ops.quantize_convrot_w4a4_weight(torch.from_numpy(w).cuda(), rot)
+    out = ops.convrot_w4a4_linear(bf16_dev(x), qw, sw, bf16_dev(bb), convrot_groupsize=rot, linear_dtype=dtype)
+    qx, sx = ref.rotquant(x, rot, dtype)
+    qr, sr = ref.weight_quant_convrot_rowwise(w, rot)
+    want = ref.linear_rowcol(qx, sx, qr, sr, ref.bf16_bits_to_f32(bb))
+    assert_bf16_close(out, want)
+
+
+def test_convrot_w4a4_swiglu_linear(ops):
+    m, n, k = 128, 256, 1024
+    h = ref.synth_activations(m, 2 * k, seed=21)
+    w = ref.synth_weight(n, k, seed=22)
+    qw, sw = ops.quantize_convrot_w4a4_weight(torch.from_numpy(w).cuda(), 256)
+    out = ops.convrot_w4a4_linear(bf16_dev(h), qw, sw, None, input_act="swiglu")
+    qx, sx = ref.rotquant(h, 256, "int4", swiglu=True)
+    qr, sr = ref.weight_quant_convrot_rowwise(w, 256)
+    want = ref.linear_rowcol(qx, sx, qr, sr)
+    # a code flipped at a tie moves a row by one quantization step: compare at the linear's level
+    assert ref.rel_l2(want, f32_of(out)) < 5e-3
+
+
+def test_int8_linear_vs_oracle(ops):
+    m, n, k = 200, 320, 2048
+    x = ref.synth_activations(m, k, seed=31)
+    w = ref.synth_weight(n, k, seed=32)
+    qw, sw = ops.quantize_int8_convrot_weight(torch.from_numpy(w).cuda(), 256)
+    out = ops.int8_linear(bf16_dev(x), qw, sw, None, convrot=True, convrot_groupsize=256)
+    qx, sx = ref.rotquant(x, 256, "int8")
+    qr, sr = ref.weight_quant_int8_rowwise(w, 256)
+    assert_bf16_close(out, ref.linear_rowcol(qx, sx, qr, sr.reshape(-1)))
+
+
+# ----------------------------------------------------------------------------------------------
+# BASELINE full size: size-independent properties + a row slice against the oracle
+# ----------------------------------------------------------------------------------------------
+
+def test_full_size_w4a8_properties(ops):
+    m, n, k = 4096, 12288, 3072
+    x = ref.synth_activations(m, k, seed=0)
+    w = ref.synth_weight(n, k, seed=1)
+    xt = bf16_dev(x)
+    qw, sw, zw = ops.quantize_affine_w4_weight(torch.from_numpy(w).cuda(), 128, 256)
+    y1 = ops.w4a8_affine_linear(xt, qw, sw, zw, None, convrot_groupsize=256)
+    y2 = ops.w4a8_affine_linear(xt, qw, sw, zw, None, convrot_groupsize=256)
+    assert torch.equal(y1, y2), "two runs differ (shared-memory or TMEM race)"
+    y3 = ops.w4a8_affine_linear(xt * 2, qw, sw, zw, None, convrot_groupsize=256)
+    assert torch.equal(y3, y1 * 2), "output must scale exactly with a power-of-two input scale"
+    rows = np.r_[0:256, m - 256:m]
+    qx, sx = ref.rotquant(x[rows], 256, "int8")
+    qr, sr, zr = ref.weight_quant_affine(w, 256, 128)
+    assert np.array_equal(ref.unpack_uint4(qw.cpu().numpy()), qr)
+    want = ref.linear_affine(qx, sx, qr, sr, zr, None, 128)
+    assert_bf16_close(y1[torch.from_numpy(rows).cuda()], want)
+    _check_status()
+
+
+def test_full_size_w4a4_properties(ops):
+    m, n, k = 4096, 12288, 3072
+    x = ref.synth_activations(m, k, seed=0)
+    w = ref.synth_weight(n, k, seed=1)
+    xt = bf16_dev(x)
+    qw, sw = ops.quantize_convrot_w4a4_weight(torch.from_numpy(w).cuda(), 256)
+    y1 = ops.convrot_w4a4_linear(xt, qw, sw)
+    assert torch.equal(y1, ops.convrot_w4a4_linear(xt, qw, sw))
+    rows = np.r_[0:256, m - 256:m]
+    qx, sx = ref.rotquant(x[rows], 256, "int4")
+    qr, sr = ref.weight_quant_convrot_rowwise(w, 256)
+    assert_bf16_close(y1[torch.from_numpy(rows).cuda()], ref.linear_rowcol(qx, sx, qr, sr))
+
+
+# ----------------------------------------------------------------------------------------------
+# error behaviour (host-side checks, nothing launched)
+# ----------------------------------------------------------------------------------------------
+
+def test_errors_raise(ops):
+    from comfy_quant_bench_b200._lib import CQShapeError
+    x = torch.zeros(4, 300, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(CQShapeError):
+        ops.quantize_int4_rowwise_convrot64(x, 256)
+    with pytest.raises(ValueError):
+        ops.convrot_w4a4_linear(torch.zeros(4, 256, device="cuda"), torch.zeros(8, 64, dtype=torch.int8, device="cuda"),
+                                torch.ones(8, device="cuda"))
+    with pytest.raises(ValueError):
+        ops.quantize_int4_rowwise_convrot64(torch.zeros(4, 256, dtype=torch.bfloat16), 256)
+    with pytest.raises(ValueError):
+        ops.convrot_w4a4_linear(torch.zeros(4, 256, device="cuda"), torch.zeros(8, 128, dtype=torch.int8, device="cuda"),
+                                torch.ones(8, device="cuda"), linear_dtype="fp8")
