@@ -1,0 +1,94 @@
+"""Multi-GPU execution of the quantized linear: one process per GPU, torch.distributed for the plumbing.
+
+Two schemes, both new relative to comfy-quant-bench (which runs on one GPU):
+
+* ``ColumnParallelLinear``: rank r holds output rows ``[r*N/P, (r+1)*N/P)`` of the packed weight (and the
+  matching scale / zero columns and bias), runs the local W4A8 / W4A4 kernels on the full activation and
+  all-gathers the bf16 output columns over NCCL (NVLink / NVSwitch).  This is the path for large-token layers
+  whose weight or output does not fit one GPU's budget.
+* ``split_batch`` / data-parallel replicas: sampler batches (cond / uncond, several seeds) are split across
+  ranks with no collective in the step.
+
+The gather is the only collective; nothing in the kernels waits on a peer.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+
+
+def shard_bounds(n: int, rank: int, world: int) -> tuple[int, int]:
+    if n % world:
+        raise ValueError(f"out_features {n} is not divisible by the {world} ranks")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_affine(qweight, scale, zeros, bias, rank: int, world: int):
+    """Column shard of an awq-layout weight: qweight rows, scale/zeros columns ([K/G, N] layout), bias."""
+    a, b = shard_bounds(qweight.shape[0], rank, world)
+    return (qweight[a:b].contiguous(), scale[:, a:b].contiguous(), zeros[:, a:b].contiguous(),
+            None if bias is None else bias[a:b].contiguous())
+
+
+def shard_rowscaled(qweight, wscale, bias, rank: int, world: int):
+    """Column shard of a per-row-scaled weight (ConvRot W4A4 or int8): qweight rows, scale rows, bias."""
+    a, b = shard_bounds(qweight.shape[0], rank, world)
+    return (qweight[a:b].contiguous(), wscale.reshape(-1)[a:b].contiguous(),
+            None if bias is None else bias[a:b].contiguous())
+
+
+def gather_columns(local: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """[M, N/P] per rank -> [M, N] on every rank (rank-major column blocks), one all_gather_into_tensor."""
+    import torch.distributed as dist
+    m, nl = local.shape
+    buf = torch.empty(world * m, nl, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
+    return buf.view(world, m, nl).permute(1, 0, 2).reshape(m, world * nl)
+
+
+class ColumnParallelLinear:
+    """y = x @ W^T + b with W split over ranks by output rows and the output all-gathered.
+
+    ``local_linear(x2d) -> [M, N/P]`` runs this rank's shard; the factories below bind it to the CUDA ops.
+    """
+
+    def __init__(self, local_linear: Callable[[torch.Tensor], torch.Tensor], out_features: int, rank: int,
+                 world: int, group=None):
+        self.local_linear = local_linear
+        self.out_features = out_features
+        self.rank = rank
+        self.world = world
+        self.group = group
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = x.reshape(-1, x.shape[-1])
+        y = self.local_linear(x2)
+        if self.world > 1:
+            y = gather_columns(y, self.world, self.group)
+        return y.reshape(*x.shape[:-1], self.out_features)
+
+    @classmethod
+    def w4a8_affine(cls, qweight, scale, zeros, bias, rank, world, group_size=128, convrot_groupsize=0, group=None):
+        from . import ops
+        q, s, z, b = shard_affine(qweight, scale, zeros, bias, rank, world)
+        return cls(lambda x2: ops.w4a8_affine_linear(x2, q, s, z, b, group_size=group_size,
+                                                     convrot_groupsize=convrot_groupsize),
+                   qweight.shape[0], rank, world, group)
+
+    @classmethod
+    def convrot_w4a4(cls, qweight, wscales, bias, rank, world, convrot_groupsize=256, linear_dtype="int4",
+                     group=None):
+        from . import ops
+        q, s, b = shard_rowscaled(qweight, wscales, bias, rank, world)
+        return cls(lambda x2: ops.convrot_w4a4_linear(x2, q, s, b, convrot_groupsize=convrot_groupsize,
+                                                      linear_dtype=linear_dtype),
+                   qweight.shape[0], rank, world, group)
+
+
+def split_batch(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
+    """This rank's slice of a sampler batch (data-parallel replicas, no collective in the step)."""
+    n = x.shape[dim]
+    per = (n + world - 1) // world
+    return x.narrow(dim, min(rank * per, n), max(0, min(per, n - rank * per)))

@@ -1,0 +1,114 @@
+"""world_size-2 gloo tests of the multi-GPU host logic on CPU: column sharding + all-gather, data-parallel
+batch split, and a rank failure seen by its peer as an error (never as a hang).
+
+The local linear is a float stand-in (the sharding and gather logic is what is under test here); the CUDA
+path of the same classes is exercised on the GPU in test_gpu_dist.py.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, fn, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+    try:
+        q.put((rank, "ok", fn(rank, world)))
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, "err", f"{type(exc).__name__}: {exc}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def run_ranks(fn, world=2, timeout=60):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fn, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        rank, st, val = q.get(timeout=timeout)
+        out[rank] = (st, val)
+    for p in procs:
+        p.join(timeout=timeout)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def _column_parallel(rank, world):
+    from comfy_quant_bench_b200.dist import ColumnParallelLinear, shard_bounds
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(12, 8, generator=g)
+    x = torch.randn(5, 8, generator=g)
+    a, b = shard_bounds(12, rank, world)
+    lin = ColumnParallelLinear(lambda x2: x2 @ w[a:b].t(), 12, rank, world)
+    y = lin(x)
+    return float((y - x @ w.t()).abs().max())
+
+
+def _affine_shards(rank, world):
+    from comfy_quant_bench_b200.dist import shard_affine
+    q = torch.arange(8 * 4, dtype=torch.int8).reshape(8, 4)
+    s = torch.arange(2 * 8, dtype=torch.float32).reshape(2, 8)
+    qs, ss, zs, bs = shard_affine(q, s, s + 100, torch.arange(8.0), rank, world)
+    lo = rank * 4
+    assert torch.equal(qs, q[lo:lo + 4]) and torch.equal(ss, s[:, lo:lo + 4]) and torch.equal(bs, torch.arange(8.0)[lo:lo + 4])
+    return tuple(qs.shape)
+
+
+def _split(rank, world):
+    from comfy_quant_bench_b200.dist import split_batch
+    x = torch.arange(5)
+    return split_batch(x, rank, world).tolist()
+
+
+def _one_rank_fails(rank, world):
+    if rank == 1:
+        raise RuntimeError("rank 1 dies before the collective")
+    t = torch.zeros(2)
+    dist.all_reduce(t)   # the peer never joins: gloo's timeout turns this into an error
+    return "unreachable"
+
+
+def test_column_parallel_gather_equals_full_matmul():
+    out = run_ranks(_column_parallel)
+    assert all(st == "ok" and val < 1e-5 for st, val in out.values()), out
+
+
+def test_affine_shards_slice_rows_and_scale_columns():
+    out = run_ranks(_affine_shards)
+    assert out[0] == ("ok", (4, 4)) and out[1] == ("ok", (4, 4))
+
+
+def test_split_batch_covers_the_batch_once():
+    out = run_ranks(_split)
+    assert out[0][1] + out[1][1] == [0, 1, 2, 3, 4]
+
+
+def test_a_failed_rank_surfaces_as_an_error_on_its_peer():
+    out = run_ranks(_one_rank_fails, timeout=90)
+    assert out[1][0] == "err"
+    assert out[0][0] == "err"       # the survivor gets an error from its collective, not a hang
+
+
+def test_shard_bounds_reject_uneven_split():
+    from comfy_quant_bench_b200.dist import shard_bounds
+    with pytest.raises(ValueError):
+        shard_bounds(10, 0, 4)
