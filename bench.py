@@ -210,25 +210,27 @@ def run_ours(args, world, rank, local):
     mp = (m + 15) // 16 * 16
     if args.workload == "w4a8":
         qw, s, z = weights
+        zt = ops.prepare_affine_zeros(z, 128)   # once per weight, as the layout class does at load
 
         def stage1():
-            return ops.rotquant(x, rot, _lib.CQ_ACT_INT8_ROW, m_pad=mp, group_sums=True)
+            return ops.rotquant(x, rot, _lib.CQ_ACT_INT8_ROW, m_pad=mp, group_sums=True, kperm=True)
 
         def stage2(a):
             q, sx, gs = a
-            return ops.gemm_affine(q[:m], sx[:m], gs, qw, s, z, bias)
+            return ops.gemm_affine(q[:m], sx[:m], gs, qw, s, z, bias, a_kperm=True, zeros_prepared=zt)
 
         def public(xin):
-            return ops.w4a8_affine_linear(xin, qw, s, z, bias, group_size=128, convrot_groupsize=rot)
+            return ops.w4a8_affine_linear(xin, qw, s, z, bias, group_size=128, convrot_groupsize=rot,
+                                          zeros_prepared=zt)
     else:
         qw, sw = weights
 
         def stage1():
-            return ops.rotquant(x, rot, _lib.CQ_ACT_INT4_ROW, m_pad=mp, int4_as_int8=True)
+            return ops.rotquant(x, rot, _lib.CQ_ACT_INT4_ROW, m_pad=mp, int4_as_int8=True, kperm=True)
 
         def stage2(a):
             q, sx, _ = a
-            return ops.gemm_rowcol(q[:m], sx[:m], qw, sw, bias)
+            return ops.gemm_rowcol(q[:m], sx[:m], qw, sw, bias, a_kperm=True)
 
         def public(xin):
             return ops.convrot_w4a4_linear(xin, qw, sw, bias, convrot_groupsize=rot)

@@ -30,6 +30,9 @@ CQ_W_INT8_ROW = 1
 CQ_W_AFFINE_INT4_GROUP = 2
 CQ_W_INT4_GROUP_BF16UP = 3
 
+CQ_Q_INT8_CODES = 1
+CQ_Q_KPERM = 2
+
 CQ_B_INT4_SIGNED = 0
 CQ_B_INT8 = 1
 
@@ -45,8 +48,10 @@ SIGNATURES = {
     "cq_rotquant": (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _i64, _int, _vp, _vp, _vp, _vp]),
     "cq_weight_rotquant": (_int, [_vp, _int, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp]),
     "cq_unpack_int4": (_int, [_vp, _i64, _i64, _vp, _vp]),
-    "cq_gemm_rowcol": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
-    "cq_gemm_affine": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "cq_gemm_rowcol": (_int, [_vp, _int, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "cq_group_sum_cols": (_i64, [_i64]),
+    "cq_prepare_affine_zeros": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
+    "cq_gemm_affine": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_linear_workspace_bytes": (_i64, [_i64, _i64]),
     "cq_linear_convrot_w4a4": (_int, [_vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "cq_linear_w4a8_affine": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64,

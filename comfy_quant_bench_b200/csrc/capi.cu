@@ -64,18 +64,36 @@ int cq_take_device_status(int* status, void* stream) {
   return CQ_OK;
 }
 
+int64_t cq_group_sum_cols(int64_t K) { return K > 0 ? 64 * ((K / 128 + 31) / 32) : 0; }
+
+int cq_prepare_affine_zeros(const void* z_bf16, int64_t N, int64_t K, int group, void* zt_bf16, void* stream) {
+  if (group != 128) return CQ_ERR_ARG;
+  if (N < 0 || N > kMaxRows || K < 128 || K % 128 != 0 || K > kMaxK) return CQ_ERR_SHAPE;
+  if (N == 0) return CQ_OK;
+  if (z_bf16 == nullptr || zt_bf16 == nullptr) return CQ_ERR_ARG;
+  if (!aligned(z_bf16, 2) || !aligned(zt_bf16, 16)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  return cuda_status(cq::launch_prep_zt(z_bf16, static_cast<int>(N), static_cast<int>(K), zt_bf16,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
 int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, int mode, int act_group,
-                int64_t M_pad, int int4_as_int8, void* q, float* scale, float* group_sums, void* stream) {
+                int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream) {
   if (M < 0 || M_pad < M || M_pad > kMaxRows) return CQ_ERR_SHAPE;
   if (K < 256 || K % 256 != 0 || K > kMaxK) return CQ_ERR_SHAPE;
   if (!valid_rot(rot_group)) return CQ_ERR_ARG;
   if (mode != CQ_ACT_INT8_ROW && mode != CQ_ACT_INT4_ROW && mode != CQ_ACT_INT4_GROUP) return CQ_ERR_ARG;
   if (mode == CQ_ACT_INT4_GROUP && act_group != 64 && act_group != 128) return CQ_ERR_ARG;
+  if (flags & ~(CQ_Q_INT8_CODES | CQ_Q_KPERM)) return CQ_ERR_ARG;
+  const int int8_codes = (mode == CQ_ACT_INT8_ROW) || (flags & CQ_Q_INT8_CODES);
+  if ((flags & CQ_Q_KPERM) && !int8_codes) return CQ_ERR_ARG;
   if (M_pad == 0) return CQ_OK;
   if ((M > 0 && x == nullptr) || q == nullptr || scale == nullptr) return CQ_ERR_ARG;
-  if (!aligned(x, 16) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(group_sums, 4)) return CQ_ERR_ALIGN;
+  if (!aligned(x, 16) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(group_sums, 16)) return CQ_ERR_ALIGN;
   if (int dv = check_device()) return dv;
-  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), act_group, int4_as_int8, q, scale, nullptr, group_sums};
+  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), act_group, (flags & CQ_Q_INT8_CODES) ? 1 : 0,
+                     (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
+                     static_cast<__nv_bfloat16*>(group_sums), cq::rsplit_cols(static_cast<int>(K))};
   return cuda_status(cq::launch_act_rotquant(rot_group, swiglu != 0, mode, a, static_cast<cudaStream_t>(stream)));
 }
 
@@ -99,7 +117,7 @@ int cq_weight_rotquant(const void* w, int w_is_bf16, int64_t N, int64_t K, int r
     return CQ_ERR_ARG;
   if (!aligned(w, 16) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(zeros, 2)) return CQ_ERR_ALIGN;
   if (int dv = check_device()) return dv;
-  cq::RotQuantArgs a{w, N, N, static_cast<int>(K), grouped ? group : 0, 0, q, scale, zeros, nullptr};
+  cq::RotQuantArgs a{w, N, N, static_cast<int>(K), grouped ? group : 0, 0, 0, q, scale, zeros, nullptr, 0};
   return cuda_status(cq::launch_weight_rotquant(rot_group, w_is_bf16 != 0, kmode, a, static_cast<cudaStream_t>(stream)));
 }
 
@@ -121,28 +139,30 @@ static int check_gemm(const void* a, const void* b, const void* out, int64_t M, 
   return CQ_OK;
 }
 
-int cq_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_format, const float* sb,
+int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
                    const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
   if (b_format != CQ_B_INT4_SIGNED && b_format != CQ_B_INT8) return CQ_ERR_ARG;
+  if (a_kperm != 0 && (a_kperm != 1 || b_format == CQ_B_INT8)) return CQ_ERR_ARG;
   if (int e = check_gemm(a, b, out, M, N, K)) return e;
   if (M == 0) return CQ_OK;
   if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
   if (int dv = check_device()) return dv;
-  return cq::launch_gemm_rowcol(a, sa, b, b_format, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
+  return cq::launch_gemm_rowcol(a, a_kperm, sa, b, b_format, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
                                 static_cast<int>(K), static_cast<cudaStream_t>(stream));
 }
 
-int cq_gemm_affine(const int8_t* a, const float* sa, const float* gsum, int64_t gsum_ld, const void* b_packed,
-                   const void* s_bf16, const void* z_bf16, const void* bias, void* out, int64_t M, int64_t N,
+int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                   const void* s_bf16, const void* zt_bf16, const void* bias, void* out, int64_t M, int64_t N,
                    int64_t K, int group, void* stream) {
   if (group != 128) return CQ_ERR_ARG;
+  if (a_kperm != 0 && a_kperm != 1) return CQ_ERR_ARG;
   if (int e = check_gemm(a, b_packed, out, M, N, K)) return e;
   if (M == 0) return CQ_OK;
-  if (sa == nullptr || gsum == nullptr || s_bf16 == nullptr || z_bf16 == nullptr) return CQ_ERR_ARG;
-  if (gsum_ld < round_up(M, 4) || gsum_ld % 4 != 0) return CQ_ERR_SHAPE;
-  if (!aligned(gsum, 16)) return CQ_ERR_ALIGN;
+  if (K > kMaxK) return CQ_ERR_SHAPE;
+  if (sa == nullptr || gsplit == nullptr || s_bf16 == nullptr || zt_bf16 == nullptr) return CQ_ERR_ARG;
+  if (!aligned(gsplit, 16) || !aligned(zt_bf16, 16)) return CQ_ERR_ALIGN;
   if (int dv = check_device()) return dv;
-  return cq::launch_gemm_affine(a, sa, gsum, gsum_ld, b_packed, s_bf16, z_bf16, bias, out, static_cast<int>(M),
+  return cq::launch_gemm_affine(a, a_kperm, sa, gsplit, b_packed, s_bf16, zt_bf16, bias, out, static_cast<int>(M),
                                 static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
 }
 
@@ -154,13 +174,13 @@ static int64_t ws_mpad(int64_t M) { return round_up(M > 0 ? M : 1, 16); }
 int64_t cq_linear_workspace_bytes(int64_t M, int64_t K) {
   if (M < 0 || K <= 0) return -1;
   const int64_t mp = ws_mpad(M);
-  return round_up(mp * K, 256) + round_up(mp * 4, 256) + round_up((K / 128 + 1) * mp * 4, 256);
+  return round_up(mp * K, 256) + round_up(mp * 4, 256) + round_up(mp * cq_group_sum_cols(K) * 2, 256);
 }
 
 struct Workspace {
   int8_t* xq;
   float* sx;
-  float* gsum;
+  __nv_bfloat16* gsplit;
   int64_t mpad;
 };
 
@@ -174,7 +194,7 @@ static int carve(void* ws, int64_t ws_bytes, int64_t M, int64_t K, Workspace* w)
   p += round_up(w->mpad * K, 256);
   w->sx = reinterpret_cast<float*>(p);
   p += round_up(w->mpad * 4, 256);
-  w->gsum = reinterpret_cast<float*>(p);
+  w->gsplit = reinterpret_cast<__nv_bfloat16*>(p);
   return CQ_OK;
 }
 
@@ -186,19 +206,22 @@ int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int r
   Workspace w;
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
   const int mode = act_bits == 4 ? CQ_ACT_INT4_ROW : CQ_ACT_INT8_ROW;
-  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, mode, 0, w.mpad, 1, w.xq, w.sx, nullptr, stream)) return e;
-  return cq_gemm_rowcol(w.xq, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream);
+  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, mode, 0, w.mpad, CQ_Q_INT8_CODES | CQ_Q_KPERM, w.xq, w.sx,
+                          nullptr, stream))
+    return e;
+  return cq_gemm_rowcol(w.xq, 1, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream);
 }
 
 int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
-                          const void* qweight, const void* s_bf16, const void* z_bf16, int group, const void* bias,
+                          const void* qweight, const void* s_bf16, const void* zt_bf16, int group, const void* bias,
                           void* out, void* workspace, int64_t workspace_bytes, void* stream) {
   if (M == 0) return CQ_OK;
   Workspace w;
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
-  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, 0, w.xq, w.sx, w.gsum, stream))
+  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
+                          stream))
     return e;
-  return cq_gemm_affine(w.xq, w.sx, w.gsum, w.mpad, qweight, s_bf16, z_bf16, bias, out, M, N, K, group, stream);
+  return cq_gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, out, M, N, K, group, stream);
 }
 
 int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,
@@ -209,7 +232,7 @@ int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
   if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, 0, w.xq, w.sx, nullptr, stream))
     return e;
-  return cq_gemm_rowcol(w.xq, w.sx, weight, CQ_B_INT8, wscale, bias, out, M, N, K, stream);
+  return cq_gemm_rowcol(w.xq, 0, w.sx, weight, CQ_B_INT8, wscale, bias, out, M, N, K, stream);
 }
 
 }  // extern "C"

@@ -54,13 +54,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// Test for the completion of the phase with parity `parity`; a waiting thread is suspended in hardware (up to
+// about 0.5 ms per call) instead of spinning, so waiting warps leave the issue slots to the working ones.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(500000u) : "memory");
   return ok != 0;
 }
 
@@ -71,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
+    if ((++spins & 3u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         record_status(CQ_ERR_TIMEOUT, where);
@@ -134,7 +136,28 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// D(tmem) (+)= A(smem desc) * B(smem desc), bf16 x bf16 -> fp32.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld that also names the 32 destination registers of the load it waits for, so the compiler
+// cannot schedule a read of them ahead of the wait (tcgen05.ld writes its registers asynchronously).
+__device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets row (lane_base + i), columns c..c+31.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -148,6 +171,21 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+
+// 32 lanes x 8 consecutive 32-bit columns, every element set to `v` (thread i writes row lane_base + i).
+// The instruction reads its 8 values from 8 consecutive registers, so the narrow shape keeps the register
+// cost of a fill small.
+__device__ __forceinline__ void tmem_st_32x32b_x8_fill(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};"
+               ::"r"(taddr), "r"(v) : "memory");
+}
+// fill `ncols` (a multiple of 8) columns starting at taddr
+template <int NCOLS>
+__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v) {
+#pragma unroll
+  for (int c = 0; c < NCOLS; c += 8) tmem_st_32x32b_x8_fill(taddr + c, v);
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte swizzle layout: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), version 1 (sm_100), base offset 0 (tiles are 1024-byte aligned).
@@ -170,6 +208,15 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
+// Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4)                                  // D format: f32
+         | (1u << 7)                                // A: bf16
+         | (1u << 10)                               // B: bf16
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
 // ---------------------------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------------------------
@@ -177,6 +224,23 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
+}
+
+// Ordered global accesses (asm volatile keeps them in program order, so the compiler cannot hoist a long run
+// of loads ahead of the stores that consume them and blow up register pressure).
+__device__ __forceinline__ float4 ld_nc_f4_ordered(const float* p) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ld_nc_f32_ordered(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_bf16_ordered(__nv_bfloat16* p, float v) {
+  const unsigned short b = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(b) : "memory");
 }
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }

@@ -5,17 +5,26 @@
 // thread therefore owns one weight row n: the per-group weight scale s[g, n] and zero z[g, n] are per-thread
 // scalars, and only the per-token terms (activation scale, code sums) are broadcast loads.
 //
-// Per CTA (persistent, one per SM, 384 threads):
+// Per CTA (persistent, one per SM, 512 threads):
 //   warp 0      TMA producer: activation tile [256 tokens x 128 B] (128-byte swizzle) and the packed weight
-//               tile [128 rows x 64 B] per 128-wide K block, into a 3-stage shared-memory ring;
+//               tile [128 rows x 64 B] per 128-wide K block, into a 4-stage ring;
+//   warps 2-7   converters: unpack int4 -> int8 from the TMA ring into a 3-stage ring laid out as the tensor
+//               core's K-major 128-byte-swizzled operand (nibble v becomes the byte 16*v, the 1/16 is folded
+//               into the weight scale; with K-permuted activations each 32-bit word unpacks with one shift and
+//               two masks, no byte shuffles), 16 packed bytes per item, then fence.proxy.async and arrive;
 //   warp 1      MMA issuer: 4 x tcgen05.mma (128 x 256 x 32) per K block into a double-buffered TMEM
-//               accumulator (2 x 256 columns); tcgen05.commit releases the stage and hands buffers over;
-//   warps 2-3   converters: unpack int4 -> int8 in shared memory into the tensor core's K-major 128-byte
-//               swizzled layout (nibble v becomes the byte 16*v: one shift/mask per word, the 1/16 is folded
-//               into the weight scale), then fence.proxy.async and arrive;
-//   warps 4-11  epilogue: tcgen05.ld the int32 partial sums.  Affine weights (per 128-group scale/zero) drain
-//               every group into fp32 registers: acc += s[g,n] * P_g + z[g,n] * R[g,m]; row/col weights drain
-//               once per tile.  Output bf16 [M, N] row-major.
+//               accumulator (2 x 256 columns); tcgen05.commit releases both rings and hands buffers over;
+//   warps 8-15  epilogue: tcgen05.ld the int32 partial sums.  Affine weights (per 128-group scale/zero) drain
+//               every group into fp32 registers with packed f32x2 ops, acc += s[g,n] * P_g, starting from the
+//               zero-point term sum_g z[g,n] * R[g,m] that the tensor core computes first (kind::f16: the bf16
+//               zeros, built by the converters, times the tokens' code sums split exactly into bf16 hi/lo parts);
+//               row/col weights drain once per tile.  Output bf16 [M, N] row-major.
+//               Affine accumulators are seeded with the integer 0x4B400000 (the bits of 1.5 * 2^23) before each
+//               group, so the int32 sum P lands in TMEM as the float 1.5 * 2^23 + P (exact, |P| < 2^22) and the
+//               drain needs no int->float conversion: x = f - 1.5 * 2^23 (exact), acc = fma(s, x, acc).  The
+//               epilogue re-seeds a buffer as it releases it; a buffer goes to the MMA only after the epilogue
+//               arrives on its tmem_empty barrier (seeded and empty).
+// int8 weights (W8A8) skip the converters: TMA loads them straight into the operand layout.
 // Every mbarrier wait is bounded (see cq_common.cuh).  No cluster launch, no multicast.
 #include <cstdio>
 #include <cstring>
@@ -27,29 +36,42 @@ namespace cq {
 constexpr int kBW = 128;       // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kBT = 256;       // tokens per tile (MMA N, TMEM columns per accumulator buffer)
 constexpr int kBK = 128;       // K elements (bytes of int8) per stage
-constexpr int kStages = 3;
-constexpr int kThreads = 384;
+constexpr int kTmaStages = 4;
+constexpr int kConvStages = 3;
+constexpr int kThreads = 512;
+constexpr int kConvWarps = 6;          // warps 2..7
+constexpr int kConvThreads = 32 * kConvWarps;
+constexpr int kEpiWarp0 = 8;           // warps 8..15
+constexpr uint32_t kMagicBits = 0x4B400000u;   // 1.5 * 2^23 as float bits
+constexpr float kMagic = 12582912.0f;
 constexpr int kXBytes = kBT * kBK;          // 32 KB
-constexpr int kWuBytes = kBW * kBK;         // 16 KB
-constexpr int kWpBytes = kBW * kBK / 2;     //  8 KB
-constexpr int kSmemData = kStages * (kXBytes + kWuBytes + kWpBytes);
-constexpr int kSmemBytes = kSmemData + 1024 /*align slack*/ + 256 /*barriers*/;
-constexpr int kProducerRegs = 80;
-constexpr int kEpilogueRegs = 208;
+constexpr int kWuBytes = kBW * kBK;         // 16 KB (unpacked int4, or TMA-loaded int8 weights)
+constexpr int kWpBytes = kBW * kBK / 2;     //  8 KB (packed int4)
+constexpr int kProducerRegs = 40;    // warps 0-7 (producer, MMA, converters)
+constexpr int kEpilogueRegs = 216;   // warps 8-15; 256*40 + 256*216 = 128*512, the launch allocation
 
 enum : int { EPI_ROWCOL = 0, EPI_AFFINE = 1 };
 enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 
+// shared-memory plan per weight format
+template <int BFMT>
+struct SmemPlan {
+  static constexpr int kWStageBytes = (BFMT == BF_S8) ? kWuBytes : kWpBytes;   // weight bytes in the TMA ring
+  static constexpr int kTmaStageBytes = kXBytes + kWStageBytes;
+  static constexpr int kConvBytes = (BFMT == BF_S8) ? 0 : kConvStages * kWuBytes;
+  static constexpr int kData = kTmaStages * kTmaStageBytes + kConvBytes;
+  static constexpr int kBytes = kData + 1024 /*align slack*/ + 256 /*barriers*/;
+};
+
 struct GemmArgs {
   const float* sa;       // [M] activation scale
-  const float* gsum;     // [K/128, gsum_ld] code sums (affine)
-  int64_t gsum_ld;
   const float* sb;       // [N] weight scale (rowcol)
   const __nv_bfloat16* ws;  // [K/128, N] bf16 (affine)
-  const __nv_bfloat16* wz;  // [K/128, N] bf16 (affine)
+  const __nv_bfloat16* zt;  // [N, 64*nz] bf16 (affine): Zt[n, j] = z[j mod G, n] for j < 2G, else 0
   const __nv_bfloat16* bias;  // [N] or null
   __nv_bfloat16* out;    // [M, N]
   int M, N, K;
+  int nz;                // affine: zero-point pseudo blocks per tile (64 bf16 columns of the split sums each)
 };
 
 __device__ __forceinline__ void setmaxnreg_dec() {
@@ -59,31 +81,63 @@ __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kEpilogueRegs));
 }
 
+// d = a * b + c on two fp32 lanes at once (sm_100 packed FMA)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// d = a + b on two fp32 lanes at once
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // 8 packed bytes (16 nibbles, low nibble = even column) -> 16 bytes holding 16*v per column.
-template <int BFMT>
+//   KPERM: the activations' K order inside each 8-column block is 0,2,4,6,1,3,5,7, so the low nibbles of a
+//          word (even columns) and its high nibbles (odd columns) are already in place.
+//   else:  natural K order, interleaved with byte permutes.
+template <int BFMT, bool KPERM>
 __device__ __forceinline__ uint4 unpack16(uint2 p) {
   const uint32_t flip = (BFMT == BF_U4) ? 0x80808080u : 0u;   // uint4 q -> signed (q - 8): flip the top bit
   const uint32_t lo0 = ((p.x << 4) & 0xF0F0F0F0u) ^ flip, hi0 = (p.x & 0xF0F0F0F0u) ^ flip;
   const uint32_t lo1 = ((p.y << 4) & 0xF0F0F0F0u) ^ flip, hi1 = (p.y & 0xF0F0F0F0u) ^ flip;
+  if (KPERM) return make_uint4(lo0, hi0, lo1, hi1);
   return make_uint4(prmt(lo0, hi0, 0x5140u), prmt(lo0, hi0, 0x7362u), prmt(lo1, hi1, 0x5140u),
                     prmt(lo1, hi1, 0x7362u));
 }
 
-template <int EPI, int BFMT>
+template <int EPI, int BFMT, bool KPERM>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, const GemmArgs args) {
+gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+            const __grid_constant__ CUtensorMap tm_r, const GemmArgs args) {
+  using P = SmemPlan<BFMT>;
+  constexpr bool kConv = BFMT != BF_S8;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sm_x = smem;                                   // [kStages][kXBytes]
-  uint8_t* sm_wu = smem + kStages * kXBytes;              // [kStages][kWuBytes]
-  uint8_t* sm_wp = sm_wu + kStages * kWuBytes;            // [kStages][kWpBytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemData);
+  // TMA ring: [stage][X 32 KB | W 8/16 KB]; converter ring after it
+  uint8_t* sm_tma = smem;
+  uint8_t* sm_conv = smem + kTmaStages * P::kTmaStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::kData);
   uint64_t* full_tma = bars;
-  uint64_t* full_conv = bars + kStages;
-  uint64_t* empty = bars + 2 * kStages;
-  uint64_t* tmem_full = bars + 3 * kStages;
-  uint64_t* tmem_empty = bars + 3 * kStages + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 4);
+  uint64_t* empty_tma = bars + kTmaStages;
+  uint64_t* full_conv = bars + 2 * kTmaStages;
+  uint64_t* empty_conv = full_conv + kConvStages;
+  uint64_t* tmem_full = empty_conv + kConvStages;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -95,10 +149,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   const int num_tiles = m_tiles * n_tiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kTmaStages; ++s) {
       mbar_init(&full_tma[s], 1);
-      mbar_init(&full_conv[s], 2);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty_tma[s], 1);
+    }
+    for (int s = 0; s < kConvStages; ++s) {
+      mbar_init(&full_conv[s], kConvWarps);
+      mbar_init(&empty_conv[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
@@ -108,6 +165,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     fence_barrier_init();
     prefetch_tensormap(&tm_x);
     prefetch_tensormap(&tm_w);
+    if (EPI == EPI_AFFINE) prefetch_tensormap(&tm_r);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -118,94 +176,161 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  if (warp < 4) {
+  if (warp < kEpiWarp0) {
     setmaxnreg_dec();
     if (warp == 0 && lane == 0) {
       // ------------------------------ TMA producer ------------------------------
       int stage = 0;
       uint32_t phase = 0;
-      const uint32_t bytes = kXBytes + (BFMT == BF_S8 ? kWuBytes : kWpBytes);
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         const int m0 = (tile % m_tiles) * kBT;
         const int n0 = (tile / m_tiles) * kBW;
+        if (EPI == EPI_AFFINE) {
+          // zero-point operand: the tokens' split group sums (bf16, 64 columns per block) into the X slot
+          for (int p = 0; p < args.nz; ++p) {
+            if (!mbar_wait(&empty_tma[stage], phase ^ 1u, abort_flag, 10)) break;
+            uint8_t* st = sm_tma + stage * P::kTmaStageBytes;
+            mbar_arrive_expect_tx(&full_tma[stage], kXBytes);
+            tma_load_2d(st, &tm_r, &full_tma[stage], p * 128, m0);
+            if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
+          }
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) break;
-          mbar_arrive_expect_tx(&full_tma[stage], bytes);
-          tma_load_2d(sm_x + stage * kXBytes, &tm_x, &full_tma[stage], kb * kBK, m0);
-          if (BFMT == BF_S8) tma_load_2d(sm_wu + stage * kWuBytes, &tm_w, &full_tma[stage], kb * kBK, n0);
-          else tma_load_2d(sm_wp + stage * kWpBytes, &tm_w, &full_tma[stage], kb * (kBK / 2), n0);
-          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          if (!mbar_wait(&empty_tma[stage], phase ^ 1u, abort_flag, 1)) break;
+          uint8_t* st = sm_tma + stage * P::kTmaStageBytes;
+          mbar_arrive_expect_tx(&full_tma[stage], P::kTmaStageBytes);
+          tma_load_2d(st, &tm_x, &full_tma[stage], kb * kBK, m0);
+          if (BFMT == BF_S8) tma_load_2d(st + kXBytes, &tm_w, &full_tma[stage], kb * kBK, n0);
+          else tma_load_2d(st + kXBytes, &tm_w, &full_tma[stage], kb * (kBK / 2), n0);
+          if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
         }
       }
     } else if (warp == 1 && lane == 0) {
       // ------------------------------ MMA issuer ------------------------------
       constexpr uint32_t idesc = idesc_i8(kBW, kBT);
-      int stage = 0;
-      uint32_t phase = 0;
+      int stage = 0, cstage = 0;
+      uint32_t phase = 0, cphase = 0;
       int buf = 0;
       uint32_t buf_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         if (EPI == EPI_ROWCOL) {
-          if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase ^ 1u, abort_flag, 2))) break;
+          if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 2))) break;
           tc_fence_after();
+        }
+        if (EPI == EPI_AFFINE) {
+          // D = sum_j Zt[n, j] * Rsplit[m, j] in fp32: the zero-point term, the accumulator's starting value
+          if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 11))) break;
+          tc_fence_after();
+          constexpr uint32_t idesc_z = idesc_bf16(kBW, kBT);
+          for (int p = 0; p < args.nz && ok; ++p) {
+            if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 12))) break;
+            if (!(ok = mbar_wait(&full_conv[cstage], cphase, abort_flag, 13))) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
+            const uint32_t a_base = smem_u32(sm_conv + cstage * kWuBytes);
+            const uint32_t b_base = smem_u32(sm_tma + stage * P::kTmaStageBytes);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)   // 64 bf16 = 4 x K16
+              mma_bf16(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc_z,
+                       (p > 0 || k > 0) ? 1u : 0u);
+            tc_commit(&empty_tma[stage]);
+            tc_commit(&empty_conv[cstage]);
+            if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
+            if (++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
+          }
+          if (!ok) break;
+          tc_commit(&tmem_full[buf]);
+          if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
         for (int kb = 0; kb < kblocks && ok; ++kb) {
           if (EPI == EPI_AFFINE) {
-            if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase ^ 1u, abort_flag, 3))) break;
+            if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 3))) break;
             tc_fence_after();
           }
           if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 4))) break;
-          if (BFMT != BF_S8 && !(ok = mbar_wait(&full_conv[stage], phase, abort_flag, 5))) break;
+          if (kConv && !(ok = mbar_wait(&full_conv[cstage], cphase, abort_flag, 5))) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
-          const uint32_t a_base = smem_u32(sm_wu + stage * kWuBytes);
-          const uint32_t b_base = smem_u32(sm_x + stage * kXBytes);
+          uint8_t* st = sm_tma + stage * P::kTmaStageBytes;
+          const uint32_t a_base = smem_u32(kConv ? sm_conv + cstage * kWuBytes : st + kXBytes);
+          const uint32_t b_base = smem_u32(st);
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
-            const uint32_t acc = (EPI == EPI_AFFINE) ? (k > 0) : (kb > 0 || k > 0);
+            // affine: every group adds onto the buffer the epilogue seeded with kMagicBits
+            const uint32_t acc = (EPI == EPI_AFFINE) ? 1u : (kb > 0 || k > 0);
             mma_i8(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc, acc);
           }
-          tc_commit(&empty[stage]);
+          tc_commit(&empty_tma[stage]);
+          if (kConv) tc_commit(&empty_conv[cstage]);
           if (EPI == EPI_AFFINE) {
             tc_commit(&tmem_full[buf]);
             if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
           }
-          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
+          if (kConv && ++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
         }
         if (EPI == EPI_ROWCOL && ok) {
           tc_commit(&tmem_full[buf]);
           if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
       }
-    } else if (warp >= 2 && BFMT != BF_S8) {
+    } else if (warp >= 2 && kConv) {
       // ------------------------------ int4 -> int8 converters ------------------------------
-      const int ct = threadIdx.x - 64;   // 0..63
-      int stage = 0;
-      uint32_t phase = 0;
+      const int ct = threadIdx.x - 64;   // 0..kConvThreads-1
+      int stage = 0, cstage = 0;
+      uint32_t phase = 0, cphase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (EPI == EPI_AFFINE) {
+          // zero-point weight operand: rows n0..n0+127 of the prepared Zt, 64 bf16 columns per pseudo block
+          const int n0 = (tile / m_tiles) * kBW;
+          const int zt_ld = 64 * args.nz;
+          for (int p = 0; p < args.nz; ++p) {
+            if (!(ok = mbar_wait(&empty_conv[cstage], cphase ^ 1u, abort_flag, 14))) break;
+            uint8_t* dst = sm_conv + cstage * kWuBytes;
+            for (int it = ct; it < kBW * 8; it += kConvThreads) {
+              const int r = it & (kBW - 1), c = it >> 7;
+              const int n = n0 + r;
+              const uint4 v = (n < N) ? *reinterpret_cast<const uint4*>(args.zt + static_cast<int64_t>(n) * zt_ld + 64 * p + 8 * c)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+              *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_conv[cstage]);
+            // the matching TMA stage carries the activation-side operand; the converters only track its index
+            if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
+            if (++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
+          }
+          if (!ok) break;
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 6))) break;
-          const uint8_t* src = sm_wp + stage * kWpBytes;
-          uint8_t* dst = sm_wu + stage * kWuBytes;
-#pragma unroll 4
-          for (int it = ct; it < kBW * 8; it += 64) {
-            const int r = it >> 3, c = it & 7;
-            const uint2 p = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
-            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = unpack16<BFMT>(p);
+          if (!(ok = mbar_wait(&empty_conv[cstage], cphase ^ 1u, abort_flag, 9))) break;
+          const uint8_t* src = sm_tma + stage * P::kTmaStageBytes + kXBytes;
+          uint8_t* dst = sm_conv + cstage * kWuBytes;
+          // item = (row r, 16 packed bytes c4): 32 K columns -> output chunks 2*c4 and 2*c4 + 1 of the row
+#pragma unroll 3
+          for (int it = ct; it < kBW * 4; it += kConvThreads) {
+            const int r = it >> 2, c4 = it & 3;
+            const uint4 p = *reinterpret_cast<const uint4*>(src + r * 64 + c4 * 16);
+            uint8_t* drow = dst + r * 128;
+            *reinterpret_cast<uint4*>(drow + (((2 * c4) ^ (r & 7)) << 4)) = unpack16<BFMT, KPERM>(make_uint2(p.x, p.y));
+            *reinterpret_cast<uint4*>(drow + (((2 * c4 + 1) ^ (r & 7)) << 4)) = unpack16<BFMT, KPERM>(make_uint2(p.z, p.w));
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&full_conv[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          if (lane == 0) mbar_arrive(&full_conv[cstage]);
+          if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
+          if (++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
         }
       }
     }
   } else {
-    // ------------------------------ epilogue (warps 4..11) ------------------------------
+    // ------------------------------ epilogue (warps 8..15) ------------------------------
     setmaxnreg_inc();
-    const int e = warp - 4;
+    const int e = warp - kEpiWarp0;
     const int quad = warp & 3;            // TMEM lane quadrant this warp may access
     const int half = e >> 2;              // token half of the tile: columns [128*half, 128*half + 128)
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
@@ -214,52 +339,110 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
+    // hand both accumulator buffers to the MMA issuer (seeded for the affine epilogue)
+    for (int b = 0; b < 2; ++b) {
+      if (EPI == EPI_AFFINE) {
+        const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(b * kBT + half * 128);
+        tmem_fill<128>(taddr, kMagicBits);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[b]);
+    }
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const int m0 = (tile % m_tiles) * kBT + half * 128;
       const int n = (tile / m_tiles) * kBW + quad * 32 + lane;
       const bool n_ok = n < N;
+      const bool m_full = m0 + 128 <= M;     // every token of this half-tile exists: no per-element checks
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
       if (EPI == EPI_AFFINE) {
-        float acc[128];
-#pragma unroll
-        for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
-        for (int g = 0; g < kblocks; ++g) {
-          if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 7))) break;
+        float2 acc[64];
+        {
+          // starting value: the zero-point term sum_g z[g, n] * R[g, m], accumulated in fp32 by the tensor core
+          if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 15))) break;
           tc_fence_after();
-          const float s = n_ok ? __bfloat162float(args.ws[static_cast<int64_t>(g) * N + n]) * wscale_fold : 0.0f;
-          const float z = n_ok ? __bfloat162float(args.wz[static_cast<int64_t>(g) * N + n]) : 0.0f;
           const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(taddr + 32 * ch, r);
-            tmem_wait_ld();
+            tmem_wait_ld_dep(r);
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              acc[32 * ch + j] = __fmaf_rn(s, __int2float_rn(static_cast<int>(r[j])), acc[32 * ch + j]);
+            for (int j = 0; j < 16; ++j) acc[16 * ch + j] = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
           }
+          tmem_fill<128>(taddr, kMagicBits);
+          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[buf]);
           if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
-          // zero-point term: z[g, n] * (sum of token m's codes over group g)
-          const float* gs = args.gsum + static_cast<int64_t>(g) * args.gsum_ld + m0;
+        }
+        // the weight scale of the next group is loaded one group ahead (its latency hides behind a drain)
+        float s_next = n_ok ? __bfloat162float(args.ws[n]) * wscale_fold : 0.0f;
+        for (int g = 0; g < kblocks; ++g) {
+          const float s = s_next;
+          if (g + 1 < kblocks && n_ok) s_next = __bfloat162float(args.ws[static_cast<int64_t>(g + 1) * N + n]) * wscale_fold;
+          if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 7))) break;
+          tc_fence_after();
+          const float2 s2 = make_float2(s, s);
+          const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
+          const float2 neg_magic = make_float2(-kMagic, -kMagic);
+          // software-pipelined drain: chunk c+1 is in flight while chunk c is scaled; each chunk is re-seeded as
+          // soon as it is in registers and the buffer goes back to the MMA before the last chunk's math
+          uint32_t ra[32], rb[32];
+          auto scale_chunk = [&](const uint32_t (&r)[32], int ch) {
 #pragma unroll
-          for (int j4 = 0; j4 < 32; ++j4) {
-            const float4 rs = (m0 + 4 * j4 < M) ? *reinterpret_cast<const float4*>(gs + 4 * j4) : make_float4(0, 0, 0, 0);
-            acc[4 * j4 + 0] = __fmaf_rn(z, rs.x, acc[4 * j4 + 0]);
-            acc[4 * j4 + 1] = __fmaf_rn(z, rs.y, acc[4 * j4 + 1]);
-            acc[4 * j4 + 2] = __fmaf_rn(z, rs.z, acc[4 * j4 + 2]);
-            acc[4 * j4 + 3] = __fmaf_rn(z, rs.w, acc[4 * j4 + 3]);
-          }
+            for (int j = 0; j < 16; ++j) {
+              // the buffer held kMagicBits + P: as a float that is 1.5 * 2^23 + P, so this subtraction is exact
+              const float2 p = fadd2(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_magic);
+              acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
+            }
+          };
+          tmem_ld_32x32b_x32(taddr, ra);
+          tmem_wait_ld_dep(ra);
+          tmem_fill<32>(taddr, kMagicBits);
+          tmem_ld_32x32b_x32(taddr + 32, rb);
+          scale_chunk(ra, 0);
+          tmem_wait_ld_dep(rb);
+          tmem_fill<32>(taddr + 32, kMagicBits);
+          tmem_ld_32x32b_x32(taddr + 64, ra);
+          scale_chunk(rb, 1);
+          tmem_wait_ld_dep(ra);
+          tmem_fill<32>(taddr + 64, kMagicBits);
+          tmem_ld_32x32b_x32(taddr + 96, rb);
+          scale_chunk(ra, 2);
+          tmem_wait_ld_dep(rb);
+          tmem_fill<32>(taddr + 96, kMagicBits);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+          scale_chunk(rb, 3);
+          if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
         if (!ok) break;
+        if (n_ok) {
+          // column n of the output for tokens m0..m0+127: one pointer walked down the rows
+          __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
+          const float* sa = args.sa + m0;
+          // scale index clamped to the last existing token (rows at or past M are not stored)
+          const int mlast = M - 1 - m0;
+          auto sa_at = [&](int i) { return ld_nc_f32_ordered(sa + (m_full ? i : min(i, mlast))); };
+          float sv[4] = {sa_at(0), sa_at(1), sa_at(2), sa_at(3)};
 #pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const int m = m0 + j;
-          if (m < M && n_ok) {
-            const float y = __fmaf_rn(acc[j], args.sa[m], bias);
-            args.out[static_cast<int64_t>(m) * N + n] = __float2bfloat16_rn(y);
+          for (int j4 = 0; j4 < 32; ++j4) {
+            const float c0 = sv[0], c1 = sv[1], c2 = sv[2], c3 = sv[3];
+            if (j4 + 1 < 32) {
+#pragma unroll
+              for (int t = 0; t < 4; ++t) sv[t] = sa_at(4 * (j4 + 1) + t);
+            }
+            const int m = m0 + 4 * j4;
+            if (m_full || m < M) st_bf16_ordered(orow, __fmaf_rn(acc[2 * j4].x, c0, bias));
+            if (m_full || m + 1 < M) st_bf16_ordered(orow + N, __fmaf_rn(acc[2 * j4].y, c1, bias));
+            if (m_full || m + 2 < M) st_bf16_ordered(orow + 2 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].x, c2, bias));
+            if (m_full || m + 3 < M) st_bf16_ordered(orow + 3 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].y, c3, bias));
+            orow += 4 * static_cast<int64_t>(N);
           }
         }
       } else {
@@ -267,17 +450,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         tc_fence_after();
         const float sb = n_ok ? args.sb[n] * wscale_fold : 0.0f;
         const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
+        __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
+        const float* sa = args.sa + m0;
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + 32 * ch, r);
-          tmem_wait_ld();
+          tmem_wait_ld_dep(r);
+          if (n_ok) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m0 + 32 * ch + j;
-            if (m < M && n_ok) {
-              const float y = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sb), args.sa[m], bias);
-              args.out[static_cast<int64_t>(m) * N + n] = __float2bfloat16_rn(y);
+            for (int j = 0; j < 32; ++j) {
+              const int mm = 32 * ch + j;
+              if (m_full || m0 + mm < M)
+                orow[0] = __float2bfloat16_rn(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sb), sa[mm], bias));
+              orow += N;
             }
           }
         }
@@ -296,6 +482,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     __syncwarp();
     tmem_dealloc(tmem_base, 512);
   }
+}
+
+// Zt[n, j] = z[j mod G, n] for j < 2G, 0 for 2G <= j < cols (the affine GEMM's zero-point weight operand)
+__global__ void prep_zt_kernel(const __nv_bfloat16* __restrict__ z, __nv_bfloat16* __restrict__ zt, int N, int G,
+                               int cols) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(N) * cols) return;
+  const int n = static_cast<int>(i / cols), j = static_cast<int>(i % cols);
+  const int g = j < G ? j : (j < 2 * G ? j - G : -1);
+  zt[i] = g >= 0 ? z[static_cast<int64_t>(g) * N + n] : __float2bfloat16_rn(0.0f);
+}
+
+cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t st) {
+  const int cols = rsplit_cols(K);
+  const int64_t total = static_cast<int64_t>(N) * cols;
+  if (total == 0) return cudaSuccess;
+  prep_zt_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(z), static_cast<__nv_bfloat16*>(zt), N, K / kBK, cols);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -334,9 +539,10 @@ static bool make_map_u8(CUtensorMap* map, const void* base, int64_t rows, int64_
 
 static int g_num_sms = 0;
 
-template <int EPI, int BFMT>
-static int launch_gemm_t(const int8_t* a, const void* b, const GemmArgs& args, cudaStream_t st) {
-  auto kern = gemm_kernel<EPI, BFMT>;
+template <int EPI, int BFMT, bool KPERM>
+static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args, cudaStream_t st) {
+  auto kern = gemm_kernel<EPI, BFMT, KPERM>;
+  constexpr int smem_bytes = SmemPlan<BFMT>::kBytes;
   static bool configured = false;
   static bool regs_ok = false;
   if (!configured) {
@@ -344,8 +550,8 @@ static int launch_gemm_t(const int8_t* a, const void* b, const GemmArgs& args, c
     if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return CQ_ERR_CUDA;
     // setmaxnreg redistributes the registers the CTA was launched with: refuse to launch when the launch
     // allocation could not cover the producer/epilogue split (the .inc would otherwise wait forever)
-    regs_ok = fa.numRegs * kThreads >= 128 * kProducerRegs + 256 * kEpilogueRegs;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    regs_ok = fa.numRegs * kThreads >= 256 * kProducerRegs + 256 * kEpilogueRegs;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
       return CQ_ERR_CUDA;
     configured = true;
   }
@@ -356,8 +562,13 @@ static int launch_gemm_t(const int8_t* a, const void* b, const GemmArgs& args, c
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_num_sms <= 0) return CQ_ERR_CUDA;
   }
-  CUtensorMap tm_x, tm_w;
+  CUtensorMap tm_x, tm_w, tm_r;
   if (!make_map_u8(&tm_x, a, args.M, args.K, kBK, kBT, true)) return CQ_ERR_CUDA;
+  if (EPI == EPI_AFFINE) {
+    if (!make_map_u8(&tm_r, rsplit, args.M, 2 * rsplit_cols(args.K), 128, kBT, true)) return CQ_ERR_CUDA;
+  } else {
+    tm_r = tm_x;   // unused
+  }
   if (BFMT == BF_S8) {
     if (!make_map_u8(&tm_w, b, args.N, args.K, kBK, kBW, true)) return CQ_ERR_CUDA;
   } else {
@@ -366,11 +577,11 @@ static int launch_gemm_t(const int8_t* a, const void* b, const GemmArgs& args, c
   const int tiles = ((args.M + kBT - 1) / kBT) * ((args.N + kBW - 1) / kBW);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
   if (grid == 0) return CQ_OK;
-  kern<<<grid, kThreads, kSmemBytes, st>>>(tm_x, tm_w, args);
+  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, args);
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
 
-int launch_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_format, const float* sb,
+int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
                        const void* bias, void* out, int M, int N, int K, cudaStream_t st) {
   GemmArgs g{};
   g.sa = sa;
@@ -378,23 +589,24 @@ int launch_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_fo
   g.bias = static_cast<const __nv_bfloat16*>(bias);
   g.out = static_cast<__nv_bfloat16*>(out);
   g.M = M; g.N = N; g.K = K;
-  if (b_format == CQ_B_INT8) return launch_gemm_t<EPI_ROWCOL, BF_S8>(a, b, g, st);
-  return launch_gemm_t<EPI_ROWCOL, BF_S4>(a, b, g, st);
+  if (b_format == CQ_B_INT8) return launch_gemm_t<EPI_ROWCOL, BF_S8, false>(a, b, nullptr, g, st);
+  if (a_kperm) return launch_gemm_t<EPI_ROWCOL, BF_S4, true>(a, b, nullptr, g, st);
+  return launch_gemm_t<EPI_ROWCOL, BF_S4, false>(a, b, nullptr, g, st);
 }
 
-int launch_gemm_affine(const int8_t* a, const float* sa, const float* gsum, int64_t gsum_ld, const void* b,
-                       const void* s, const void* z, const void* bias, void* out, int M, int N, int K,
+int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
+                       const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st) {
   GemmArgs g{};
   g.sa = sa;
-  g.gsum = gsum;
-  g.gsum_ld = gsum_ld;
+  g.nz = rsplit_cols(K) / 64;
   g.ws = static_cast<const __nv_bfloat16*>(s);
-  g.wz = static_cast<const __nv_bfloat16*>(z);
+  g.zt = static_cast<const __nv_bfloat16*>(zt);
   g.bias = static_cast<const __nv_bfloat16*>(bias);
   g.out = static_cast<__nv_bfloat16*>(out);
   g.M = M; g.N = N; g.K = K;
-  return launch_gemm_t<EPI_AFFINE, BF_U4>(a, b, g, st);
+  if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st);
+  return launch_gemm_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st);
 }
 
 }  // namespace cq

@@ -11,19 +11,27 @@ struct RotQuantArgs {
   int K;
   int act_group;        // 64/128 for the per-group modes
   int int4_as_int8;     // int4 modes: write int8 codes [rows_pad, K] instead of packed nibbles
+  int kperm;            // int8 outputs: store each 8-column block in the order 0,2,4,6,1,3,5,7 (the K order
+                        // the int4-weight GEMMs unpack their nibbles into)
   void* q;
   void* scale;          // f32 [rows_pad] | f32 [K/G, rows_pad] | bf16 [K/G, rows_pad] (affine)
   void* zeros;          // bf16 [K/G, rows_pad] (affine)
-  float* gsum;          // f32 [K/128, rows_pad] or null
+  __nv_bfloat16* rsplit;  // bf16 [rows_pad, rs_cols] or null: per-token code sums over 128-wide K groups, split
+                          // exactly into hi = 128*floor(R/128) (columns [0, G)) and lo = R - hi (columns [G, 2G))
+  int rs_cols;            // 64 * ceil(G / 32), G = K / 128; columns [2G, rs_cols) are zero
 };
+
+// columns of the split group-sum array for a K (the affine GEMM's zero-point operand)
+__host__ __device__ constexpr int rsplit_cols(int K) { return 64 * ((K / 128 + 31) / 32); }
 
 cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_weight_rotquant(int rot, bool w_bf16, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_unpack_int4(const void* src, int64_t n_bytes, void* dst, cudaStream_t st);
-int launch_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_format, const float* sb,
+int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
                        const void* bias, void* out, int M, int N, int K, cudaStream_t st);
-int launch_gemm_affine(const int8_t* a, const float* sa, const float* gsum, int64_t gsum_ld, const void* b,
-                       const void* s, const void* z, const void* bias, void* out, int M, int N, int K,
+int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
+                       const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st);
+cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t st);
 
 }  // namespace cq

@@ -232,6 +232,11 @@ __global__ void __launch_bounds__(1024) rotquant_kernel(const RotQuantArgs args)
   }
 
   const int64_t ld = args.rows_pad;
+  if (args.rsplit != nullptr) {
+    const int G = K >> 7;
+    for (int j = 2 * G + threadIdx.x; j < args.rs_cols; j += blockDim.x)
+      args.rsplit[row * args.rs_cols + j] = __float2bfloat16_rn(0.0f);
+  }
   const bool pack4 = !(MODE == MODE_ACT_INT8_ROW || MODE == MODE_W_INT8_ROW) && !args.int4_as_int8;
 #pragma unroll
   for (int s = 0; s < PPW; ++s) {
@@ -294,17 +299,35 @@ __global__ void __launch_bounds__(1024) rotquant_kernel(const RotQuantArgs args)
       for (int i = 0; i < 16; ++i) c[i] = 0;
     }
     if (valid[s]) {
-      if (pack4) store_codes<true>(static_cast<uint8_t*>(args.q) + row * (static_cast<int64_t>(K) / 2), e, c);
-      else store_codes<false>(static_cast<int8_t*>(args.q) + row * static_cast<int64_t>(K), e, c);
+      if (pack4) {
+        store_codes<true>(static_cast<uint8_t*>(args.q) + row * (static_cast<int64_t>(K) / 2), e, c);
+      } else if (args.kperm) {
+        int cp[16];
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            cp[8 * b + j] = c[8 * b + 2 * j];
+            cp[8 * b + 4 + j] = c[8 * b + 2 * j + 1];
+          }
+        store_codes<false>(static_cast<int8_t*>(args.q) + row * static_cast<int64_t>(K), e, cp);
+      } else {
+        store_codes<false>(static_cast<int8_t*>(args.q) + row * static_cast<int64_t>(K), e, c);
+      }
     }
-    if (args.gsum != nullptr) {
+    if (args.rsplit != nullptr) {
       int sum = 0;
 #pragma unroll
       for (int i = 0; i < 16; ++i) sum += c[i];
       sum = group_sum<8>(sum);
-      if (valid[s] && (lane & 7) == 0) args.gsum[(e >> 7) * ld + row] = static_cast<float>(sum);
-    }
-  }
+      if (valid[s] && (lane & 7) == 0) {
+        const int g = e >> 7, G = K >> 7;
+        const int hi = (sum >= 0 ? sum : sum - 127) / 128 * 128;   // 128 * floor(sum / 128)
+        __nv_bfloat16* rrow = args.rsplit + row * args.rs_cols;
+        rrow[g] = __float2bfloat16_rn(static_cast<float>(hi));
+        rrow[G + g] = __float2bfloat16_rn(static_cast<float>(sum - hi));
+      }
+    }  }
 }
 
 template <typename IN_T, int ROT, bool SWIGLU, int MODE>

@@ -158,10 +158,22 @@ class B200AffineW4A8Layout(QuantizedLayout):
         return {"": qdata, "_scale": params.scale, "_zeros": params.zeros}
 
     @classmethod
+    def prepared_zeros(cls, params):
+        """The GEMM's zero-point operand for these params, built on first use and kept on the params object
+        (rebuilt if the zeros tensor is modified in place)."""
+        from .ops import prepare_affine_zeros
+        cached = params.__dict__.get("_zt")
+        if cached is None or cached[0] != params.zeros._version or cached[1].device != params.zeros.device:
+            cached = (params.zeros._version, prepare_affine_zeros(params.zeros, params.group_size))
+            object.__setattr__(params, "_zt", cached)   # frozen dataclass: a cache, not a field
+        return cached[1]
+
+    @classmethod
     def linear(cls, x, qdata, params, bias=None, input_act=None):
         from .ops import w4a8_affine_linear
         return w4a8_affine_linear(x, qdata, params.scale, params.zeros, bias, group_size=params.group_size,
-                                  convrot_groupsize=params.convrot_groupsize, input_act=input_act)
+                                  convrot_groupsize=params.convrot_groupsize, input_act=input_act,
+                                  zeros_prepared=cls.prepared_zeros(params))
 
 
 class B200TensorWiseINT8Layout(QuantizedLayout):

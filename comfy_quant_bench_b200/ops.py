@@ -71,8 +71,14 @@ def _bias_bf16(bias: torch.Tensor | None) -> torch.Tensor | None:
 # --------------------------------------------------------------------------------------------------
 
 def rotquant(x: torch.Tensor, rot_group: int, mode: int, *, swiglu: bool = False, act_group: int = 0,
-             m_pad: int | None = None, int4_as_int8: bool = False, group_sums: bool = False):
-    """Raw activation stage: returns (q, scale, gsum or None).  See cq_rotquant in include/cq_b200.h."""
+             m_pad: int | None = None, int4_as_int8: bool = False, group_sums: bool = False, kperm: bool = False):
+    """Raw activation stage: returns (q, scale, gsplit or None).  See cq_rotquant in include/cq_b200.h.
+
+    ``group_sums`` also returns the per-token code sums over 128-wide K groups, split into bf16 hi/lo parts
+    ([M_pad, cq_group_sum_cols(K)]; the zero-point operand of ``gemm_affine``).
+
+    ``kperm`` writes int8 codes with each 8-column block of K in the order 0,2,4,6,1,3,5,7 (the order the
+    int4-weight GEMMs unpack into; pass ``a_kperm=True`` to them)."""
     dev = _require_cuda(x)
     x2 = _as2d(x)
     m = x2.shape[0]
@@ -86,9 +92,10 @@ def rotquant(x: torch.Tensor, rot_group: int, mode: int, *, swiglu: bool = False
         scale = torch.empty(k // act_group, mp, dtype=torch.float32, device=dev)
     else:
         scale = torch.empty(mp, dtype=torch.float32, device=dev)
-    gs = torch.empty(k // 128, mp, dtype=torch.float32, device=dev) if group_sums else None
+    gs = torch.empty(mp, int(_lib.load().cq_group_sum_cols(k)), dtype=torch.bfloat16, device=dev) if group_sums else None
+    flags = (_lib.CQ_Q_INT8_CODES if int4_as_int8 else 0) | (_lib.CQ_Q_KPERM if kperm else 0)
     _lib.call("cq_rotquant", _ptr(x2), m, k, _check_rot(rot_group), int(bool(swiglu)), int(mode), int(act_group), mp,
-              int(bool(int4_as_int8)), _ptr(q), _ptr(scale), _ptr(gs), _stream(dev))
+              flags, _ptr(q), _ptr(scale), _ptr(gs), _stream(dev))
     return q, scale, gs
 
 
@@ -199,7 +206,7 @@ def quantize_int4_groupwise_weight(weight: torch.Tensor, group_size: int = 128, 
 # --------------------------------------------------------------------------------------------------
 
 def gemm_rowcol(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, bias=None, *,
-                b_int8: bool = False) -> torch.Tensor:
+                b_int8: bool = False, a_kperm: bool = False) -> torch.Tensor:
     """out = (a @ b^T) * sa[:, None] * sb[None, :] + bias -> bf16.  a int8 codes [M, K]; b packed int4 or int8."""
     dev = _require_cuda(a, sa, b, sb, bias)
     m, k = a.shape
@@ -208,7 +215,7 @@ def gemm_rowcol(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Te
         raise ValueError(f"Input K={k} does not match weight K={b.shape[1] * (1 if b_int8 else 2)}")
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     bias = _bias_bf16(bias)
-    _lib.call("cq_gemm_rowcol", _ptr(a), _ptr(sa.float().contiguous()), _ptr(b),
+    _lib.call("cq_gemm_rowcol", _ptr(a), int(bool(a_kperm)), _ptr(sa.float().contiguous()), _ptr(b),
               _lib.CQ_B_INT8 if b_int8 else _lib.CQ_B_INT4_SIGNED, _ptr(sb.float().contiguous()), _ptr(bias),
               _ptr(out), m, n, k, _stream(dev))
     return out
@@ -291,13 +298,27 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     return out if dt == torch.bfloat16 else out.to(dt)
 
 
+def prepare_affine_zeros(zeros: torch.Tensor, group_size: int = 128) -> torch.Tensor:
+    """The zero-point operand of the W4A8 GEMM, built once per weight from the awq-layout zeros [K/G, N]:
+    zt [N, cq_group_sum_cols(K)] bf16 with zt[n, j] = zeros[j mod G, n] for j < 2G, else 0."""
+    dev = _require_cuda(zeros)
+    g, n = zeros.shape
+    k = g * group_size
+    z = zeros.to(torch.bfloat16).contiguous()
+    zt = torch.empty(n, int(_lib.load().cq_group_sum_cols(k)), dtype=torch.bfloat16, device=dev)
+    _lib.call("cq_prepare_affine_zeros", _ptr(z), n, k, int(group_size), _ptr(zt), _stream(dev))
+    return zt
+
+
 def w4a8_affine_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, zeros: torch.Tensor,
                        bias: torch.Tensor | None = None, group_size: int = 128, convrot_groupsize: int = 0,
-                       input_act: str | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+                       input_act: str | None = None, out_dtype: torch.dtype | None = None,
+                       zeros_prepared: torch.Tensor | None = None) -> torch.Tensor:
     """W4A8 linear with awq-layout weights (W = (q - 8) * scale + zeros, scale/zeros [K/G, N] bf16).
 
     Activations are (optionally rotated and) quantized per token to int8; the GEMM accumulates int8 x int4
     products per 128-group in int32 and applies scale, zero-point, activation scale and bias in fp32.
+    ``zeros_prepared`` (from ``prepare_affine_zeros``) skips rebuilding the zero-point operand on every call.
     """
     if group_size != 128:
         raise ValueError("the W4A8 affine kernel supports group_size 128")
@@ -317,23 +338,25 @@ def w4a8_affine_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     ws = _workspace(m, k, dev)
     wp, wn = _ws_ptr(ws)
     bias = _bias_bf16(bias)
+    zt = zeros_prepared if zeros_prepared is not None else prepare_affine_zeros(zeros, group_size)
     _lib.call("cq_linear_w4a8_affine", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), int(swiglu),
-              _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()),
-              _ptr(zeros.to(torch.bfloat16).contiguous()), int(group_size), _ptr(bias), _ptr(out), wp, wn,
-              _stream(dev))
+              _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()), _ptr(zt), int(group_size),
+              _ptr(bias), _ptr(out), wp, wn, _stream(dev))
     out = out.reshape(*x.shape[:-1], n)
     dt = out_dtype or x.dtype
     return out if dt == torch.bfloat16 else out.to(dt)
 
 
-def gemm_affine(a: torch.Tensor, sa: torch.Tensor, gsum: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
-                zeros: torch.Tensor, bias=None) -> torch.Tensor:
-    """The affine GEMM alone on pre-quantized activations (a int8 [M, K], sa [M], gsum [K/128, M_pad])."""
-    dev = _require_cuda(a, sa, gsum, qweight, scale, zeros, bias)
+def gemm_affine(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
+                zeros: torch.Tensor, bias=None, *, a_kperm: bool = False,
+                zeros_prepared: torch.Tensor | None = None) -> torch.Tensor:
+    """The affine GEMM alone on pre-quantized activations (a int8 [M, K], sa [M], gsplit from ``rotquant``)."""
+    dev = _require_cuda(a, sa, gsplit, qweight, scale, zeros, bias)
+    zt = zeros_prepared if zeros_prepared is not None else prepare_affine_zeros(zeros, 128)
     m, k = a.shape
     n = qweight.shape[0]
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     bias = _bias_bf16(bias)
-    _lib.call("cq_gemm_affine", _ptr(a), _ptr(sa), _ptr(gsum), gsum.shape[1], _ptr(qweight),
-              _ptr(scale.contiguous()), _ptr(zeros.contiguous()), _ptr(bias), _ptr(out), m, n, k, 128, _stream(dev))
+    _lib.call("cq_gemm_affine", _ptr(a), int(bool(a_kperm)), _ptr(sa), _ptr(gsplit), _ptr(qweight),
+              _ptr(scale.contiguous()), _ptr(zt), _ptr(bias), _ptr(out), m, n, k, 128, _stream(dev))
     return out

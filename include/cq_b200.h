@@ -60,6 +60,11 @@ typedef enum {
   CQ_W_INT4_GROUP_BF16UP = 3  /* per-group symmetric int4, s = bf16_up(amax/7) f32 [K/G, N]                    */
 } cq_weight_mode;
 
+/* cq_rotquant output flags. */
+#define CQ_Q_INT8_CODES 1  /* int4 modes: write int8 codes [M_pad, K] instead of packed nibbles            */
+#define CQ_Q_KPERM 2       /* int8 code outputs: store each 8-column block of K in the order 0,2,4,6,1,3,5,7 -
+                              the order the int4-weight GEMMs unpack nibbles into (see cq_gemm_rowcol)    */
+
 /* Weight operand encodings accepted by the GEMMs. */
 typedef enum {
   CQ_B_INT4_SIGNED = 0,  /* packed signed int4 [N, K/2] (ConvRot W4A4)             */
@@ -88,15 +93,29 @@ CQ_API int cq_take_device_status(int* status, void* stream);
  *   mode       cq_act_mode
  *   act_group  64 or 128 for CQ_ACT_INT4_GROUP, else ignored
  *   M_pad      >= M; rows M..M_pad-1 of q (and of scale for CQ_ACT_INT4_GROUP) are written as 0
+ *   flags      CQ_Q_INT8_CODES | CQ_Q_KPERM (see above), 0 for the reference's layouts
  *   q          int8 [M_pad, K] for CQ_ACT_INT8_ROW; packed int4 [M_pad, K/2] for the int4 modes,
- *              or int8 codes [M_pad, K] when int4_as_int8 != 0 (what the fused linears feed the GEMM)
+ *              or int8 codes [M_pad, K] with CQ_Q_INT8_CODES (what the fused linears feed the GEMM)
  *   scale      f32 [M_pad] for the per-token modes, f32 [K/act_group, M_pad] for CQ_ACT_INT4_GROUP
- *   group_sums NULL, or f32 [K/128, M_pad]: sum of the codes of each token over each 128-wide K group
- *              (the affine zero-point term of cq_gemm_affine)
+ *   group_sums NULL, or bf16 [M_pad, cq_group_sum_cols(K)]: the sum R of each token's codes over each
+ *              128-wide K group g (G = K/128 groups), split exactly into hi = 128*floor(R/128) in column g
+ *              and lo = R - hi in column G + g, remaining columns 0 (the affine zero-point operand of
+ *              cq_gemm_affine)
  * Constraints: K % 512 == 0 or K % 256 == 0 (multiple of 256), K <= 32768; M >= 0.
  */
 CQ_API int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, int mode, int act_group,
-                int64_t M_pad, int int4_as_int8, void* q, float* scale, float* group_sums, void* stream);
+                       int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream);
+
+/* Columns of cq_rotquant's split group-sum array (and of the prepared zero-point operand of
+ * cq_prepare_affine_zeros) for a given K: 64 * ceil(K / 4096). */
+CQ_API int64_t cq_group_sum_cols(int64_t K);
+
+/*
+ * Prepare the zero-point operand of the affine W4A8 GEMM from the awq-layout zeros, once per weight:
+ *   zt[n, j] = z[j mod G, n] for j < 2G, 0 for 2G <= j < cq_group_sum_cols(K)   (G = K / group)
+ *   z   bf16 [K/group, N] (patches/comfyui_awq_w4a16_format.patch:79-80 layout);  zt bf16 [N, cq_group_sum_cols(K)]
+ */
+CQ_API int cq_prepare_affine_zeros(const void* z_bf16, int64_t N, int64_t K, int group, void* zt_bf16, void* stream);
 
 /*
  * Weight rotate-and-quantize (the converter kernel).
@@ -127,6 +146,8 @@ CQ_API int cq_unpack_int4(const void* src, int64_t R, int64_t C, void* dst, void
  * of g64_gemm6.gemm (experiments/qwen21-kernel/kernels/g64_gemm6.cu:383-411).
  *
  *   a      int8 codes [M, K] (int8, or int4 values held in int8)
+ *   a_kperm 1 when `a` was written with CQ_Q_KPERM (int4 weights only; the unpack then needs no byte
+ *          shuffles), 0 for natural K order
  *   sa     f32 [M]
  *   b      CQ_B_INT4_SIGNED: packed [N, K/2]; CQ_B_INT8: int8 [N, K]
  *   sb     f32 [N]
@@ -134,21 +155,26 @@ CQ_API int cq_unpack_int4(const void* src, int64_t R, int64_t C, void* dst, void
  *   out    bf16 [M, N]
  * Constraints: K % 128 == 0; N % 16 == 0; pointers 16-byte aligned.
  */
-CQ_API int cq_gemm_rowcol(const int8_t* a, const float* sa, const void* b, int b_format, const float* sb,
-                   const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream);
+CQ_API int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format,
+                          const float* sb, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
+                          void* stream);
 
 /*
  * W4A8 affine linear, the BASELINE north-star GEMM:
  *   out[m, n] = bf16( sa[m] * sum_g ( s[g,n] * sum_{k in g} a[m,k]*(q[n,k]-8) + z[g,n] * gsum[g,m] ) + bias[n] )
- * with q the awq_w4a16 uint4 codes (packed [N, K/2]) and s/z bf16 [K/group, N]
+ * with q the awq_w4a16 uint4 codes (packed [N, K/2]), s bf16 [K/group, N] and the zeros z passed as zt, the
+ * operand cq_prepare_affine_zeros builds from z bf16 [K/group, N]
  * (patches/comfyui_awq_w4a16_format.patch:79-80; the int8 x int4 policy family of
  * experiments/qwen21-kernel/kernels/g64_gemm6.cu:5-11, 93-343).
- *   a      int8 [M, K];  sa f32 [M];  gsum f32 [K/128, M_pad>=M] from cq_rotquant (sum of a over each group)
- *   group  128
+ *   a       int8 [M, K] (a_kperm as for cq_gemm_rowcol);  sa f32 [M];
+ *   gsplit  bf16 [M, cq_group_sum_cols(K)]: the split group sums of `a` written by cq_rotquant
+ *   group   128
+ * The zero-point term sum_g z[g,n] * gsum[g,m] runs on the tensor core (bf16 x bf16 -> fp32, exact products)
+ * and seeds the fp32 accumulator that the per-group int32 partial sums are scaled into.
  */
-CQ_API int cq_gemm_affine(const int8_t* a, const float* sa, const float* gsum, int64_t gsum_ld, const void* b_packed,
-                   const void* s_bf16, const void* z_bf16, const void* bias, void* out, int64_t M, int64_t N,
-                   int64_t K, int group, void* stream);
+CQ_API int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                          const void* s_bf16, const void* zt_bf16, const void* bias, void* out, int64_t M, int64_t N,
+                          int64_t K, int group, void* stream);
 
 /*
  * Fused linears (activation stage + GEMM) with caller-provided scratch.  `workspace` must hold at least
@@ -157,7 +183,8 @@ CQ_API int cq_gemm_affine(const int8_t* a, const float* sa, const float* gsum, i
  * cq_linear_convrot_w4a4: comfy-kitchen convrot_w4a4_linear(x, qweight, wscales, bias, convrot_groupsize,
  *   quant_group_size=64, linear_dtype, input_act) (signature: patches/comfy_kitchen_swiglu_w4a4_fused.patch:41-50,
  *   compile_support.py:84-113).  act_bits 4 or 8 (linear_dtype "int4" / "int8"); swiglu: x is [M, 2K].
- * cq_linear_w4a8_affine: the affine W4A8 linear (rotation optional, per-token int8 activations).
+ * cq_linear_w4a8_affine: the affine W4A8 linear (rotation optional, per-token int8 activations); the zeros are
+ *   passed prepared (zt from cq_prepare_affine_zeros, computed once per weight).
  * cq_linear_w8a8: comfy-kitchen int8_linear(x, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize,
  *   input_act) (tools/_native_probe.py:234-255).
  */
@@ -166,8 +193,8 @@ CQ_API int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N
                            const void* qweight, const float* wscale, const void* bias, void* out, void* workspace,
                            int64_t workspace_bytes, void* stream);
 CQ_API int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
-                          const void* qweight, const void* s_bf16, const void* z_bf16, int group, const void* bias,
-                          void* out, void* workspace, int64_t workspace_bytes, void* stream);
+                                 const void* qweight, const void* s_bf16, const void* zt_bf16, int group,
+                                 const void* bias, void* out, void* workspace, int64_t workspace_bytes, void* stream);
 CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,
                    const float* wscale, const void* bias, void* out, void* workspace, int64_t workspace_bytes,
                    void* stream);

@@ -205,6 +205,24 @@ def group_sums(q: np.ndarray, group: int = 128) -> np.ndarray:
     return q.reshape(m, k // group, group).sum(axis=2).astype(np.int32)
 
 
+def group_sum_cols(k: int) -> int:
+    """Columns of the split group-sum array: 64 * ceil((K / 128) / 32)."""
+    return 64 * ((k // 128 + 31) // 32)
+
+
+def group_sums_split(q: np.ndarray, group: int = 128) -> np.ndarray:
+    """The zero-point operand of the affine GEMM: R = group_sums(q) split exactly into bf16 parts,
+    hi = 128 * floor(R / 128) in column g and lo = R - hi in column G + g, zero-padded to group_sum_cols(K).
+    Returned as float32 values (every entry is exactly representable in bf16)."""
+    r = group_sums(q, group).astype(np.int64)
+    m, g = r.shape
+    hi = np.floor_divide(r, 128) * 128
+    out = np.zeros((m, group_sum_cols(g * group)), np.float32)
+    out[:, :g] = hi
+    out[:, g:2 * g] = r - hi
+    return out
+
+
 def rotquant(x_bits: np.ndarray, rot_group: int, mode: str, swiglu: bool = False, act_group: int = 0):  # noqa: F811
     """The activation stage: (optional SwiGLU) -> rotation -> quantization.
 

@@ -48,15 +48,22 @@ def test_host_side_argument_checks_need_no_device(lib):
     # per-group mode needs act_group 64/128
     assert lib.cq_rotquant(vp, 4, 512, 256, 0, 2, 32, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_ARG
     # GEMM: K must be a multiple of 128; bad weight format
-    assert lib.cq_gemm_rowcol(vp, vp, vp, 0, vp, None, vp, 4, 8, 100, None) == _lib.CQ_ERR_SHAPE
-    assert lib.cq_gemm_rowcol(vp, vp, vp, 7, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ARG
-    # affine: only group 128, gsum leading dimension >= M rounded to 4
-    assert lib.cq_gemm_affine(vp, vp, vp, 4, vp, vp, vp, None, vp, 4, 8, 128, 64, None) == _lib.CQ_ERR_ARG
-    assert lib.cq_gemm_affine(vp, vp, vp, 2, vp, vp, vp, None, vp, 4, 8, 128, 128, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_gemm_rowcol(vp, 0, vp, vp, 0, vp, None, vp, 4, 8, 100, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_gemm_rowcol(vp, 0, vp, vp, 7, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ARG
+    # K-permuted activations only make sense with int4 weights
+    assert lib.cq_gemm_rowcol(vp, 1, vp, vp, 1, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ARG
+    # affine: only group 128; the split group sums must be 16-byte aligned
+    assert lib.cq_gemm_affine(vp, 0, vp, vp, vp, vp, vp, None, vp, 4, 8, 128, 64, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_gemm_affine(vp, 0, vp, ctypes.c_void_p(18), vp, vp, vp, None, vp, 4, 8, 128, 128, None) == \
+        _lib.CQ_ERR_ALIGN
+    assert lib.cq_group_sum_cols(3072) == 64 and lib.cq_group_sum_cols(4096) == 64
+    assert lib.cq_group_sum_cols(4224) == 128 and lib.cq_group_sum_cols(12288) == 192
     # misaligned pointer
-    assert lib.cq_gemm_rowcol(ctypes.c_void_p(17), vp, vp, 0, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ALIGN
+    assert lib.cq_gemm_rowcol(ctypes.c_void_p(17), 0, vp, vp, 0, vp, None, vp, 4, 8, 128, None) == _lib.CQ_ERR_ALIGN
     # empty problems are no-ops
-    assert lib.cq_gemm_rowcol(None, None, None, 0, None, None, None, 0, 8, 128, None) == _lib.CQ_OK
+    assert lib.cq_gemm_rowcol(None, 0, None, None, 0, None, None, None, 0, 8, 128, None) == _lib.CQ_OK
+    # rotquant: K-permuted packed int4 output is not a layout
+    assert lib.cq_rotquant(vp, 4, 512, 256, 0, 1, 0, 4, 2, vp, vp, None, None) == _lib.CQ_ERR_ARG
     # workspace sizing is pure arithmetic
     assert lib.cq_linear_workspace_bytes(4096, 3072) >= 4096 * 3072 + 4096 * 4
     assert lib.cq_linear_workspace_bytes(-1, 3072) == -1

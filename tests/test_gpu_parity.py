@@ -72,7 +72,12 @@ def test_rotquant_int8_rowwise_bit_exact(ops, m, k, rot):
     qr, sr = ref.rotquant(x, rot, "int8")
     assert np.array_equal(q.cpu().numpy(), qr.astype(np.int8))
     assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
-    assert np.array_equal(gs.cpu().numpy().T, ref.group_sums(qr, 128).astype(np.float32))
+    assert np.array_equal(f32_of(gs), ref.group_sums_split(qr, 128))
+    # K-permuted int8 codes: each 8-column block in the order 0,2,4,6,1,3,5,7
+    qp, _, _ = ops.rotquant(bf16_dev(x), rot, 0, kperm=True)
+    perm = np.concatenate([np.arange(0, 8, 2), np.arange(1, 8, 2)])
+    want = qr.reshape(m, k // 8, 8)[:, :, perm].reshape(m, k).astype(np.int8)
+    assert np.array_equal(qp.cpu().numpy(), want)
     _check_status()
 
 
@@ -212,14 +217,31 @@ def test_int32_accumulators_bit_exact_affine(ops, m, n, k):
     acc = ref.int_gemm(a, q - 8)
     s = torch.ones(k // 128, n, dtype=torch.bfloat16, device="cuda")
     z = torch.zeros_like(s)
-    gsum = torch.from_numpy(ref.group_sums(a, 128).T.astype(np.float32).copy()).cuda()
-    out = ops.gemm_affine(torch.from_numpy(a).cuda(), torch.ones(m, device="cuda"), gsum,
+    gs = torch.from_numpy(ref.group_sums_split(a, 128)).to(torch.bfloat16).cuda()
+    out = ops.gemm_affine(torch.from_numpy(a).cuda(), torch.ones(m, device="cuda"), gs,
                           torch.from_numpy(ref.pack_int4(q)).cuda(), s, z)
     assert np.array_equal(f32_of(out), acc.astype(np.float32))
 
 
+@pytest.mark.parametrize("m,n,k", [(256, 128, 128), (300, 200, 3072), (64, 128, 4224)])
+def test_affine_zero_point_term_exact(ops, m, n, k):
+    """scale 0, zero 1: out == sum_g R[g, m] (the tensor-core zero-point pass on the split group sums)."""
+    rng = np.random.default_rng(m + k)
+    a = _sparse_codes(rng, (m, k), 0.02, -1, 1).astype(np.int8)
+    q = np.full((n, k), 8, np.int16)
+    want = ref.group_sums(a, 128).sum(axis=1).astype(np.float32)
+    assert np.abs(want).max() <= 256
+    s = torch.zeros(k // 128, n, dtype=torch.bfloat16, device="cuda")
+    z = torch.ones_like(s)
+    gs = torch.from_numpy(ref.group_sums_split(a, 128)).to(torch.bfloat16).cuda()
+    out = ops.gemm_affine(torch.from_numpy(a).cuda(), torch.ones(m, device="cuda"), gs,
+                          torch.from_numpy(ref.pack_int4(q)).cuda(), s, z)
+    assert np.array_equal(f32_of(out), np.repeat(want[:, None], n, axis=1))
+
+
 @pytest.mark.parametrize("m,n,k,bias", [(300, 200, 768, True), (512, 1024, 3072, True), (64, 384, 2048, False)])
-def test_gemm_rowcol_random_scales(ops, m, n, k, bias):
+@pytest.mark.parametrize("kperm", [False, True])
+def test_gemm_rowcol_random_scales(ops, m, n, k, bias, kperm):
     rng = np.random.default_rng(k + m)
     a = rng.integers(-127, 128, size=(m, k)).astype(np.int8)
     b = rng.integers(-7, 8, size=(n, k)).astype(np.int8)
@@ -227,9 +249,13 @@ def test_gemm_rowcol_random_scales(ops, m, n, k, bias):
     sb = (rng.random(n) * 0.01 + 0.005).astype(np.float32)
     bb = ref.synth_bias(n, seed=k) if bias else None
     want = ref.linear_rowcol(a, sa, b, sb, None if bb is None else ref.bf16_bits_to_f32(bb))
-    out = ops.gemm_rowcol(torch.from_numpy(a).cuda(), torch.from_numpy(sa).cuda(),
+    ad = a
+    if kperm:
+        perm = np.concatenate([np.arange(0, 8, 2), np.arange(1, 8, 2)])
+        ad = a.reshape(m, k // 8, 8)[:, :, perm].reshape(m, k)
+    out = ops.gemm_rowcol(torch.from_numpy(np.ascontiguousarray(ad)).cuda(), torch.from_numpy(sa).cuda(),
                           torch.from_numpy(ref.pack_int4(b)).cuda(), torch.from_numpy(sb).cuda(),
-                          None if bb is None else bf16_dev(bb))
+                          None if bb is None else bf16_dev(bb), a_kperm=kperm)
     assert_bf16_close(out, want)
 
 
