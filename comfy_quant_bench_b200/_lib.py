@@ -57,6 +57,7 @@ SIGNATURES = {
     "cq_linear_w4a8_affine": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64,
                                      _vp]),
     "cq_linear_w8a8": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "cq_linear_w4a8_affine_noalloc": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp]),
 }
 
 

@@ -3,3 +3,4 @@
 #include "rotquant.cu"
 #include "gemm_sm100.cu"
 #include "capi.cu"
+#include "noalloc.cu"

@@ -199,6 +199,21 @@ CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int ro
                    const float* wscale, const void* bias, void* out, void* workspace, int64_t workspace_bytes,
                    void* stream);
 
+/*
+ * cq_linear_w4a8_affine without a workspace argument: for callers that cannot allocate device memory where
+ * they run the linear (a frozen or defragmenting memory pool, allocator hooks that must not re-enter the
+ * allocator, plugins handed only input and output buffers).  No counterpart in the reference.
+ * The scratch (activation codes, scales, split group sums) is a fixed 32 MiB device array inside this library,
+ * held by every GPU that loads it until the process exits; problems needing more than that
+ * (cq_linear_workspace_bytes(M, K) > 32 MiB, e.g. M = 8192 at K = 3072 fits, M = 16384 does not) return
+ * CQ_ERR_CAPACITY.  All calls share the array: calls that overlap on the GPU race, so serialize them on one
+ * stream.  The first call on each device looks up the array's device address; make it before any stream
+ * capture.  It calls no cudaMalloc / cudaFree.
+ */
+CQ_API int cq_linear_w4a8_affine_noalloc(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
+                                         const void* qweight, const void* s_bf16, const void* zt_bf16, int group,
+                                         const void* bias, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
