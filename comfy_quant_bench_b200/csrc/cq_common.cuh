@@ -172,21 +172,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
-// 32 lanes x 8 consecutive 32-bit columns, every element set to `v` (thread i writes row lane_base + i).
-// The instruction reads its 8 values from 8 consecutive registers, so the narrow shape keeps the register
-// cost of a fill small.
-__device__ __forceinline__ void tmem_st_32x32b_x8_fill(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};"
-               ::"r"(taddr), "r"(v) : "memory");
-}
-// fill `ncols` (a multiple of 8) columns starting at taddr
-template <int NCOLS>
-__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v) {
-#pragma unroll
-  for (int c = 0; c < NCOLS; c += 8) tmem_st_32x32b_x8_fill(taddr + c, v);
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte swizzle layout: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), version 1 (sm_100), base offset 0 (tiles are 1024-byte aligned).
 __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {

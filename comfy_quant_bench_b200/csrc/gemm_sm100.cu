@@ -11,19 +11,19 @@
 //   warps 2-7   converters: unpack int4 -> int8 from the TMA ring into a 3-stage ring laid out as the tensor
 //               core's K-major 128-byte-swizzled operand (nibble v becomes the byte 16*v, the 1/16 is folded
 //               into the weight scale; with K-permuted activations each 32-bit word unpacks with one shift and
-//               two masks, no byte shuffles), 16 packed bytes per item, then fence.proxy.async and arrive;
+//               two masks, no byte shuffles), 16 packed bytes per item, then fence.proxy.async and arrive.
+//               Each pair of converter warps owns one converter stage and takes every third K block, so three
+//               blocks are converted at once;
 //   warp 1      MMA issuer: 4 x tcgen05.mma (128 x 256 x 32) per K block into a double-buffered TMEM
 //               accumulator (2 x 256 columns); tcgen05.commit releases both rings and hands buffers over;
 //   warps 8-15  epilogue: tcgen05.ld the int32 partial sums.  Affine weights (per 128-group scale/zero) drain
-//               every group into fp32 registers with packed f32x2 ops, acc += s[g,n] * P_g, starting from the
+//               every group into fp32 registers, acc += s[g,n] * float(P_g) (the exact int32 -> fp32 conversion
+//               runs on the integer pipe, the packed f32x2 FMA on the FMA pipe, side by side), starting from the
 //               zero-point term sum_g z[g,n] * R[g,m] that the tensor core computes first (kind::f16: the bf16
 //               zeros, built by the converters, times the tokens' code sums split exactly into bf16 hi/lo parts);
-//               row/col weights drain once per tile.  Output bf16 [M, N] row-major.
-//               Affine accumulators are seeded with the integer 0x4B400000 (the bits of 1.5 * 2^23) before each
-//               group, so the int32 sum P lands in TMEM as the float 1.5 * 2^23 + P (exact, |P| < 2^22) and the
-//               drain needs no int->float conversion: x = f - 1.5 * 2^23 (exact), acc = fma(s, x, acc).  The
-//               epilogue re-seeds a buffer as it releases it; a buffer goes to the MMA only after the epilogue
-//               arrives on its tmem_empty barrier (seeded and empty).
+//               each group's first MMA overwrites the buffer, so the drain only reads TMEM (no re-seeding
+//               stores), and a buffer goes back to the MMA as soon as its last chunk is in registers.
+//               Row/col weights drain once per tile.  Output bf16 [M, N] row-major.
 // int8 weights (W8A8) skip the converters: TMA loads them straight into the operand layout.
 // Every mbarrier wait is bounded (see cq_common.cuh).  No cluster launch, no multicast.
 #include <cstdio>
@@ -39,11 +39,9 @@ constexpr int kBK = 128;       // K elements (bytes of int8) per stage
 constexpr int kTmaStages = 4;
 constexpr int kConvStages = 3;
 constexpr int kThreads = 512;
-constexpr int kConvWarps = 6;          // warps 2..7
-constexpr int kConvThreads = 32 * kConvWarps;
+constexpr int kConvWarps = 6;          // warps 2..7, one pair per converter stage
+static_assert(kConvWarps == 2 * kConvStages, "one pair of converter warps per converter stage");
 constexpr int kEpiWarp0 = 8;           // warps 8..15
-constexpr uint32_t kMagicBits = 0x4B400000u;   // 1.5 * 2^23 as float bits
-constexpr float kMagic = 12582912.0f;
 constexpr int kXBytes = kBT * kBK;          // 32 KB
 constexpr int kWuBytes = kBW * kBK;         // 16 KB (unpacked int4, or TMA-loaded int8 weights)
 constexpr int kWpBytes = kBW * kBK / 2;     //  8 KB (packed int4)
@@ -90,18 +88,6 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
       "mov.b64 {%0, %1}, rd;\n\t}"
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-
-// d = a + b on two fp32 lanes at once
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\t"
-      "mov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
 
@@ -154,7 +140,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       mbar_init(&empty_tma[s], 1);
     }
     for (int s = 0; s < kConvStages; ++s) {
-      mbar_init(&full_conv[s], kConvWarps);
+      mbar_init(&full_conv[s], kConvWarps / kConvStages);   // the pair of converter warps that owns the stage
       mbar_init(&empty_conv[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -257,8 +243,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           const uint32_t b_base = smem_u32(st);
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
-            // affine: every group adds onto the buffer the epilogue seeded with kMagicBits
-            const uint32_t acc = (EPI == EPI_AFFINE) ? 1u : (kb > 0 || k > 0);
+            // affine: every 128-wide group starts its own int32 sum
+            const uint32_t acc = (EPI == EPI_AFFINE) ? (k > 0) : (kb > 0 || k > 0);
             mma_i8(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc, acc);
           }
           tc_commit(&empty_tma[stage]);
@@ -277,54 +263,53 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       }
     } else if (warp >= 2 && kConv) {
       // ------------------------------ int4 -> int8 converters ------------------------------
-      const int ct = threadIdx.x - 64;   // 0..kConvThreads-1
-      int stage = 0, cstage = 0;
+      // Three pairs of warps take this CTA's operand blocks round-robin: pair c converts blocks c, c + 3, c + 6, ...
+      // (block j = the j-th K block of the CTA's tile sequence, zero-point pseudo blocks included) into converter
+      // stage c, so three blocks are in conversion at once instead of one block at a time.
+      const int pair = (warp - 2) >> 1;               // 0..kConvStages-1: this pair's converter stage
+      const int pt = threadIdx.x - 64 * (1 + pair);   // 0..63
+      const int nzb = (EPI == EPI_AFFINE) ? args.nz : 0;
+      const int bpt = nzb + kblocks;                  // operand blocks per tile
+      uint8_t* dst = sm_conv + pair * kWuBytes;
+      // block j = pair + 3 i: its tile, its index b inside the tile and its TMA stage advance incrementally
+      int tile = blockIdx.x, b = pair, stage = pair;
       uint32_t phase = 0, cphase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (EPI == EPI_AFFINE) {
-          // zero-point weight operand: rows n0..n0+127 of the prepared Zt, 64 bf16 columns per pseudo block
+      while (b >= bpt) { b -= bpt; tile += gridDim.x; }
+      for (; tile < num_tiles; cphase ^= 1u) {
+        if (!mbar_wait(&empty_conv[pair], cphase ^ 1u, abort_flag, 9)) break;
+        if (EPI == EPI_AFFINE && b < nzb) {
+          // zero-point weight operand: rows n0..n0+127 of the prepared Zt, 64 bf16 columns per pseudo block (the
+          // matching TMA stage carries the activation-side operand)
           const int n0 = (tile / m_tiles) * kBW;
           const int zt_ld = 64 * args.nz;
-          for (int p = 0; p < args.nz; ++p) {
-            if (!(ok = mbar_wait(&empty_conv[cstage], cphase ^ 1u, abort_flag, 14))) break;
-            uint8_t* dst = sm_conv + cstage * kWuBytes;
-            for (int it = ct; it < kBW * 8; it += kConvThreads) {
-              const int r = it & (kBW - 1), c = it >> 7;
-              const int n = n0 + r;
-              const uint4 v = (n < N) ? *reinterpret_cast<const uint4*>(args.zt + static_cast<int64_t>(n) * zt_ld + 64 * p + 8 * c)
-                                      : make_uint4(0u, 0u, 0u, 0u);
-              *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full_conv[cstage]);
-            // the matching TMA stage carries the activation-side operand; the converters only track its index
-            if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
-            if (++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
+#pragma unroll 1
+          for (int it = pt; it < kBW * 8; it += 64) {
+            const int r = it & (kBW - 1), c = it >> 7;
+            const int n = n0 + r;
+            const uint4 v = (n < N) ? *reinterpret_cast<const uint4*>(args.zt + static_cast<int64_t>(n) * zt_ld + 64 * b + 8 * c)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
           }
-          if (!ok) break;
-        }
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 6))) break;
-          if (!(ok = mbar_wait(&empty_conv[cstage], cphase ^ 1u, abort_flag, 9))) break;
+        } else {
+          if (!mbar_wait(&full_tma[stage], phase, abort_flag, 6)) break;
           const uint8_t* src = sm_tma + stage * P::kTmaStageBytes + kXBytes;
-          uint8_t* dst = sm_conv + cstage * kWuBytes;
           // item = (row r, 16 packed bytes c4): 32 K columns -> output chunks 2*c4 and 2*c4 + 1 of the row
-#pragma unroll 3
-          for (int it = ct; it < kBW * 4; it += kConvThreads) {
+#pragma unroll 2
+          for (int it = pt; it < kBW * 4; it += 64) {
             const int r = it >> 2, c4 = it & 3;
             const uint4 p = *reinterpret_cast<const uint4*>(src + r * 64 + c4 * 16);
             uint8_t* drow = dst + r * 128;
             *reinterpret_cast<uint4*>(drow + (((2 * c4) ^ (r & 7)) << 4)) = unpack16<BFMT, KPERM>(make_uint2(p.x, p.y));
             *reinterpret_cast<uint4*>(drow + (((2 * c4 + 1) ^ (r & 7)) << 4)) = unpack16<BFMT, KPERM>(make_uint2(p.z, p.w));
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full_conv[cstage]);
-          if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
-          if (++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_conv[pair]);
+        b += kConvStages;
+        while (b >= bpt) { b -= bpt; tile += gridDim.x; }
+        stage += kConvStages;
+        if (stage >= kTmaStages) { stage -= kTmaStages; phase ^= 1u; }
       }
     }
   } else {
@@ -339,13 +324,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
-    // hand both accumulator buffers to the MMA issuer (seeded for the affine epilogue)
+    // hand both accumulator buffers to the MMA issuer
     for (int b = 0; b < 2; ++b) {
-      if (EPI == EPI_AFFINE) {
-        const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(b * kBT + half * 128);
-        tmem_fill<128>(taddr, kMagicBits);
-        tmem_wait_st();
-      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
@@ -371,8 +351,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[16 * ch + j] = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
           }
-          tmem_fill<128>(taddr, kMagicBits);
-          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[buf]);
@@ -387,34 +365,28 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           tc_fence_after();
           const float2 s2 = make_float2(s, s);
           const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
-          const float2 neg_magic = make_float2(-kMagic, -kMagic);
-          // software-pipelined drain: chunk c+1 is in flight while chunk c is scaled; each chunk is re-seeded as
-          // soon as it is in registers and the buffer goes back to the MMA before the last chunk's math
+          // software-pipelined drain: chunk c+1 is in flight while chunk c is scaled, and the buffer goes back to
+          // the MMA as soon as the last chunk is in registers
           uint32_t ra[32], rb[32];
           auto scale_chunk = [&](const uint32_t (&r)[32], int ch) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              // the buffer held kMagicBits + P: as a float that is 1.5 * 2^23 + P, so this subtraction is exact
-              const float2 p = fadd2(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_magic);
+              // |P| < 2^22, so the int32 -> fp32 conversion is exact (it runs on the integer pipe, beside the FMAs)
+              const float2 p = make_float2(__int2float_rn(static_cast<int>(r[2 * j])), __int2float_rn(static_cast<int>(r[2 * j + 1])));
               acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
             }
           };
           tmem_ld_32x32b_x32(taddr, ra);
           tmem_wait_ld_dep(ra);
-          tmem_fill<32>(taddr, kMagicBits);
           tmem_ld_32x32b_x32(taddr + 32, rb);
           scale_chunk(ra, 0);
           tmem_wait_ld_dep(rb);
-          tmem_fill<32>(taddr + 32, kMagicBits);
           tmem_ld_32x32b_x32(taddr + 64, ra);
           scale_chunk(rb, 1);
           tmem_wait_ld_dep(ra);
-          tmem_fill<32>(taddr + 64, kMagicBits);
           tmem_ld_32x32b_x32(taddr + 96, rb);
           scale_chunk(ra, 2);
           tmem_wait_ld_dep(rb);
-          tmem_fill<32>(taddr + 96, kMagicBits);
-          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[buf]);
