@@ -58,7 +58,9 @@ struct SmemPlan {
   static constexpr int kTmaStageBytes = kXBytes + kWStageBytes;
   static constexpr int kConvBytes = (BFMT == BF_S8) ? 0 : kConvStages * kWuBytes;
   static constexpr int kData = kTmaStages * kTmaStageBytes + kConvBytes;
-  static constexpr int kBytes = kData + 1024 /*align slack*/ + 256 /*barriers*/;
+  static constexpr int kSaStage = kData + 256;                    // after the barriers: per-token scales
+  static constexpr int kSaBytes = 8 * 128 * 4;                    // 128 fp32 per epilogue warp
+  static constexpr int kBytes = kSaStage + kSaBytes + 1024 /*align slack*/;
 };
 
 struct GemmArgs {
@@ -321,6 +323,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
     // the int4 unpack stores 16*v; fold the 1/16 into the weight scale (exact)
     const float wscale_fold = (BFMT == BF_S8) ? 1.0f : 0.0625f;
+    // this warp's 128 token scales for the store phase (read back as broadcast float4 loads)
+    float* sa_stage = reinterpret_cast<float*>(smem + P::kSaStage) + e * 128;
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
@@ -336,6 +340,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       const bool n_ok = n < N;
       const bool m_full = m0 + 128 <= M;     // every token of this half-tile exists: no per-element checks
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
+      // the tokens' activation scales, one per lane and 32-token chunk, loaded when the tile starts so that their
+      // latency hides behind the tile's MMAs (indices past the last token clamp to it; those rows are not stored)
+      float sa_pre[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sa_pre[c] = __ldg(args.sa + min(m0 + 32 * c + lane, M - 1));
+      auto stage_sa = [&]() {
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sa_stage[32 * c + lane] = sa_pre[c];
+        __syncwarp();
+      };
       if (EPI == EPI_AFFINE) {
         float2 acc[64];
         {
@@ -394,26 +409,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
         if (!ok) break;
+        stage_sa();
         if (n_ok) {
           // column n of the output for tokens m0..m0+127: one pointer walked down the rows
           __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
-          const float* sa = args.sa + m0;
-          // scale index clamped to the last existing token (rows at or past M are not stored)
-          const int mlast = M - 1 - m0;
-          auto sa_at = [&](int i) { return ld_nc_f32_ordered(sa + (m_full ? i : min(i, mlast))); };
-          float sv[4] = {sa_at(0), sa_at(1), sa_at(2), sa_at(3)};
 #pragma unroll
           for (int j4 = 0; j4 < 32; ++j4) {
-            const float c0 = sv[0], c1 = sv[1], c2 = sv[2], c3 = sv[3];
-            if (j4 + 1 < 32) {
-#pragma unroll
-              for (int t = 0; t < 4; ++t) sv[t] = sa_at(4 * (j4 + 1) + t);
-            }
+            const float4 c = *reinterpret_cast<const float4*>(sa_stage + 4 * j4);
             const int m = m0 + 4 * j4;
-            if (m_full || m < M) st_bf16_ordered(orow, __fmaf_rn(acc[2 * j4].x, c0, bias));
-            if (m_full || m + 1 < M) st_bf16_ordered(orow + N, __fmaf_rn(acc[2 * j4].y, c1, bias));
-            if (m_full || m + 2 < M) st_bf16_ordered(orow + 2 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].x, c2, bias));
-            if (m_full || m + 3 < M) st_bf16_ordered(orow + 3 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].y, c3, bias));
+            if (m_full || m < M) st_bf16_ordered(orow, __fmaf_rn(acc[2 * j4].x, c.x, bias));
+            if (m_full || m + 1 < M) st_bf16_ordered(orow + N, __fmaf_rn(acc[2 * j4].y, c.y, bias));
+            if (m_full || m + 2 < M) st_bf16_ordered(orow + 2 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].x, c.z, bias));
+            if (m_full || m + 3 < M) st_bf16_ordered(orow + 3 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].y, c.w, bias));
             orow += 4 * static_cast<int64_t>(N);
           }
         }
@@ -423,7 +430,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         const float sb = n_ok ? args.sb[n] * wscale_fold : 0.0f;
         const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
         __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
-        const float* sa = args.sa + m0;
+        stage_sa();
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t r[32];
@@ -431,11 +438,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           tmem_wait_ld_dep(r);
           if (n_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int mm = 32 * ch + j;
-              if (m_full || m0 + mm < M)
-                orow[0] = __float2bfloat16_rn(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sb), sa[mm], bias));
-              orow += N;
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 c = *reinterpret_cast<const float4*>(sa_stage + 32 * ch + 4 * j4);
+              const float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int mm = 32 * ch + 4 * j4 + t;
+                if (m_full || m0 + mm < M)
+                  orow[0] = __float2bfloat16_rn(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j4 + t])), sb), cv[t], bias));
+                orow += N;
+              }
             }
           }
         }
