@@ -223,9 +223,16 @@ __device__ __forceinline__ float ld_nc_f32_ordered(const float* p) {
   asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
   return v;
 }
-__device__ __forceinline__ void st_bf16_ordered(__nv_bfloat16* p, float v) {
-  const unsigned short b = __bfloat16_as_ushort(__float2bfloat16_rn(v));
-  asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(b) : "memory");
+// v0 -> *p0 and v1 -> *p1 as bf16 (round to nearest even): one paired conversion (cvt.rn.bf16x2.f32 runs at four
+// times the rate of the single-value form) and two 16-bit stores.
+__device__ __forceinline__ void st_bf16_pair_ordered(__nv_bfloat16* p0, __nv_bfloat16* p1, float v0, float v1) {
+  asm volatile(
+      "{\n\t.reg .b32 d;\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.bf16x2.f32 d, %3, %2;\n\t"
+      "mov.b32 {lo, hi}, d;\n\t"
+      "st.global.b16 [%0], lo;\n\t"
+      "st.global.b16 [%1], hi;\n\t}"
+      ::"l"(p0), "l"(p1), "f"(v0), "f"(v1) : "memory");
 }
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }

@@ -273,6 +273,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       const int nzb = (EPI == EPI_AFFINE) ? args.nz : 0;
       const int bpt = nzb + kblocks;                  // operand blocks per tile
       uint8_t* dst = sm_conv + pair * kWuBytes;
+      // the thread's items are it = pt + 64 i (i = 0..7): row (pt >> 2) + 16 i, 16-byte column c4 = pt & 3.  Row
+      // steps of 16 keep (row & 7), so both swizzled destination chunks sit at fixed offsets from the row start
+      // and every address below is a per-thread base plus an immediate.
+      const int rr = pt >> 2, c4 = pt & 3;
+      const uint32_t src_off = static_cast<uint32_t>(rr * 64 + c4 * 16);
+      uint8_t* const drow0 = dst + rr * 128;
+      const uint32_t dlo = static_cast<uint32_t>(((2 * c4) ^ (rr & 7)) << 4), dhi = static_cast<uint32_t>(((2 * c4 + 1) ^ (rr & 7)) << 4);
       // block j = pair + 3 i: its tile, its index b inside the tile and its TMA stage advance incrementally
       int tile = blockIdx.x, b = pair, stage = pair;
       uint32_t phase = 0, cphase = 0;
@@ -294,15 +301,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           }
         } else {
           if (!mbar_wait(&full_tma[stage], phase, abort_flag, 6)) break;
-          const uint8_t* src = sm_tma + stage * P::kTmaStageBytes + kXBytes;
-          // item = (row r, 16 packed bytes c4): 32 K columns -> output chunks 2*c4 and 2*c4 + 1 of the row
-#pragma unroll 2
-          for (int it = pt; it < kBW * 4; it += 64) {
-            const int r = it >> 2, c4 = it & 3;
-            const uint4 p = *reinterpret_cast<const uint4*>(src + r * 64 + c4 * 16);
-            uint8_t* drow = dst + r * 128;
-            *reinterpret_cast<uint4*>(drow + (((2 * c4) ^ (r & 7)) << 4)) = unpack16<BFMT, KPERM>(make_uint2(p.x, p.y));
-            *reinterpret_cast<uint4*>(drow + (((2 * c4 + 1) ^ (r & 7)) << 4)) = unpack16<BFMT, KPERM>(make_uint2(p.z, p.w));
+          const uint8_t* src = sm_tma + stage * P::kTmaStageBytes + kXBytes + src_off;
+          // item i: 16 packed bytes (32 K columns) of row rr + 16 i -> output chunks 2*c4 and 2*c4 + 1 of that row
+#pragma unroll 4
+          for (int i = 0; i < kBW / 16; ++i) {
+            const uint4 p = *reinterpret_cast<const uint4*>(src + i * 1024);
+            *reinterpret_cast<uint4*>(drow0 + i * 2048 + dlo) = unpack16<BFMT, KPERM>(make_uint2(p.x, p.y));
+            *reinterpret_cast<uint4*>(drow0 + i * 2048 + dhi) = unpack16<BFMT, KPERM>(make_uint2(p.z, p.w));
           }
         }
         fence_proxy_async_smem();
@@ -417,10 +422,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           for (int j4 = 0; j4 < 32; ++j4) {
             const float4 c = *reinterpret_cast<const float4*>(sa_stage + 4 * j4);
             const int m = m0 + 4 * j4;
-            if (m_full || m < M) st_bf16_ordered(orow, __fmaf_rn(acc[2 * j4].x, c.x, bias));
-            if (m_full || m + 1 < M) st_bf16_ordered(orow + N, __fmaf_rn(acc[2 * j4].y, c.y, bias));
-            if (m_full || m + 2 < M) st_bf16_ordered(orow + 2 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].x, c.z, bias));
-            if (m_full || m + 3 < M) st_bf16_ordered(orow + 3 * static_cast<int64_t>(N), __fmaf_rn(acc[2 * j4 + 1].y, c.w, bias));
+            const float v0 = __fmaf_rn(acc[2 * j4].x, c.x, bias), v1 = __fmaf_rn(acc[2 * j4].y, c.y, bias);
+            const float v2 = __fmaf_rn(acc[2 * j4 + 1].x, c.z, bias), v3 = __fmaf_rn(acc[2 * j4 + 1].y, c.w, bias);
+            if (m_full || m + 3 < M) {
+              st_bf16_pair_ordered(orow, orow + N, v0, v1);
+              st_bf16_pair_ordered(orow + 2 * static_cast<int64_t>(N), orow + 3 * static_cast<int64_t>(N), v2, v3);
+            } else {
+              // partial tile: rows at or past M are not stored (the paired form writes both rows)
+              __nv_bfloat16* rows[4] = {orow, orow + N, orow + 2 * static_cast<int64_t>(N), orow + 3 * static_cast<int64_t>(N)};
+              const float vs[4] = {v0, v1, v2, v3};
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                if (m + t < M) *rows[t] = __float2bfloat16_rn(vs[t]);
+            }
             orow += 4 * static_cast<int64_t>(N);
           }
         }
@@ -442,11 +456,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
               const float4 c = *reinterpret_cast<const float4*>(sa_stage + 32 * ch + 4 * j4);
               const float cv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
+              for (int t = 0; t < 4; t += 2) {
                 const int mm = 32 * ch + 4 * j4 + t;
-                if (m_full || m0 + mm < M)
-                  orow[0] = __float2bfloat16_rn(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j4 + t])), sb), cv[t], bias));
-                orow += N;
+                const float v0 = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j4 + t])), sb), cv[t], bias);
+                const float v1 = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j4 + t + 1])), sb), cv[t + 1], bias);
+                if (m_full || m0 + mm + 1 < M) {
+                  st_bf16_pair_ordered(orow, orow + N, v0, v1);
+                } else if (m0 + mm < M) {
+                  *orow = __float2bfloat16_rn(v0);
+                }
+                orow += 2 * static_cast<int64_t>(N);
               }
             }
           }
