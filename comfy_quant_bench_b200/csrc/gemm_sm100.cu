@@ -376,13 +376,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (lane == 0) mbar_arrive(&tmem_empty[buf]);
           if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
-        // the weight scale of the next group is loaded one group ahead (its latency hides behind a drain)
-        float s_next = n_ok ? __bfloat162float(args.ws[n]) * wscale_fold : 0.0f;
+        // the weight scale of the next group is loaded one group ahead as raw bf16 bits and converted only when it
+        // is used, so its latency hides behind a drain instead of stalling the warp at the load
+        const unsigned short* ws_bits = reinterpret_cast<const unsigned short*>(args.ws) + n;
+        unsigned short s_bits_next = n_ok ? __ldg(ws_bits) : static_cast<unsigned short>(0);
         for (int g = 0; g < kblocks; ++g) {
-          const float s = s_next;
-          if (g + 1 < kblocks && n_ok) s_next = __bfloat162float(args.ws[static_cast<int64_t>(g + 1) * N + n]) * wscale_fold;
+          const unsigned short s_bits = s_bits_next;
+          if (g + 1 < kblocks && n_ok) s_bits_next = __ldg(ws_bits + static_cast<int64_t>(g + 1) * N);
           if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 7))) break;
           tc_fence_after();
+          const float s = bf16_bits_to_f32(s_bits) * wscale_fold;
           const float2 s2 = make_float2(s, s);
           const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
           // software-pipelined drain: chunk c+1 is in flight while chunk c is scaled, and the buffer goes back to
