@@ -66,9 +66,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the phase with parity `parity` (a few cycles when the phase is already complete, where the
+// suspending form above costs several times more).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with parity `parity` to complete; false on timeout or when the CTA aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int where) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
@@ -93,6 +105,18 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+
+// TMA tensor store (2-D) from shared memory into global memory, tracked by this thread's bulk-async groups.
+// Coordinates are element indices into the tensor map (never negative here); out-of-range parts are clipped.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until every committed bulk store of this thread has finished reading its shared-memory source
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// wait until every committed bulk store of this thread has completed
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -233,6 +257,17 @@ __device__ __forceinline__ void st_bf16_pair_ordered(__nv_bfloat16* p0, __nv_bfl
       "st.global.b16 [%0], lo;\n\t"
       "st.global.b16 [%1], hi;\n\t}"
       ::"l"(p0), "l"(p1), "f"(v0), "f"(v1) : "memory");
+}
+
+// v0 -> shared address a0 and v1 -> a1 as bf16 (round to nearest even), one paired conversion
+__device__ __forceinline__ void sts_bf16_pair(uint32_t a0, uint32_t a1, float v0, float v1) {
+  asm volatile(
+      "{\n\t.reg .b32 d;\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.bf16x2.f32 d, %3, %2;\n\t"
+      "mov.b32 {lo, hi}, d;\n\t"
+      "st.shared.b16 [%0], lo;\n\t"
+      "st.shared.b16 [%1], hi;\n\t}"
+      ::"r"(a0), "r"(a1), "f"(v0), "f"(v1) : "memory");
 }
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }

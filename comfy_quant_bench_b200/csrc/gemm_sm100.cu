@@ -36,7 +36,6 @@ namespace cq {
 constexpr int kBW = 128;       // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kBT = 256;       // tokens per tile (MMA N, TMEM columns per accumulator buffer)
 constexpr int kBK = 128;       // K elements (bytes of int8) per stage
-constexpr int kTmaStages = 4;
 constexpr int kConvStages = 3;
 constexpr int kThreads = 512;
 constexpr int kConvWarps = 6;          // warps 2..7, one pair per converter stage
@@ -51,16 +50,21 @@ constexpr int kEpilogueRegs = 216;   // warps 8-15; 256*40 + 256*216 = 128*512, 
 enum : int { EPI_ROWCOL = 0, EPI_AFFINE = 1 };
 enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 
-// shared-memory plan per weight format
-template <int BFMT>
+// shared-memory plan per epilogue and weight format.  The affine kernel trades one TMA stage for the output
+// staging buffers of its asynchronous (TMA) output stores.
+template <int EPI, int BFMT>
 struct SmemPlan {
+  static constexpr int kStages = (EPI == EPI_AFFINE) ? 3 : 4;       // TMA ring depth
   static constexpr int kWStageBytes = (BFMT == BF_S8) ? kWuBytes : kWpBytes;   // weight bytes in the TMA ring
   static constexpr int kTmaStageBytes = kXBytes + kWStageBytes;
   static constexpr int kConvBytes = (BFMT == BF_S8) ? 0 : kConvStages * kWuBytes;
-  static constexpr int kData = kTmaStages * kTmaStageBytes + kConvBytes;
+  static constexpr int kData = kStages * kTmaStageBytes + kConvBytes;
   static constexpr int kSaStage = kData + 256;                    // after the barriers: per-token scales
   static constexpr int kSaBytes = 8 * 128 * 4;                    // 128 fp32 per epilogue warp
-  static constexpr int kBytes = kSaStage + kSaBytes + 1024 /*align slack*/;
+  static constexpr int kOutStage = kSaStage + kSaBytes;           // output staging: 64 tokens x 32 columns bf16
+  static constexpr int kOutWarpBytes = 64 * 32 * 2;               //   per epilogue warp (affine only)
+  static constexpr int kOutBytes = (EPI == EPI_AFFINE) ? 8 * kOutWarpBytes : 0;
+  static constexpr int kBytes = kOutStage + kOutBytes + 1024 /*align slack*/;
 };
 
 struct GemmArgs {
@@ -72,6 +76,7 @@ struct GemmArgs {
   __nv_bfloat16* out;    // [M, N]
   int M, N, K;
   int nz;                // affine: zero-point pseudo blocks per tile (64 bf16 columns of the split sums each)
+  int tma_out;           // affine: outputs leave through the TMA store map (N % 8 == 0, 16-byte aligned out)
 };
 
 __device__ __forceinline__ void setmaxnreg_dec() {
@@ -110,8 +115,9 @@ __device__ __forceinline__ uint4 unpack16(uint2 p) {
 template <int EPI, int BFMT, bool KPERM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-            const __grid_constant__ CUtensorMap tm_r, const GemmArgs args) {
-  using P = SmemPlan<BFMT>;
+            const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_o, const GemmArgs args) {
+  using P = SmemPlan<EPI, BFMT>;
+  constexpr int kTmaStages = P::kStages;
   constexpr bool kConv = BFMT != BF_S8;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -154,6 +160,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     prefetch_tensormap(&tm_x);
     prefetch_tensormap(&tm_w);
     if (EPI == EPI_AFFINE) prefetch_tensormap(&tm_r);
+    if (EPI == EPI_AFFINE && args.tma_out) prefetch_tensormap(&tm_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -236,7 +243,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 3))) break;
             tc_fence_after();
           }
-          if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 4))) break;
+          // int4 weights: the converters waited on full_tma before they arrived on full_conv, so full_conv alone
+          // orders both the activation tile and the converted weights before these MMAs
+          if (!kConv && !(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 4))) break;
           if (kConv && !(ok = mbar_wait(&full_conv[cstage], cphase, abort_flag, 5))) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
@@ -418,7 +427,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         }
         if (!ok) break;
         stage_sa();
-        if (n_ok) {
+        if (args.tma_out) {
+          // two passes of 64 tokens: bf16 results into this warp's staging buffer ([token][32 columns]), then one
+          // TMA tensor store per pass.  The store drains in the background while the warp moves on; rows past M
+          // and columns past N are clipped by the tensor map.
+          unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOutStage + e * P::kOutWarpBytes);
+          const uint32_t ost_lane = smem_u32(ost) + 2u * lane;
+          const int x0 = (tile / m_tiles) * kBW + quad * 32;
+#pragma unroll
+          for (int pass = 0; pass < 2; ++pass) {
+            if (lane == 0) bulk_wait_group_read0();   // the previous store has finished reading the buffer
+            __syncwarp();
+#pragma unroll
+            for (int j4 = 0; j4 < 16; ++j4) {
+              const int t = 64 * pass + 4 * j4;
+              const float4 c = *reinterpret_cast<const float4*>(sa_stage + t);
+              const float v0 = __fmaf_rn(acc[t / 2].x, c.x, bias), v1 = __fmaf_rn(acc[t / 2].y, c.y, bias);
+              const float v2 = __fmaf_rn(acc[t / 2 + 1].x, c.z, bias), v3 = __fmaf_rn(acc[t / 2 + 1].y, c.w, bias);
+              sts_bf16_pair(ost_lane + (4 * j4) * 64u, ost_lane + (4 * j4 + 1) * 64u, v0, v1);
+              sts_bf16_pair(ost_lane + (4 * j4 + 2) * 64u, ost_lane + (4 * j4 + 3) * 64u, v2, v3);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && x0 < N && m0 + 64 * pass < M) {   // boxes wholly past the edge are not issued
+              tma_store_2d(&tm_o, ost, x0, m0 + 64 * pass);
+              bulk_commit_group();
+            }
+          }
+        } else if (n_ok) {
           // column n of the output for tokens m0..m0+127: one pointer walked down the rows
           __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
 #pragma unroll
@@ -481,6 +517,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     }
   }
 
+  // outstanding TMA output stores of this thread complete before the CTA exits
+  if (EPI == EPI_AFFINE && warp >= kEpiWarp0 && lane == 0) bulk_wait_group0();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -543,12 +581,25 @@ static bool make_map_u8(CUtensorMap* map, const void* base, int64_t rows, int64_
   return r == CUDA_SUCCESS;
 }
 
+// 2-D bf16 tensor map over the [rows, cols] output (row stride cols), box box_cols x box_rows, no swizzle.
+static bool make_map_bf16(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static int g_num_sms = 0;
 
 template <int EPI, int BFMT, bool KPERM>
 static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args, cudaStream_t st) {
   auto kern = gemm_kernel<EPI, BFMT, KPERM>;
-  constexpr int smem_bytes = SmemPlan<BFMT>::kBytes;
+  constexpr int smem_bytes = SmemPlan<EPI, BFMT>::kBytes;
   static bool configured = false;
   static bool regs_ok = false;
   if (!configured) {
@@ -568,7 +619,7 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_num_sms <= 0) return CQ_ERR_CUDA;
   }
-  CUtensorMap tm_x, tm_w, tm_r;
+  CUtensorMap tm_x, tm_w, tm_r, tm_o;
   if (!make_map_u8(&tm_x, a, args.M, args.K, kBK, kBT, true)) return CQ_ERR_CUDA;
   if (EPI == EPI_AFFINE) {
     if (!make_map_u8(&tm_r, rsplit, args.M, 2 * rsplit_cols(args.K), 128, kBT, true)) return CQ_ERR_CUDA;
@@ -580,10 +631,18 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
   } else {
     if (!make_map_u8(&tm_w, b, args.N, args.K / 2, kBK / 2, kBW, false)) return CQ_ERR_CUDA;
   }
+  GemmArgs ga = args;
+  ga.tma_out = 0;
+  if (EPI == EPI_AFFINE && args.N % 8 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0) {
+    if (!make_map_bf16(&tm_o, args.out, args.M, args.N, 32, 64)) return CQ_ERR_CUDA;
+    ga.tma_out = 1;
+  } else {
+    tm_o = tm_x;   // unused
+  }
   const int tiles = ((args.M + kBT - 1) / kBT) * ((args.N + kBW - 1) / kBW);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
   if (grid == 0) return CQ_OK;
-  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, args);
+  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_o, ga);
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
 
