@@ -115,7 +115,8 @@ __device__ __forceinline__ uint4 unpack16(uint2 p) {
 template <int EPI, int BFMT, bool KPERM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-            const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_o, const GemmArgs args) {
+            const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_z,
+            const __grid_constant__ CUtensorMap tm_o, const GemmArgs args) {
   using P = SmemPlan<EPI, BFMT>;
   constexpr int kTmaStages = P::kStages;
   constexpr bool kConv = BFMT != BF_S8;
@@ -131,7 +132,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   uint64_t* empty_conv = full_conv + kConvStages;
   uint64_t* tmem_full = empty_conv + kConvStages;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  uint64_t* zt_full = tmem_empty + 2;   // affine: per converter pair, the TMA load of its zero-point operand
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(zt_full + kConvStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -150,6 +152,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     for (int s = 0; s < kConvStages; ++s) {
       mbar_init(&full_conv[s], kConvWarps / kConvStages);   // the pair of converter warps that owns the stage
       mbar_init(&empty_conv[s], 1);
+      mbar_init(&zt_full[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
@@ -160,6 +163,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     prefetch_tensormap(&tm_x);
     prefetch_tensormap(&tm_w);
     if (EPI == EPI_AFFINE) prefetch_tensormap(&tm_r);
+    if (EPI == EPI_AFFINE) prefetch_tensormap(&tm_z);
     if (EPI == EPI_AFFINE && args.tma_out) prefetch_tensormap(&tm_o);
   }
   if (warp == 1) {
@@ -291,23 +295,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       const uint32_t dlo = static_cast<uint32_t>(((2 * c4) ^ (rr & 7)) << 4), dhi = static_cast<uint32_t>(((2 * c4 + 1) ^ (rr & 7)) << 4);
       // block j = pair + 3 i: its tile, its index b inside the tile and its TMA stage advance incrementally
       int tile = blockIdx.x, b = pair, stage = pair;
-      uint32_t phase = 0, cphase = 0;
+      uint32_t phase = 0, cphase = 0, zphase = 0;
       while (b >= bpt) { b -= bpt; tile += gridDim.x; }
       for (; tile < num_tiles; cphase ^= 1u) {
         if (!mbar_wait(&empty_conv[pair], cphase ^ 1u, abort_flag, 9)) break;
         if (EPI == EPI_AFFINE && b < nzb) {
-          // zero-point weight operand: rows n0..n0+127 of the prepared Zt, 64 bf16 columns per pseudo block (the
-          // matching TMA stage carries the activation-side operand)
-          const int n0 = (tile / m_tiles) * kBW;
-          const int zt_ld = 64 * args.nz;
-#pragma unroll 1
-          for (int it = pt; it < kBW * 8; it += 64) {
-            const int r = it & (kBW - 1), c = it >> 7;
-            const int n = n0 + r;
-            const uint4 v = (n < N) ? *reinterpret_cast<const uint4*>(args.zt + static_cast<int64_t>(n) * zt_ld + 64 * b + 8 * c)
-                                    : make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+          // zero-point weight operand: rows n0..n0+127 of the prepared Zt, 64 bf16 columns per pseudo block, one TMA
+          // load straight into this stage in the operand layout (rows past N read as zeros).  The matching TMA
+          // stage carries the activation-side operand.
+          if (warp == 2 + 2 * pair && lane == 0) {
+            mbar_arrive_expect_tx(&zt_full[pair], kWuBytes);
+            tma_load_2d(dst, &tm_z, &zt_full[pair], 128 * b, (tile / m_tiles) * kBW);
           }
+          if (!mbar_wait(&zt_full[pair], zphase, abort_flag, 16)) break;
+          zphase ^= 1u;
         } else {
           if (!mbar_wait(&full_tma[stage], phase, abort_flag, 6)) break;
           const uint8_t* src = sm_tma + stage * P::kTmaStageBytes + kXBytes + src_off;
@@ -619,12 +620,15 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_num_sms <= 0) return CQ_ERR_CUDA;
   }
-  CUtensorMap tm_x, tm_w, tm_r, tm_o;
+  CUtensorMap tm_x, tm_w, tm_r, tm_z, tm_o;
   if (!make_map_u8(&tm_x, a, args.M, args.K, kBK, kBT, true)) return CQ_ERR_CUDA;
   if (EPI == EPI_AFFINE) {
     if (!make_map_u8(&tm_r, rsplit, args.M, 2 * rsplit_cols(args.K), 128, kBT, true)) return CQ_ERR_CUDA;
+    // prepared zeros Zt [N, 64 * nz] bf16 as bytes: 128-byte column blocks, 128 weight rows, operand swizzle
+    if (!make_map_u8(&tm_z, args.zt, args.N, 128 * static_cast<int64_t>(args.nz), 128, kBW, true)) return CQ_ERR_CUDA;
   } else {
     tm_r = tm_x;   // unused
+    tm_z = tm_x;
   }
   if (BFMT == BF_S8) {
     if (!make_map_u8(&tm_w, b, args.N, args.K, kBK, kBW, true)) return CQ_ERR_CUDA;
@@ -642,7 +646,7 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
   const int tiles = ((args.M + kBT - 1) / kBT) * ((args.N + kBW - 1) / kBW);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
   if (grid == 0) return CQ_OK;
-  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_o, ga);
+  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_o, ga);
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
 
