@@ -1,0 +1,215 @@
+"""Qwen-Image-like dual-stream MMDiT denoise step with every linear on the W4A8 affine path (random init).
+
+This is the model-level workload of the quantized-linear path: a stack of dual-stream (image + text) MMDiT
+blocks whose linears - per-stream adaLN modulation, QKV, attention output, MLP up and down - all run
+``ops.w4a8_affine_linear`` (ConvRot-256 rotation + per-token int8 activations, packed uint4 weights with bf16
+per-128-group scale/zero, tcgen05 GEMM).  The block follows the usual MMDiT layout (SD3 / Flux / Qwen-Image):
+
+    mod   = Linear(silu(temb))                    -> shift1, scale1, gate1, shift2, scale2, gate2 per stream
+    x_n   = LayerNorm(x) * (1 + scale1) + shift1  (no affine)
+    q,k,v = Linear_qkv(x_n) per stream, RMSNorm(q), RMSNorm(k) per head, rotary embedding on q, k
+    joint attention over [text; image] tokens (torch scaled_dot_product_attention)
+    x     = x + gate1 * Linear_out(attn)
+    x     = x + gate2 * Linear_fc2(gelu_tanh(Linear_fc1(LayerNorm(x) * (1 + scale2) + shift2)))
+
+Norms, rotary embedding, GELU and attention are plain torch ops: they are not part of the quantized-linear path
+(fused attention/normalisation kernels are a separate work item).  Weights are drawn N(0, 0.02) per linear from a
+seeded generator, quantized on the device with the library's weight kernel, and only the packed form is kept.
+
+``MMDiT.step(..., reference=True)`` runs the same step with every linear replaced by a torch fp32 product of the
+dequantized weights (W = (q - 8) * scale + zeros, in the rotated basis) and the dequantized activation codes that
+the library's own activation kernel produced: it checks the GEMM and its epilogue inside the whole model.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from . import _lib
+
+
+@dataclass(frozen=True)
+class MMDiTConfig:
+    blocks: int = 60
+    hidden: int = 3072
+    heads: int = 24
+    mlp: int = 12288
+    img_tokens: int = 4096        # 1024^2 latent with 2x2 patches
+    txt_tokens: int = 256
+    group_size: int = 128
+    convrot_groupsize: int = 256
+    quantize_modulation: bool = True   # BASELINE: every linear W4A8; the reference excludes modulation layers
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+
+class QLinear:
+    """One W4A8 affine linear (packed uint4 weight, bf16 scale/zero [K/128, N], prepared zero operand)."""
+
+    def __init__(self, in_f: int, out_f: int, gen: torch.Generator, device, cfg: MMDiTConfig, bias: bool = True):
+        w = torch.randn(out_f, in_f, generator=gen, device=device, dtype=torch.float32).mul_(0.02)
+        self.qweight, self.scale, self.zeros = ops.quantize_affine_w4_weight(w, cfg.group_size, cfg.convrot_groupsize)
+        del w
+        self.zt = ops.prepare_affine_zeros(self.zeros, cfg.group_size)
+        self.bias = (torch.randn(out_f, generator=gen, device=device, dtype=torch.float32) * 0.01).to(torch.bfloat16) if bias else None
+        self.cfg = cfg
+        self.in_f, self.out_f = in_f, out_f
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.w4a8_affine_linear(x, self.qweight, self.scale, self.zeros, self.bias, self.cfg.group_size,
+                                      self.cfg.convrot_groupsize, zeros_prepared=self.zt)
+
+    def dequantized_weight(self) -> torch.Tensor:
+        """W in the rotated basis, fp32 [N, K]: (q - 8) * scale + zeros per 128-wide group."""
+        q8 = self.qweight.view(torch.uint8)
+        q = torch.stack((q8 & 15, q8 >> 4), dim=-1).reshape(self.out_f, self.in_f).float()
+        g = self.cfg.group_size
+        s = self.scale.float().t().repeat_interleave(g, dim=1)
+        z = self.zeros.float().t().repeat_interleave(g, dim=1)
+        return (q - 8.0) * s + z
+
+    def reference(self, x: torch.Tensor) -> torch.Tensor:
+        """The same linear in torch fp32 on the library's own activation codes (dequantized) and the dequantized
+        weight; bf16 out."""
+        x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
+        q, sx, _ = ops.rotquant(x2, self.cfg.convrot_groupsize, _lib.CQ_ACT_INT8_ROW)
+        m = x2.shape[0]
+        xa = q[:m].float() * sx[:m, None]
+        y = xa @ self.dequantized_weight().t()
+        if self.bias is not None:
+            y = y + self.bias.float()
+        return y.to(torch.bfloat16).reshape(*x.shape[:-1], self.out_f)
+
+
+class _Stream:
+    """The per-stream (image or text) linears and norm weights of one block."""
+
+    def __init__(self, gen, device, cfg: MMDiTConfig):
+        h = cfg.hidden
+        self.mod = QLinear(h, 6 * h, gen, device, cfg) if cfg.quantize_modulation else None
+        self.mod_bf16 = None
+        if not cfg.quantize_modulation:
+            self.mod_bf16 = (torch.randn(6 * h, h, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+        self.qkv = QLinear(h, 3 * h, gen, device, cfg)
+        self.out = QLinear(h, h, gen, device, cfg)
+        self.fc1 = QLinear(h, cfg.mlp, gen, device, cfg)
+        self.fc2 = QLinear(cfg.mlp, h, gen, device, cfg)
+        self.q_norm = torch.ones(cfg.head_dim, device=device, dtype=torch.bfloat16)
+        self.k_norm = torch.ones(cfg.head_dim, device=device, dtype=torch.bfloat16)
+
+
+def _rope_table(n: int, dim: int, device, offset: int = 0) -> torch.Tensor:
+    """Rotary factors exp(i * pos * 10000^(-2j/dim)) for positions offset..offset+n-1, complex64 [n, dim/2]."""
+    inv = 1.0 / (10000.0 ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim))
+    pos = torch.arange(offset, offset + n, device=device, dtype=torch.float32)
+    ang = torch.outer(pos, inv)
+    return torch.complex(torch.cos(ang), torch.sin(ang))
+
+
+def _apply_rope(x: torch.Tensor, rot: torch.Tensor) -> torch.Tensor:
+    """Rotate interleaved pairs of the head dim: x [S, H, D] bf16 by rot [S, D/2] complex64 -> bf16."""
+    xc = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+    return torch.view_as_real(xc * rot[:, None, :]).reshape(x.shape).to(torch.bfloat16)
+
+
+class MMDiT:
+    def __init__(self, cfg: MMDiTConfig = MMDiTConfig(), device="cuda", seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(seed)
+        self.blocks = [(_Stream(gen, self.device, cfg), _Stream(gen, self.device, cfg)) for _ in range(cfg.blocks)]
+        d = cfg.head_dim
+        self.rope_txt = _rope_table(cfg.txt_tokens, d, self.device)
+        self.rope_img = _rope_table(cfg.img_tokens, d, self.device, offset=cfg.txt_tokens)
+
+    # ---- per-linear dispatch (kernel path or torch reference) ----
+    @staticmethod
+    def _lin(layer: QLinear, x: torch.Tensor, reference: bool) -> torch.Tensor:
+        return layer.reference(x) if reference else layer(x)
+
+    def _mod(self, st: _Stream, temb_act: torch.Tensor, reference: bool) -> torch.Tensor:
+        if st.mod is not None:
+            return self._lin(st.mod, temb_act, reference)
+        return F.linear(temb_act, st.mod_bf16)
+
+    def linears(self):
+        """Every QLinear of the model, in block order."""
+        out = []
+        for img, txt in self.blocks:
+            for st in (img, txt):
+                out += [l for l in (st.mod, st.qkv, st.out, st.fc1, st.fc2) if l is not None]
+        return out
+
+    def weight_bytes(self) -> int:
+        return sum(l.qweight.numel() + 2 * l.scale.numel() * 2 + l.zt.numel() * 2 for l in self.linears())
+
+    def linear_int_ops(self) -> float:
+        """2 * M * N * K summed over the quantized linears of one step."""
+        c = self.cfg
+        tot = 0.0
+        for img, txt in self.blocks:
+            for st, m in ((img, c.img_tokens), (txt, c.txt_tokens)):
+                if st.mod is not None:
+                    tot += 2.0 * 1 * st.mod.out_f * st.mod.in_f
+                for l in (st.qkv, st.out, st.fc1, st.fc2):
+                    tot += 2.0 * m * l.out_f * l.in_f
+        return tot
+
+    def attention_flops(self) -> float:
+        c = self.cfg
+        s = c.img_tokens + c.txt_tokens
+        return 4.0 * s * s * c.hidden * c.blocks
+
+    def step(self, img: torch.Tensor, txt: torch.Tensor, temb: torch.Tensor, reference: bool = False):
+        """One denoise step: img [S_img, hidden], txt [S_txt, hidden], temb [1, hidden] (bf16).  Returns img, txt.
+
+        The glue around the linears stays in bf16 (fp32 inside the norms and the rotary rotation): layer norm,
+        modulation as one fused multiply-add, q/k/v written straight into the joint [heads, tokens, dim]
+        attention layout, GELU on bf16, gated residual as one fused multiply-add."""
+        c = self.cfg
+        h, nh, d = c.hidden, c.heads, c.head_dim
+        st_txt, st_img = txt.shape[0], img.shape[0]
+        s_all = st_txt + st_img
+        temb_act = F.silu(temb.float()).to(torch.bfloat16)
+        q = torch.empty(1, nh, s_all, d, dtype=torch.bfloat16, device=img.device)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        for si, st in self.blocks:
+            mi = self._mod(si, temb_act, reference).chunk(6, dim=-1)
+            mt = self._mod(st, temb_act, reference).chunk(6, dim=-1)
+            for x, s, m, rot, lo, hi in ((txt, st, mt, self.rope_txt, 0, st_txt),
+                                         (img, si, mi, self.rope_img, st_txt, s_all)):
+                xn = torch.addcmul(m[0], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[1])
+                y = self._lin(s.qkv, xn, reference).view(x.shape[0], 3, nh, d)
+                q[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 0], (d,), s.q_norm, eps=1e-6), rot).transpose(0, 1)
+                k[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 1], (d,), s.k_norm, eps=1e-6), rot).transpose(0, 1)
+                v[0, :, lo:hi] = y[:, 2].transpose(0, 1)
+            a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
+            new = []
+            for x, s, m, att in ((txt, st, mt, a[:st_txt]), (img, si, mi, a[st_txt:])):
+                x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
+                xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
+                f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
+                new.append(torch.addcmul(x, m[5], self._lin(s.fc2, f, reference)))
+            txt, img = new
+        return img, txt
+
+    def inputs(self, seed: int = 1):
+        c = self.cfg
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        img = torch.randn(c.img_tokens, c.hidden, generator=g, device=self.device).to(torch.bfloat16)
+        txt = torch.randn(c.txt_tokens, c.hidden, generator=g, device=self.device).to(torch.bfloat16)
+        temb = torch.randn(1, c.hidden, generator=g, device=self.device).to(torch.bfloat16)
+        return img, txt, temb
+
+
+def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
+    a64, b64 = a.double(), b.double()
+    return float((a64 - b64).norm() / b64.norm().clamp_min(1e-30))
