@@ -1,6 +1,7 @@
 """Benchmark of the W4A8 quantized linear (BASELINE north-star workload) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload w4a8|w4a4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload w4a8|w4a4|c1|mmdit]
+                    [--mode dp|tp]
 
 One step = one pass of the hot path over one synthetic batch: activation rotation (ConvRot g256) + per-token
 int8 quantization, then the packed-int4 x int8 tcgen05 GEMM with the per-group affine epilogue, bf16 out.
@@ -10,7 +11,13 @@ Timing: W warm-up steps, then K steps each bracketed by CUDA events on the launc
 (256 MiB memset, outside the events) before every step so every step reads its inputs from HBM.  The K step
 times are summed; the whole timed loop is bracketed by a barrier + synchronize; the max over ranks is taken.
 N > 1 runs N data-parallel replicas (sampler batches, one process per GPU, no collective in the step:
-"scaling": "weak"); ``--mode tp`` instead shards N column-parallel with an NCCL all-gather of the output.
+"scaling": "weak"); ``--mode tp`` instead shards the linear's N column-parallel over the ranks (each rank rotates
+and quantizes the full activation, runs its N/P columns, and an NCCL all-gather assembles the [M, N] bf16 output:
+"scaling": "strong").
+
+``--workload mmdit`` times one denoise step of a Qwen-Image-like 60-block dual-stream MMDiT with every linear on
+the W4A8 affine path (4096 image + 256 text tokens, hidden 3072, MLP 12288; random init; graph-replayed), as
+data-parallel replicas across ranks: value = steps/s over all ranks, ms_per_step = the step latency.
 
 ``--impl reference`` times the reference's CPU path (dequantize-and-matmul, oracle port) on the host cores.
 """
@@ -35,6 +42,7 @@ WORKLOADS = {
     "w4a8": (4096, 3072, 12288, 256, "W4A8 linear, affine int4 g128 weights (bf16 scale/zero), ConvRot g256, "
                                      "per-token int8 acts, bf16 out"),
     "w4a4": (4096, 3072, 12288, 256, "ConvRot W4A4 linear, per-row int4 weights, per-token int4 acts, bf16 out"),
+    "c1": (4096, 3072, 3072, 0, "W4A8 linear (BASELINE config 1), affine int4 g128, no rotation, per-token int8 acts"),
 }
 
 
@@ -145,7 +153,7 @@ def make_problem(workload: str, seed: int, dev):
     x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16).to(dev)
     w = torch.from_numpy(ref.synth_weight(n, k, seed=seed + 1)).to(dev)
     bias = torch.from_numpy(ref.synth_bias(n, seed=seed + 2).view(np.int16)).view(torch.bfloat16).to(dev)
-    if workload == "w4a8":
+    if workload in ("w4a8", "c1"):
         qw, s, z = ops.quantize_affine_w4_weight(w, group_size=128, convrot_groupsize=rot)
         weights = (qw, s, z)
     else:
@@ -208,7 +216,9 @@ def run_ours(args, world, rank, local):
 
     # stage buffers for the kernel-level timing (same kernels the fused call enqueues)
     mp = (m + 15) // 16 * 16
-    if args.workload == "w4a8":
+    if args.mode == "tp":
+        return run_tp(args, world, rank, local, x, weights, bias)
+    if args.workload in ("w4a8", "c1"):
         qw, s, z = weights
         zt = ops.prepare_affine_zeros(z, 128)   # once per weight, as the layout class does at load
 
@@ -236,9 +246,9 @@ def run_ours(args, world, rank, local):
             return ops.convrot_w4a4_linear(xin, qw, sw, bias, convrot_groupsize=rot)
 
     def one_step(ev):
-        # a ~0.1 ms spin on the device (outside the events) lets the host enqueue both stages before the GPU reaches
+        # a ~0.5 ms spin on the device (outside the events) lets the host enqueue both stages before the GPU reaches
         # them, so the stage events time the kernels rather than host launch latency
-        torch.cuda._sleep(200_000)
+        torch.cuda._sleep(1_000_000)
         ev[0].record(stream)
         a = stage1()
         ev[1].record(stream)
@@ -303,7 +313,7 @@ def run_ours(args, world, rank, local):
         ts = []
         for _ in range(10):
             flush.zero_()
-            torch.cuda._sleep(200_000)
+            torch.cuda._sleep(1_000_000)
             e0.record(stream)
             torch._int_mm(a8, b8)
             e1.record(stream)
@@ -328,16 +338,16 @@ def run_ours(args, world, rank, local):
             traffic = json.load(f).get("dram_bytes_per_launch")
     act_bytes = m * k * 2 + m * k * 1 + m * 4 + (k // 128) * mp * 4
     line = {
-        "metric": "W4A8 linear INT8-TOPS" if args.workload == "w4a8" else "W4A4 linear INT8-TOPS",
+        "metric": "W4A4 linear INT8-TOPS" if args.workload == "w4a4" else "W4A8 linear INT8-TOPS",
         "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic",
         "config": {"workload": f"{args.workload}_linear", "desc": desc, "M": m, "K": k, "N": n,
-                   "convrot_groupsize": rot, "group_size": 128 if args.workload == "w4a8" else None,
+                   "convrot_groupsize": rot, "group_size": None if args.workload == "w4a4" else 128,
                    "parallelism": f"dp{world}", "l2": "flushed before every step (256 MiB memset outside the events)",
                    "inputs": "x ~ N(0,1) bf16 with 1% outlier channels x20, W ~ N(0,0.02), bias ~ N(0,0.01), seeded"},
         "breakdown_ms": {"rotquant": quant_ms, "gemm": gemm_ms},
-        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<affine>" if args.workload == "w4a8" else "gemm_kernel<rowcol>",
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<rowcol>" if args.workload == "w4a4" else "gemm_kernel<affine>",
                      "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
                      "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16_tflops']} TFLOP/s; B200 int8 "
                                     "dense rate is twice bf16)",
@@ -351,14 +361,173 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": e2e_val, "unit": "TOPS", "ms_per_step": e2e_ms, "h2d_bytes_per_step": m * k * 2,
                 "d2h_bytes_per_step": m * n * 2,
                 "path": "ops.w4a8_affine_linear (C ABI cq_linear_w4a8_affine) with pinned host buffers"
-                        if args.workload == "w4a8" else "ops.convrot_w4a4_linear (C ABI cq_linear_convrot_w4a4)"},
+                        if args.workload != "w4a4" else "ops.convrot_w4a4_linear (C ABI cq_linear_convrot_w4a4)"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.workload if args.workload == "w4a8" else "w4a8", args.cpu_rows,
+        line["cpu_baseline"] = cpu_baseline("w4a8" if args.workload == "w4a4" else args.workload, args.cpu_rows,
                                             args.cpu_steps)
     print(json.dumps(line), flush=True)
+
+
+def run_tp(args, world, rank, local, x, weights, bias):
+    """Column-parallel linear: rotquant on every rank, the local N/P GEMM, NCCL all-gather of the bf16 output."""
+    import torch.distributed as dist
+    from comfy_quant_bench_b200 import ops, _lib, dist as cqdist
+    dev = torch.device("cuda", local)
+    m, k, n, rot, desc = WORKLOADS[args.workload]
+    if args.workload == "w4a4":
+        raise SystemExit("--mode tp is built for the W4A8 affine workloads")
+    qw, s, z, b = cqdist.shard_affine(*weights, bias, rank, world)
+    zt = ops.prepare_affine_zeros(z, 128)
+    nl = qw.shape[0]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    mp = (m + 15) // 16 * 16
+    gbuf = torch.empty(world * m, nl, dtype=torch.bfloat16, device=dev)
+
+    def one_step(ev):
+        torch.cuda._sleep(1_000_000)
+        ev[0].record(stream)
+        q, sx, gs = ops.rotquant(x, rot, _lib.CQ_ACT_INT8_ROW, m_pad=mp, group_sums=True, kperm=True)
+        y = ops.gemm_affine(q[:m], sx[:m], gs, qw, s, z, b, a_kperm=True, zeros_prepared=zt)
+        ev[1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gbuf, y)
+            out = gbuf.view(world, m, nl).permute(1, 0, 2).reshape(m, world * nl)
+        else:
+            out = y
+        ev[2].record(stream)
+        return out
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        one_step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            out = one_step(evs[i])
+        torch.cuda.synchronize()
+    barrier(world)
+    if _lib.take_device_status() != (0, 0):
+        raise RuntimeError("device status set")
+    compute_ms = allreduce_max(sum(e[0].elapsed_time(e[1]) for e in evs), world)
+    gather_ms = allreduce_max(sum(e[1].elapsed_time(e[2]) for e in evs), world)
+    total_ms = allreduce_max(sum(e[0].elapsed_time(e[2]) for e in evs), world)
+    ops_step = 2.0 * m * n * k
+    gathered = m * n * 2
+    line = {
+        "metric": "W4A8 linear INT8-TOPS", "value": ops_step * args.steps / (total_ms / 1e3) / 1e12, "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{args.workload}_linear_column_parallel", "desc": desc, "M": m, "K": k, "N": n,
+                   "N_per_rank": nl, "convrot_groupsize": rot, "group_size": 128, "parallelism": f"tp{world}",
+                   "l2": "flushed before every step (256 MiB memset outside the events)"},
+        "breakdown_ms": {"rotquant_plus_local_gemm": compute_ms / args.steps, "all_gather_plus_relayout": gather_ms / args.steps},
+        "per_gpu_tops": ops_step / world / (compute_ms / args.steps / 1e3) / 1e12,
+        "all_gather": {"bytes": gathered, "algbw_gbs": gathered / (gather_ms / args.steps / 1e3) / 1e9 if world > 1 else None,
+                       "busbw_gbs": gathered * (world - 1) / world / (gather_ms / args.steps / 1e3) / 1e9 if world > 1 else None},
+        "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_mmdit(args, world, rank, local):
+    """One MMDiT denoise step per replica per iteration, graph-replayed; data-parallel over ranks."""
+    from comfy_quant_bench_b200 import mmdit as mm, _lib
+    dev = torch.device("cuda", local)
+    cfg = mm.MMDiTConfig(blocks=args.mmdit_blocks)
+    model = mm.MMDiT(cfg, device=dev, seed=0)
+    img, txt, temb = model.inputs(seed=1 + rank)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        model.step(img, txt, temb)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        model.step(img, txt, temb)
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out_img, out_txt = model.step(img, txt, temb)
+    graph.replay()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for e0, e1 in evs:
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in evs), world)
+    step_ms = total_ms / args.steps
+    # e2e: the step's inputs from pinned host memory into the graph's input buffers, the step, its image output back
+    h_img, h_txt, h_temb = img.cpu().pin_memory(), txt.cpu().pin_memory(), temb.cpu().pin_memory()
+    y_host = torch.empty_like(out_img, device="cpu").pin_memory()
+    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(3, min(args.steps, 10)))]
+    barrier(world)
+    for e0, e1 in ee:
+        e0.record(stream)
+        img.copy_(h_img, non_blocking=True)
+        txt.copy_(h_txt, non_blocking=True)
+        temb.copy_(h_temb, non_blocking=True)
+        graph.replay()
+        y_host.copy_(out_img, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in ee), world) / len(ee)
+    st = _lib.take_device_status()
+    if st != (0, 0):
+        raise RuntimeError(f"device status {st}")
+    lin_ops = model.linear_int_ops()
+    peaks = _peaks()
+    line = {
+        "metric": "MMDiT denoise steps/s", "value": world * args.steps / (total_ms / 1e3), "unit": "steps/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 linears, bf16 glue",
+        "data": "synthetic (random-init weights N(0,0.02), inputs N(0,1))",
+        "config": {"workload": "mmdit_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads,
+                   "mlp": cfg.mlp, "img_tokens": cfg.img_tokens, "txt_tokens": cfg.txt_tokens, "batch": 1,
+                   "linears": "every linear W4A8 affine g128, ConvRot g256 (modulation included)",
+                   "parallelism": f"dp{world}", "l2": "weights (%.1f GB) larger than L2" % (model.weight_bytes() / 1e9),
+                   "graph": "one CUDA graph per step"},
+        "step_latency_ms": step_ms,
+        "linear_int_ops_per_step": lin_ops, "attention_flops_per_step": model.attention_flops(),
+        "roofline": {"bound": "tensor", "kernel": "step-level: linear int-ops / step time (the GEMM kernel alone is "
+                                                  "measured by the w4a8 workload)",
+                     "achieved": lin_ops / (step_ms / 1e3) / 1e12, "peak": 2.0 * peaks["bf16_tflops"], "unit": "TOPS",
+                     "frac": lin_ops / (step_ms / 1e3) / 1e12 / (2.0 * peaks["bf16_tflops"]), "traffic": None},
+        "e2e": {"value": world / (e2e_ms / 1e3), "unit": "steps/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": (img.numel() + txt.numel() + temb.numel()) * 2,
+                "d2h_bytes_per_step": out_img.numel() * 2,
+                "path": "graph-replayed MMDiT step with pinned-host input/output copies"},
+        "gpu_launches": 2 * len(model.linears()) * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_reference_check:
+        ref_img, _ = model.step(img, txt, temb, reference=True)
+        line["reference_check"] = {"rel_l2_img": mm.rel_l2(out_img, ref_img),
+                                   "against": "the same step with every linear as a torch fp32 product of the "
+                                              "dequantized weight and the dequantized activation codes"}
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline("w4a8", args.cpu_rows, args.cpu_steps)
+        line["cpu_baseline"] = {"value": cb["value"] * 1e12 / lin_ops, "unit": "steps/s", "cores": cb["cores"],
+                                "kind": cb["kind"],
+                                "sample": cb["sample"] + "; steps/s = that CPU rate over the step's linear int-ops "
+                                                         "(attention and glue not counted)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
 
 
 def main():
@@ -367,7 +536,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="w4a8")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit"], default="w4a8")
+    ap.add_argument("--mode", choices=["dp", "tp"], default="dp")
+    ap.add_argument("--mmdit-blocks", type=int, default=60)
+    ap.add_argument("--no-reference-check", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--cpu-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -378,6 +550,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "mmdit":
+            run_mmdit(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
