@@ -13,7 +13,8 @@ times are summed; the whole timed loop is bracketed by a barrier + synchronize; 
 N > 1 runs N data-parallel replicas (sampler batches, one process per GPU, no collective in the step:
 "scaling": "weak"); ``--mode tp`` instead shards the linear's N column-parallel over the ranks (each rank rotates
 and quantizes the full activation, runs its N/P columns, and an NCCL all-gather assembles the [M, N] bf16 output:
-"scaling": "strong").
+"scaling": "strong"); ``--mode tp_fused`` writes each rank's columns into every rank's output from inside the GEMM
+(peer TMA stores into symmetric memory) instead of running an all-gather.
 
 ``--workload mmdit`` times one denoise step of a Qwen-Image-like 60-block dual-stream MMDiT with every linear on
 the W4A8 affine path (4096 image + 256 text tokens, hidden 3072, MLP 12288; random init; graph-replayed), as
@@ -216,7 +217,7 @@ def run_ours(args, world, rank, local):
 
     # stage buffers for the kernel-level timing (same kernels the fused call enqueues)
     mp = (m + 15) // 16 * 16
-    if args.mode == "tp":
+    if args.mode in ("tp", "tp_fused"):
         return run_tp(args, world, rank, local, x, weights, bias)
     if args.workload in ("w4a8", "c1"):
         qw, s, z = weights
@@ -382,6 +383,8 @@ def run_tp(args, world, rank, local, x, weights, bias):
     qw, s, z, b = cqdist.shard_affine(*weights, bias, rank, world)
     zt = ops.prepare_affine_zeros(z, 128)
     nl = qw.shape[0]
+    fused = cqdist.FusedColumnParallelW4A8(*weights, bias, rank, world, max_tokens=m, convrot_groupsize=rot) \
+        if args.mode == "tp_fused" else None
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     mp = (m + 15) // 16 * 16
@@ -390,6 +393,11 @@ def run_tp(args, world, rank, local, x, weights, bias):
     def one_step(ev):
         torch.cuda._sleep(1_000_000)
         ev[0].record(stream)
+        if fused is not None:   # the GEMM writes every rank's output; the barriers are the only synchronization
+            out = fused(x)
+            ev[1].record(stream)
+            ev[2].record(stream)
+            return out
         q, sx, gs = ops.rotquant(x, rot, _lib.CQ_ACT_INT8_ROW, m_pad=mp, group_sums=True, kperm=True)
         y = ops.gemm_affine(q[:m], sx[:m], gs, qw, s, z, b, a_kperm=True, zeros_prepared=zt)
         ev[1].record(stream)
@@ -416,6 +424,13 @@ def run_tp(args, world, rank, local, x, weights, bias):
     barrier(world)
     if _lib.take_device_status() != (0, 0):
         raise RuntimeError("device status set")
+    gather_check = None
+    if fused is not None:
+        # the assembled [M, N] output on this rank against this rank's own full single-GPU linear
+        full = ops.w4a8_affine_linear(x, *weights, bias, 128, rot, zeros_prepared=ops.prepare_affine_zeros(weights[2], 128))
+        same = torch.equal(out, full)
+        bad = allreduce_max(0.0 if same else 1.0, world)
+        gather_check = "bit-identical to the single-GPU linear on every rank" if bad == 0.0 else "MISMATCH"
     compute_ms = allreduce_max(sum(e[0].elapsed_time(e[1]) for e in evs), world)
     gather_ms = allreduce_max(sum(e[1].elapsed_time(e[2]) for e in evs), world)
     total_ms = allreduce_max(sum(e[0].elapsed_time(e[2]) for e in evs), world)
@@ -425,15 +440,22 @@ def run_tp(args, world, rank, local, x, weights, bias):
         "metric": "W4A8 linear INT8-TOPS", "value": ops_step * args.steps / (total_ms / 1e3) / 1e12, "unit": "TOPS",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": f"{args.workload}_linear_column_parallel", "desc": desc, "M": m, "K": k, "N": n,
+        "config": {"workload": f"{args.workload}_linear_column_parallel" + ("_fused_gather" if fused else ""),
+                   "desc": desc, "M": m, "K": k, "N": n,
                    "N_per_rank": nl, "convrot_groupsize": rot, "group_size": 128, "parallelism": f"tp{world}",
                    "l2": "flushed before every step (256 MiB memset outside the events)"},
-        "breakdown_ms": {"rotquant_plus_local_gemm": compute_ms / args.steps, "all_gather_plus_relayout": gather_ms / args.steps},
+        "breakdown_ms": ({"rotquant_plus_gemm_with_peer_stores_and_barriers": compute_ms / args.steps} if fused else
+                         {"rotquant_plus_local_gemm": compute_ms / args.steps,
+                          "all_gather_plus_relayout": gather_ms / args.steps}),
         "per_gpu_tops": ops_step / world / (compute_ms / args.steps / 1e3) / 1e12,
-        "all_gather": {"bytes": gathered, "algbw_gbs": gathered / (gather_ms / args.steps / 1e3) / 1e9 if world > 1 else None,
-                       "busbw_gbs": gathered * (world - 1) / world / (gather_ms / args.steps / 1e3) / 1e9 if world > 1 else None},
+        "all_gather": ({"bytes": gathered, "fused": "peer TMA stores inside the GEMM"} if fused else
+                       {"bytes": gathered,
+                        "algbw_gbs": gathered / (gather_ms / args.steps / 1e3) / 1e9 if world > 1 else None,
+                        "busbw_gbs": gathered * (world - 1) / world / (gather_ms / args.steps / 1e3) / 1e9 if world > 1 else None}),
         "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
     }
+    if gather_check is not None:
+        line["gather_check"] = gather_check
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -537,7 +559,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit"], default="w4a8")
-    ap.add_argument("--mode", choices=["dp", "tp"], default="dp")
+    ap.add_argument("--mode", choices=["dp", "tp", "tp_fused"], default="dp")
     ap.add_argument("--mmdit-blocks", type=int, default=60)
     ap.add_argument("--no-reference-check", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=256)

@@ -58,6 +58,10 @@ SIGNATURES = {
                                      _vp]),
     "cq_linear_w8a8": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "cq_linear_w4a8_affine_noalloc": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp]),
+    "cq_gemm_affine_peers": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64,
+                                    _int, _vp]),
+    "cq_linear_w4a8_affine_peers": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _int,
+                                           _i64, _i64, _vp, _i64, _vp]),
 }
 
 

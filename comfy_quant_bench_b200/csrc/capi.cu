@@ -212,6 +212,44 @@ int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int r
   return cq_gemm_rowcol(w.xq, 1, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream);
 }
 
+int cq_gemm_affine_peers(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                         const void* s_bf16, const void* zt_bf16, const void* bias, void* const* outs, int n_outs,
+                         int64_t col0, int64_t ldo, int64_t M, int64_t N, int64_t K, int group, void* stream) {
+  if (group != 128) return CQ_ERR_ARG;
+  if (a_kperm != 0 && a_kperm != 1) return CQ_ERR_ARG;
+  if (outs == nullptr || n_outs < 1 || n_outs > cq::kMaxOutBuffers) return CQ_ERR_ARG;
+  for (int i = 0; i < n_outs; ++i) {
+    if (outs[i] == nullptr) return CQ_ERR_ARG;
+    if (!aligned(outs[i], 16)) return CQ_ERR_ALIGN;
+  }
+  // whole 32-column store boxes of this launch, 16-byte aligned, inside the output rows
+  if (N % 32 != 0 || col0 < 0 || col0 % 8 != 0 || ldo % 8 != 0 || col0 + N > ldo || ldo > kMaxRows)
+    return CQ_ERR_SHAPE;
+  if (int e = check_gemm(a, b_packed, outs[0], M, N, K)) return e;
+  if (M == 0) return CQ_OK;
+  if (K > kMaxK) return CQ_ERR_SHAPE;
+  if (sa == nullptr || gsplit == nullptr || s_bf16 == nullptr || zt_bf16 == nullptr) return CQ_ERR_ARG;
+  if (!aligned(gsplit, 16) || !aligned(zt_bf16, 16)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  return cq::launch_gemm_affine(a, a_kperm, sa, gsplit, b_packed, s_bf16, zt_bf16, bias, outs[0], static_cast<int>(M),
+                                static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream), outs,
+                                n_outs, static_cast<int>(col0), ldo);
+}
+
+int cq_linear_w4a8_affine_peers(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
+                                const void* qweight, const void* s_bf16, const void* zt_bf16, int group,
+                                const void* bias, void* const* outs, int n_outs, int64_t col0, int64_t ldo,
+                                void* workspace, int64_t workspace_bytes, void* stream) {
+  if (M == 0) return CQ_OK;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
+                          stream))
+    return e;
+  return cq_gemm_affine_peers(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, outs, n_outs, col0, ldo, M, N,
+                              K, group, stream);
+}
+
 int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
                           const void* qweight, const void* s_bf16, const void* zt_bf16, int group, const void* bias,
                           void* out, void* workspace, int64_t workspace_bytes, void* stream) {

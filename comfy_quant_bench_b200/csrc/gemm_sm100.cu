@@ -41,6 +41,7 @@ constexpr int kThreads = 512;
 constexpr int kConvWarps = 6;          // warps 2..7, one pair per converter stage
 static_assert(kConvWarps == 2 * kConvStages, "one pair of converter warps per converter stage");
 constexpr int kEpiWarp0 = 8;           // warps 8..15
+constexpr int kMaxOutMaps = kMaxOutBuffers;   // affine: output buffers one launch writes (column-parallel)
 constexpr int kXBytes = kBT * kBK;          // 32 KB
 constexpr int kWuBytes = kBW * kBK;         // 16 KB (unpacked int4, or TMA-loaded int8 weights)
 constexpr int kWpBytes = kBW * kBK / 2;     //  8 KB (packed int4)
@@ -67,6 +68,12 @@ struct SmemPlan {
   static constexpr int kBytes = kOutStage + kOutBytes + 1024 /*align slack*/;
 };
 
+// Output tensor maps of the affine epilogue: map i covers buffer i ([M, ldo] bf16); every staged output box is
+// stored to each of the first n_out maps at column out_col0 + its tile column.
+struct OutMaps {
+  CUtensorMap m[kMaxOutMaps];
+};
+
 struct GemmArgs {
   const float* sa;       // [M] activation scale
   const float* sb;       // [N] weight scale (rowcol)
@@ -76,7 +83,9 @@ struct GemmArgs {
   __nv_bfloat16* out;    // [M, N]
   int M, N, K;
   int nz;                // affine: zero-point pseudo blocks per tile (64 bf16 columns of the split sums each)
-  int tma_out;           // affine: outputs leave through the TMA store map (N % 8 == 0, 16-byte aligned out)
+  int tma_out;           // affine: outputs leave through the TMA store maps (N % 8 == 0, 16-byte aligned out)
+  int n_out;             // affine with tma_out: number of output maps (1, or the ranks of a column-parallel layer)
+  int out_col0;          // affine with tma_out: column of the output maps where this launch's N columns start
 };
 
 __device__ __forceinline__ void setmaxnreg_dec() {
@@ -116,7 +125,7 @@ template <int EPI, int BFMT, bool KPERM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
             const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_z,
-            const __grid_constant__ CUtensorMap tm_o, const GemmArgs args) {
+            const __grid_constant__ OutMaps tm_out, const GemmArgs args) {
   using P = SmemPlan<EPI, BFMT>;
   constexpr int kTmaStages = P::kStages;
   constexpr bool kConv = BFMT != BF_S8;
@@ -164,7 +173,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     prefetch_tensormap(&tm_w);
     if (EPI == EPI_AFFINE) prefetch_tensormap(&tm_r);
     if (EPI == EPI_AFFINE) prefetch_tensormap(&tm_z);
-    if (EPI == EPI_AFFINE && args.tma_out) prefetch_tensormap(&tm_o);
+    if (EPI == EPI_AFFINE && args.tma_out)
+      for (int i = 0; i < args.n_out; ++i) prefetch_tensormap(&tm_out.m[i]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -451,7 +461,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0 && x0 < N && m0 + 64 * pass < M) {   // boxes wholly past the edge are not issued
-              tma_store_2d(&tm_o, ost, x0, m0 + 64 * pass);
+              // one store per output buffer (column-parallel layers: this rank's columns into every rank's output)
+              for (int i = 0; i < args.n_out; ++i) tma_store_2d(&tm_out.m[i], ost, args.out_col0 + x0, m0 + 64 * pass);
               bulk_commit_group();
             }
           }
@@ -597,8 +608,17 @@ static bool make_map_bf16(CUtensorMap* map, void* base, int64_t rows, int64_t co
 
 static int g_num_sms = 0;
 
+// Output destinations of an affine launch: n buffers of [M, ldo] bf16, this launch's columns starting at col0.
+struct OutSpec {
+  void* const* ptrs;
+  int n;
+  int col0;
+  int64_t ldo;
+};
+
 template <int EPI, int BFMT, bool KPERM>
-static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args, cudaStream_t st) {
+static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args, cudaStream_t st,
+                         const OutSpec* outs = nullptr) {
   auto kern = gemm_kernel<EPI, BFMT, KPERM>;
   constexpr int smem_bytes = SmemPlan<EPI, BFMT>::kBytes;
   static bool configured = false;
@@ -620,7 +640,8 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_num_sms <= 0) return CQ_ERR_CUDA;
   }
-  CUtensorMap tm_x, tm_w, tm_r, tm_z, tm_o;
+  CUtensorMap tm_x, tm_w, tm_r, tm_z;
+  OutMaps tm_out;
   if (!make_map_u8(&tm_x, a, args.M, args.K, kBK, kBT, true)) return CQ_ERR_CUDA;
   if (EPI == EPI_AFFINE) {
     if (!make_map_u8(&tm_r, rsplit, args.M, 2 * rsplit_cols(args.K), 128, kBT, true)) return CQ_ERR_CUDA;
@@ -637,16 +658,25 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
   }
   GemmArgs ga = args;
   ga.tma_out = 0;
-  if (EPI == EPI_AFFINE && args.N % 8 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0) {
-    if (!make_map_bf16(&tm_o, args.out, args.M, args.N, 32, 64)) return CQ_ERR_CUDA;
+  ga.n_out = 0;
+  ga.out_col0 = 0;
+  std::memset(&tm_out, 0, sizeof(tm_out));
+  // box = one store pass of an epilogue warp: 32 columns x 64 tokens (its 4 KB staging buffer)
+  if (EPI == EPI_AFFINE && outs != nullptr) {
+    for (int i = 0; i < outs->n; ++i)
+      if (!make_map_bf16(&tm_out.m[i], outs->ptrs[i], args.M, outs->ldo, 32, 64)) return CQ_ERR_CUDA;
     ga.tma_out = 1;
-  } else {
-    tm_o = tm_x;   // unused
+    ga.n_out = outs->n;
+    ga.out_col0 = outs->col0;
+  } else if (EPI == EPI_AFFINE && args.N % 8 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0) {
+    if (!make_map_bf16(&tm_out.m[0], args.out, args.M, args.N, 32, 64)) return CQ_ERR_CUDA;
+    ga.tma_out = 1;
+    ga.n_out = 1;
   }
   const int tiles = ((args.M + kBT - 1) / kBT) * ((args.N + kBW - 1) / kBW);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
   if (grid == 0) return CQ_OK;
-  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_o, ga);
+  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_out, ga);
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
 
@@ -665,7 +695,7 @@ int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void
 
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
-                       cudaStream_t st) {
+                       cudaStream_t st, void* const* outs, int n_outs, int col0, int64_t ldo) {
   GemmArgs g{};
   g.sa = sa;
   g.nz = rsplit_cols(K) / 64;
@@ -674,8 +704,10 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   g.bias = static_cast<const __nv_bfloat16*>(bias);
   g.out = static_cast<__nv_bfloat16*>(out);
   g.M = M; g.N = N; g.K = K;
-  if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st);
-  return launch_gemm_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st);
+  const OutSpec spec{outs, n_outs, col0, ldo};
+  const OutSpec* sp = outs != nullptr ? &spec : nullptr;
+  if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st, sp);
+  return launch_gemm_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st, sp);
 }
 
 }  // namespace cq

@@ -9,7 +9,9 @@ Two schemes, both new relative to comfy-quant-bench (which runs on one GPU):
 * ``split_batch`` / data-parallel replicas: sampler batches (cond / uncond, several seeds) are split across
   ranks with no collective in the step.
 
-The gather is the only collective; nothing in the kernels waits on a peer.
+``FusedColumnParallelW4A8`` removes the separate gather: its GEMM stores each output tile into every rank's
+(symmetric-memory) output buffer over NVLink as the tile finishes.  Nothing in the library's kernels waits on a
+peer; the ranks synchronize with torch's symmetric-memory barrier around the launch.
 """
 from __future__ import annotations
 
@@ -85,6 +87,47 @@ class ColumnParallelLinear:
         return cls(lambda x2: ops.convrot_w4a4_linear(x2, q, s, b, convrot_groupsize=convrot_groupsize,
                                                       linear_dtype=linear_dtype),
                    qweight.shape[0], rank, world, group)
+
+
+class FusedColumnParallelW4A8:
+    """Column-parallel W4A8 affine linear whose GEMM writes its output columns straight into every rank's output.
+
+    Each rank holds output rows ``[r*N/P, (r+1)*N/P)`` of the packed weight.  The [max_tokens, N] bf16 output is
+    one symmetric-memory allocation per rank (torch.distributed symmetric memory: every rank maps every other
+    rank's buffer).  The GEMM epilogue stores each finished output tile, by TMA over NVLink, into all P buffers at
+    this rank's columns.  The gather therefore overlaps the GEMM and needs no separate collective or re-layout
+    copy.  A device-side barrier before the launch keeps any rank from overwriting an output that a peer is still
+    reading; one after it makes every rank's columns visible.
+    """
+
+    def __init__(self, qweight, scale, zeros, bias, rank: int, world: int, max_tokens: int, group=None,
+                 group_size: int = 128, convrot_groupsize: int = 0):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import ops
+        if world > 8:
+            raise ValueError("the fused column-parallel GEMM writes at most 8 output buffers")
+        q, s, z, b = shard_affine(qweight, scale, zeros, bias, rank, world)
+        self.q, self.s, self.b = q, s, b
+        self.zt = ops.prepare_affine_zeros(z, group_size)
+        self.n = qweight.shape[0]
+        self.col0 = rank * q.shape[0]
+        self.group_size, self.convrot_groupsize = group_size, convrot_groupsize
+        self.out = symm_mem.empty(max_tokens, self.n, dtype=torch.bfloat16, device=q.device)
+        self.hdl = symm_mem.rendezvous(self.out, group if group is not None else dist.group.WORLD)
+        self.ptrs = [int(p) for p in self.hdl.buffer_ptrs]
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        from . import ops
+        x2 = x.reshape(-1, x.shape[-1])
+        m = x2.shape[0]
+        if m > self.out.shape[0]:
+            raise ValueError(f"{m} tokens exceed the layer's max_tokens {self.out.shape[0]}")
+        self.hdl.barrier(channel=0)
+        ops.w4a8_affine_linear_into(x2, self.q, self.s, self.zt, self.b, self.ptrs, self.col0, self.n,
+                                    group_size=self.group_size, convrot_groupsize=self.convrot_groupsize)
+        self.hdl.barrier(channel=0)
+        return self.out[:m].reshape(*x.shape[:-1], self.n)
 
 
 def split_batch(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:

@@ -16,6 +16,8 @@ on the CPU or on a non-sm_100 device are rejected: there is no eager fallback.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -345,6 +347,37 @@ def w4a8_affine_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     out = out.reshape(*x.shape[:-1], n)
     dt = out_dtype or x.dtype
     return out if dt == torch.bfloat16 else out.to(dt)
+
+
+def w4a8_affine_linear_into(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, zeros_prepared: torch.Tensor,
+                            bias: torch.Tensor | None, outs, col0: int, ldo: int, group_size: int = 128,
+                            convrot_groupsize: int = 0) -> None:
+    """Column-parallel W4A8 linear: this shard's N = qweight.shape[0] output columns are written into every buffer
+    of ``outs`` (bf16 [M, ldo] tensors, or raw device pointers of such buffers, e.g. the peer buffers of a symmetric
+    memory allocation) at columns [col0, col0 + N).  The zeros must be prepared (``prepare_affine_zeros``)."""
+    if group_size != 128:
+        raise ValueError("the W4A8 affine kernel supports group_size 128")
+    k = x.shape[-1]
+    if k != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
+    n = qweight.shape[0]
+    dev = _require_cuda(x, qweight, scale, zeros_prepared, bias)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    ptrs = []
+    for o in outs:
+        if isinstance(o, torch.Tensor):
+            if o.dtype != torch.bfloat16 or o.dim() != 2 or o.shape[1] != ldo or o.shape[0] < m or not o.is_contiguous():
+                raise ValueError(f"output buffers must be contiguous bf16 [>= {m}, {ldo}]")
+            ptrs.append(o.data_ptr())
+        else:
+            ptrs.append(int(o))
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    ws = _workspace(m, k, dev)
+    wp, wb = _ws_ptr(ws)
+    _lib.call("cq_linear_w4a8_affine_peers", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), 0, _ptr(qweight),
+              _ptr(scale), _ptr(zeros_prepared), int(group_size), _ptr(_bias_bf16(bias)), arr, len(ptrs), int(col0),
+              int(ldo), wp, wb, _stream(dev))
 
 
 def gemm_affine(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,

@@ -200,6 +200,24 @@ CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int ro
                    void* stream);
 
 /*
+ * Column-parallel forms of cq_gemm_affine / cq_linear_w4a8_affine: the launch computes N output columns (one rank's
+ * shard of a layer with ldo = N_total outputs) and writes them, as they are produced, into each of the n_outs
+ * (1..8) output buffers outs[i] (bf16 [M, ldo], 16-byte aligned) at columns [col0, col0 + N).  Passing every
+ * rank's output buffer (peer pointers mapped into this process, e.g. symmetric memory) assembles the gathered
+ * [M, ldo] output over NVLink inside the GEMM, with no separate all-gather; the caller still synchronizes the ranks
+ * before reading it.  Requires N % 32 == 0, col0 % 8 == 0, ldo % 8 == 0, col0 + N <= ldo.  No counterpart in the
+ * reference, which runs one GPU: these replace its per-layer output with a sharded layer plus an all-gather.
+ */
+CQ_API int cq_gemm_affine_peers(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                                const void* s_bf16, const void* zt_bf16, const void* bias, void* const* outs,
+                                int n_outs, int64_t col0, int64_t ldo, int64_t M, int64_t N, int64_t K, int group,
+                                void* stream);
+CQ_API int cq_linear_w4a8_affine_peers(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
+                                       const void* qweight, const void* s_bf16, const void* zt_bf16, int group,
+                                       const void* bias, void* const* outs, int n_outs, int64_t col0, int64_t ldo,
+                                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * cq_linear_w4a8_affine without a workspace argument: for callers that cannot allocate device memory where
  * they run the linear (a frozen or defragmenting memory pool, allocator hooks that must not re-enter the
  * allocator, plugins handed only input and output buffers).  No counterpart in the reference.

@@ -387,3 +387,36 @@ def test_errors_raise(ops):
     with pytest.raises(ValueError):
         ops.convrot_w4a4_linear(torch.zeros(4, 256, device="cuda"), torch.zeros(8, 128, dtype=torch.int8, device="cuda"),
                                 torch.ones(8, device="cuda"), linear_dtype="fp8")
+
+
+@pytest.mark.parametrize("m,n,k,col0,ldo", [(300, 256, 1024, 256, 768), (1000, 640, 3072, 0, 1280)])
+def test_affine_linear_into_several_buffers_at_an_offset(ops, m, n, k, col0, ldo):
+    """The column-parallel form writes this shard's columns into every output buffer at col0; the rest stays."""
+    x = bf16_dev(ref.synth_activations(m, k, seed=11))
+    w = torch.from_numpy(ref.synth_weight(n, k, seed=12)).cuda()
+    qw, s, z = ops.quantize_affine_w4_weight(w, 128, 256)
+    zt = ops.prepare_affine_zeros(z, 128)
+    bias = bf16_dev(ref.synth_bias(n, seed=13))
+    want = ops.w4a8_affine_linear(x, qw, s, z, bias, 128, 256, zeros_prepared=zt)
+    outs = [torch.full((m, ldo), 7.0, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    ops.w4a8_affine_linear_into(x, qw, s, zt, bias, outs, col0, ldo, convrot_groupsize=256)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o[:, col0:col0 + n], want)
+        assert (o[:, :col0] == 7.0).all() and (o[:, col0 + n:] == 7.0).all()
+
+
+def test_affine_linear_into_rejects_bad_layouts(ops):
+    from comfy_quant_bench_b200 import _lib
+    m, n, k = 64, 256, 256
+    x = bf16_dev(ref.synth_activations(m, k, seed=1))
+    w = torch.from_numpy(ref.synth_weight(n, k, seed=2)).cuda()
+    qw, s, z = ops.quantize_affine_w4_weight(w, 128, 0)
+    zt = ops.prepare_affine_zeros(z, 128)
+    out = torch.zeros(m, 512, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.CQShapeError):      # columns past the row
+        ops.w4a8_affine_linear_into(x, qw, s, zt, None, [out], 384, 512)
+    with pytest.raises(_lib.CQShapeError):      # offset not a multiple of 8
+        ops.w4a8_affine_linear_into(x, qw, s, zt, None, [out], 4, 512)
+    with pytest.raises(_lib.CQError):           # more than 8 buffers
+        ops.w4a8_affine_linear_into(x, qw, s, zt, None, [out] * 9, 0, 512)
