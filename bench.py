@@ -1,6 +1,6 @@
 """Benchmark of the W4A8 quantized linear (BASELINE north-star workload) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload w4a8|w4a4|c1|mmdit]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload w4a8|w4a4|c1|mmdit|sweep]
                     [--mode dp|tp]
 
 One step = one pass of the hot path over one synthetic batch: activation rotation (ConvRot g256) + per-token
@@ -552,13 +552,87 @@ def run_mmdit(args, world, rank, local):
     del graph
 
 
+def run_sweep(args, world, rank, local):
+    """One JSON line per case: the W4A8 GEMM sweep over M, the activation kernel at large M, and the W4A4
+    (ConvRot 256/64/16, SwiGLU prologue) linears.  Device-timed with CUDA events after a device-side lead; L2 is
+    flushed before every timed call; each line is the median of the calls."""
+    from comfy_quant_bench_b200 import ops, _lib
+    dev = torch.device("cuda", local)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    peaks = _peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+
+    def timed(fn, reps):
+        for _ in range(2):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            torch.cuda._sleep(1_000_000)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    def emit(d):
+        if rank == 0:
+            print(json.dumps(d), flush=True)
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    # --- W4A8 affine GEMM sweep (activation kernel + GEMM per call), M x (N, K) ---
+    for n, k in ((12288, 4096), (4096, 4096), (16384, 4096), (4096, 16384)):
+        w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+        qw, sc, z = ops.quantize_affine_w4_weight(w, 128, 256)
+        zt = ops.prepare_affine_zeros(z, 128)
+        del w
+        for m in (256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536):
+            x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+            ms = timed(lambda: ops.w4a8_affine_linear(x, qw, sc, z, None, 128, 256, zeros_prepared=zt), args.steps)
+            emit({"case": "w4a8_affine_linear", "M": m, "N": n, "K": k, "ms": ms,
+                  "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12, "frac_of_int8_peak": 2.0 * m * n * k / (ms / 1e3) / 1e12 / int8_peak})
+            del x
+        torch.cuda.empty_cache()
+    # --- activation rotation + int8 quantization at large M (HBM-bound) ---
+    for m in (4096, 32768, 65536):
+        k = 3072
+        x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+        ms = timed(lambda: ops.rotquant(x, 256, _lib.CQ_ACT_INT8_ROW, group_sums=True, kperm=True), args.steps)
+        byts = m * k * 2 + m * k + m * 4 + m * 2 * 64 * ((k // 128 + 31) // 32)
+        emit({"case": "rotquant_int8_convrot256", "M": m, "K": k, "ms": ms, "gbs": byts / (ms / 1e3) / 1e9,
+              "frac_of_hbm": byts / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        del x
+    # --- W4A4 ConvRot linears (BASELINE config 2): rotation groups and the SwiGLU prologue ---
+    m, k, n = 4096, 3072, 12288
+    w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+    x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+    for rot in (256, 64, 16):
+        qw, sw = ops.quantize_convrot_w4a4_weight(w, rot)
+        ms = timed(lambda: ops.convrot_w4a4_linear(x, qw, sw, None, convrot_groupsize=rot), args.steps)
+        emit({"case": "convrot_w4a4_linear", "M": m, "N": n, "K": k, "rot": rot, "ms": ms,
+              "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12})
+    kd, nd = 6144, 3072   # down projection after SwiGLU: h [M, 2*6144] -> silu(g)*u -> [M, 6144] @ W^T
+    wd = torch.randn(nd, kd, generator=gen, device=dev) * 0.02
+    qd, sd = ops.quantize_convrot_w4a4_weight(wd, 256)
+    h = torch.randn(m, 2 * kd, generator=gen, device=dev).to(torch.bfloat16)
+    ms = timed(lambda: ops.convrot_w4a4_linear(h, qd, sd, None, convrot_groupsize=256, input_act="swiglu"), args.steps)
+    emit({"case": "convrot_w4a4_linear_swiglu_prologue", "M": m, "N": nd, "K": kd, "rot": 256, "ms": ms,
+          "tops": 2.0 * m * nd * kd / (ms / 1e3) / 1e12})
+    if _lib.take_device_status() != (0, 0):
+        raise RuntimeError("device status set")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit"], default="w4a8")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit", "sweep"], default="w4a8")
     ap.add_argument("--mode", choices=["dp", "tp", "tp_fused"], default="dp")
     ap.add_argument("--mmdit-blocks", type=int, default=60)
     ap.add_argument("--no-reference-check", action="store_true")
@@ -574,6 +648,8 @@ def main():
             run_reference(args, world, rank)
         elif args.workload == "mmdit":
             run_mmdit(args, world, rank, local)
+        elif args.workload == "sweep":
+            run_sweep(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -107,6 +107,21 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// Tile order.  Tiles are visited in groups of up to kRasterGroup token tiles: inside a group the token tile varies
+// fastest and the weight tile next, so one wave of CTAs (consecutive tile indices) covers a few token tiles by many
+// weight tiles.  Both operands of a wave then stay in L2, where a plain token-fastest order would stream a
+// different activation tile into every CTA of the wave and re-read all activations from HBM for every weight
+// tile once they outgrow L2.
+constexpr int kRasterGroup = 8;
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int per_group = kRasterGroup * n_tiles;
+  const int g = tile / per_group;
+  const int t = tile - g * per_group;
+  const int rows = min(kRasterGroup, m_tiles - g * kRasterGroup);   // token tiles in this (possibly last) group
+  mt = g * kRasterGroup + t % rows;
+  nt = t / rows;
+}
+
 // 8 packed bytes (16 nibbles, low nibble = even column) -> 16 bytes holding 16*v per column.
 //   KPERM: the activations' K order inside each 8-column block is 0,2,4,6,1,3,5,7, so the low nibbles of a
 //          word (even columns) and its high nibbles (odd columns) are already in place.
@@ -192,8 +207,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile % m_tiles) * kBT;
-        const int n0 = (tile / m_tiles) * kBW;
+        int mt, nt;
+        tile_coords(tile, m_tiles, n_tiles, mt, nt);
+        const int m0 = mt * kBT;
+        const int n0 = nt * kBW;
         if (EPI == EPI_AFFINE) {
           // zero-point operand: the tokens' split group sums (bf16, 64 columns per block) into the X slot
           for (int p = 0; p < args.nz; ++p) {
@@ -315,7 +332,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // stage carries the activation-side operand.
           if (warp == 2 + 2 * pair && lane == 0) {
             mbar_arrive_expect_tx(&zt_full[pair], kWuBytes);
-            tma_load_2d(dst, &tm_z, &zt_full[pair], 128 * b, (tile / m_tiles) * kBW);
+            int mt, nt;
+            tile_coords(tile, m_tiles, n_tiles, mt, nt);
+            tma_load_2d(dst, &tm_z, &zt_full[pair], 128 * b, nt * kBW);
           }
           if (!mbar_wait(&zt_full[pair], zphase, abort_flag, 16)) break;
           zphase ^= 1u;
@@ -360,8 +379,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
     }
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile % m_tiles) * kBT + half * 128;
-      const int n = (tile / m_tiles) * kBW + quad * 32 + lane;
+      int mt, nt;
+      tile_coords(tile, m_tiles, n_tiles, mt, nt);
+      const int m0 = mt * kBT + half * 128;
+      const int n = nt * kBW + quad * 32 + lane;
       const bool n_ok = n < N;
       const bool m_full = m0 + 128 <= M;     // every token of this half-tile exists: no per-element checks
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
@@ -444,7 +465,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // and columns past N are clipped by the tensor map.
           unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOutStage + e * P::kOutWarpBytes);
           const uint32_t ost_lane = smem_u32(ost) + 2u * lane;
-          const int x0 = (tile / m_tiles) * kBW + quad * 32;
+          const int x0 = nt * kBW + quad * 32;
 #pragma unroll
           for (int pass = 0; pass < 2; ++pass) {
             if (lane == 0) bulk_wait_group_read0();   // the previous store has finished reading the buffer
