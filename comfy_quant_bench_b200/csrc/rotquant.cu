@@ -330,6 +330,347 @@ __global__ void __launch_bounds__(1024) rotquant_kernel(const RotQuantArgs args)
     }  }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Per-token int8 activations (the W4A8 / W8A8 activation kernel): two rows per CTA, packed f32x2 arithmetic.
+//
+// A CTA of W warps ("team") owns rows 2b and 2b+1.  Every register holds a float2 (row A value, row B value) of
+// the same column, so each butterfly, scale multiply and rounding step is one f32x2 instruction for two tokens,
+// with exactly the per-element rounding of the scalar kernel above (same operations, same order).  Warp w of the
+// team owns the 512-column chunks j = w, w + W, w + 2W; lane (h, c) holds columns 512j + 256h + 16c + [0, 16).
+//   * strides 1 and 4 run in registers; the lane's 16 float2 then go through a padded shared-memory tile (row
+//     stride 144 B: conflict-free 16-byte writes and 8-byte reads, immediate offsets only) so that lane (h, c)
+//     holds columns 512j + 256h + 16t + c, t = 0..15, for strides 16 and 64;
+//   * the codes are formed in that layout: fp32(q * (1 / scale)) + 1.5 * 2^23 (round to nearest even) leaves
+//     the int8 code in the low byte; the two tokens' bytes go to a shared staging block as one 16-bit store at
+//     the column's (K-permuted) position, and each lane reads back 16 contiguous columns of both rows (row
+//     stride 48 B: conflict-free 16-byte reads), splits them with one byte permute per word and stores 16 bytes
+//     a row;
+//   * the absolute maximum propagates NaN, so a token with a NaN or infinite value is seen before rounding and
+//     takes the scalar kernel's semantics (NaN ignored by the maximum, NaN products give code 0).
+// Group sums for the affine GEMM come from dp4a over the stored words and three xor-shuffles.
+// Instructions: about 13 thread-instructions per element, against 28 for the scalar kernel (ncu counters).
+namespace act8 {
+constexpr int kMaxPasses = 3;           // 512-column chunks per warp: 48 float2 registers per lane
+constexpr int kTileRow = 144;           // bytes per transpose-tile row (16 float2 + 16 B pad)
+constexpr int kTileBytes = 32 * kTileRow;
+constexpr int kStageRow = 48;           // bytes per staged 16-column chunk (32 B of codes + 16 B pad)
+constexpr int kStageBlock = 16 * kStageRow + 32;   // second 256-column block: banks shifted by 8
+constexpr int kMaxTeamWarps = 16;
+constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+}  // namespace act8
+
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+__device__ __forceinline__ void h4r_butterfly2(float2& x0, float2& x1, float2& x2, float2& x3) {
+  const float2 hs = f2_mul(make_float2(0.5f, 0.5f), f2_add(f2_add(f2_add(x0, x1), x2), x3));
+  const float2 y0 = f2_sub(hs, x3), y1 = f2_sub(hs, x2), y2 = f2_sub(hs, x1), y3 = f2_sub(hs, x0);
+  x0 = y0; x1 = y1; x2 = y2; x3 = y3;
+}
+
+// strides 1 and 4 on the 16 register columns of a lane
+__device__ __forceinline__ void stages_1_4_x2(float2 (&v)[16]) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a) h4r_butterfly2(v[4 * a + 0], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3]);
+#pragma unroll
+  for (int d = 0; d < 4; ++d) h4r_butterfly2(v[d], v[d + 4], v[d + 8], v[d + 12]);
+}
+
+// Lane (h, c) holds columns 16c + i (i = 0..15) of block h on entry and columns 16t + c (t = 0..15) on exit;
+// then stride 16 (t digit 0) and, for ROT 256, stride 64 (t digit 1).
+template <int ROT>
+__device__ __forceinline__ void stages_cross_x2(float2 (&v)[16], unsigned char* tile, int lane) {
+  unsigned char* wr = tile + lane * act8::kTileRow;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<float4*>(wr + 16 * k) = make_float4(v[2 * k].x, v[2 * k].y, v[2 * k + 1].x, v[2 * k + 1].y);
+  __syncwarp();
+  const unsigned char* rd = tile + (lane >> 4) * 16 * act8::kTileRow + (lane & 15) * 8;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) v[t] = *reinterpret_cast<const float2*>(rd + t * act8::kTileRow);
+  __syncwarp();
+#pragma unroll
+  for (int a = 0; a < 4; ++a) h4r_butterfly2(v[4 * a + 0], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3]);
+  if (ROT == 256) {
+#pragma unroll
+    for (int d = 0; d < 4; ++d) h4r_butterfly2(v[d], v[d + 4], v[d + 8], v[d + 12]);
+  }
+}
+
+// low bytes of four words, in order
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return prmt(prmt(a, b, 0x0040u), prmt(c, d, 0x0040u), 0x5410u);
+}
+
+// One lane's 16 stored columns (512j + 256h + 16c + [0, 16)) of both rows: codes, group sums.
+__device__ __forceinline__ void act8_emit(const RotQuantArgs& args, int64_t rA, bool storeB, int j, int lane,
+                                          bool valid, const uint32_t (&wa)[4], const uint32_t (&wb)[4]) {
+  const int K = args.K;
+  const int e0 = 512 * j + 16 * lane;          // 256h + 16c == 16 * lane
+  int8_t* q = static_cast<int8_t*>(args.q);
+  if (valid) {
+    *reinterpret_cast<uint4*>(q + rA * K + e0) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+    if (storeB) *reinterpret_cast<uint4*>(q + (rA + 1) * K + e0) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+  }
+  if (args.rsplit != nullptr) {
+    int sa = 0, sb = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { sa = __dp4a(static_cast<int>(wa[k]), 0x01010101, sa); sb = __dp4a(static_cast<int>(wb[k]), 0x01010101, sb); }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, o);
+      sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    }
+    if (valid && (lane & 7) == 0) {
+      const int g = e0 >> 7, G = K >> 7;
+      __nv_bfloat16* ra = args.rsplit + rA * args.rs_cols;
+      const int ha = (sa >= 0 ? sa : sa - 127) / 128 * 128;   // 128 * floor(sum / 128)
+      ra[g] = __float2bfloat16_rn(static_cast<float>(ha));
+      ra[G + g] = __float2bfloat16_rn(static_cast<float>(sa - ha));
+      if (storeB) {
+        __nv_bfloat16* rb = ra + args.rs_cols;
+        const int hb = (sb >= 0 ? sb : sb - 127) / 128 * 128;
+        rb[g] = __float2bfloat16_rn(static_cast<float>(hb));
+        rb[G + g] = __float2bfloat16_rn(static_cast<float>(sb - hb));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// codes of one float2: round-to-nearest-even integer of the rounded product in the low byte of each word (SAFE:
+// a NaN product, which only a token flagged non-finite can produce, gives code 0).  The product must be rounded
+// to fp32 before the integer rounding (the reference rounds v * (1/s) first): a multiply followed by an add of
+// 1.5 * 2^23 was measured to come out as one fused operation (a product just inside a half-integer then rounds
+// the other way), so the add is written as an fma whose multiplier, 1.0, is a value the compiler cannot see
+// (`one`, computed at run time from the kernel arguments).
+template <bool SAFE>
+__device__ __forceinline__ uint2 act8_code(float2 v, float2 inv, float one) {
+  float2 r = f2_fma(f2_mul(v, inv), make_float2(one, one), make_float2(act8::kRound, act8::kRound));
+  if (SAFE) {
+    if (r.x != r.x) r.x = act8::kRound;
+    if (r.y != r.y) r.y = act8::kRound;
+  }
+  return make_uint2(__float_as_uint(r.x), __float_as_uint(r.y));
+}
+
+template <int ROT, int PASSES, bool SAFE>
+__device__ __forceinline__ void act8_quant_store(const RotQuantArgs& args, float2 (&v)[PASSES][16],
+                                                 float2 inv, int64_t rA, bool storeB, int warp, int nwarps,
+                                                 int nchunks, int lane, unsigned char* tile) {
+  const int K = args.K;
+  const int h = lane >> 4, c = lane & 15;
+  const float one = args.rows_pad > 0 ? 1.0f : 2.0f;   // 1.0 whenever the kernel runs (rows_pad > 0)
+  // K-permuted position of this lane's column inside its 8-column block (0,2,4,6,1,3,5,7 order)
+  const int c7 = c & 7;
+  const int ip = args.kperm ? ((c7 & 1) ? 4 + (c7 >> 1) : (c7 >> 1)) : c7;
+  unsigned char* st_wr = tile + h * act8::kStageBlock + 2 * ((c & 8) + ip);
+  const unsigned char* st_rd = tile + h * act8::kStageBlock + c * act8::kStageRow;
+#pragma unroll
+  for (int s = 0; s < PASSES; ++s) {
+    const int j = warp + s * nwarps;
+    if (j >= nchunks) break;                                   // warp-uniform
+    const bool valid = 512 * j + 256 * h < K;
+    uint32_t wa[4], wb[4];
+    if constexpr (ROT >= 64) {
+      __syncwarp();
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const uint2 b = act8_code<SAFE>(v[s][t], inv, one);
+        const uint32_t pair = prmt(b.x, b.y, 0x0040u);         // byte 0: row A code, byte 1: row B code
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(smem_u32(st_wr + t * act8::kStageRow)), "h"(static_cast<unsigned short>(pair & 0xFFFFu)) : "memory");
+      }
+      __syncwarp();
+      const uint4 lo = *reinterpret_cast<const uint4*>(st_rd);
+      const uint4 hi = *reinterpret_cast<const uint4*>(st_rd + 16);
+      const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        wa[k] = prmt(w[2 * k], w[2 * k + 1], 0x6420u);
+        wb[k] = prmt(w[2 * k], w[2 * k + 1], 0x7531u);
+      }
+    } else {
+      uint32_t ca[16], cb[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) { const uint2 b = act8_code<SAFE>(v[s][i], inv, one); ca[i] = b.x; cb[i] = b.y; }
+      if (args.kperm) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int o = 8 * (k >> 1) + (k & 1);
+          wa[k] = pack_low_bytes(ca[o], ca[o + 2], ca[o + 4], ca[o + 6]);
+          wb[k] = pack_low_bytes(cb[o], cb[o + 2], cb[o + 4], cb[o + 6]);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          wa[k] = pack_low_bytes(ca[4 * k], ca[4 * k + 1], ca[4 * k + 2], ca[4 * k + 3]);
+          wb[k] = pack_low_bytes(cb[4 * k], cb[4 * k + 1], cb[4 * k + 2], cb[4 * k + 3]);
+        }
+      }
+    }
+    act8_emit(args, rA, storeB, j, lane, valid, wa, wb);
+  }
+}
+
+template <int ROT, int PASSES>
+__global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
+  extern __shared__ __align__(16) unsigned char act8_smem[];
+  __shared__ float red[2][act8::kMaxTeamWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int K = args.K;
+  const int nchunks = (K + 511) >> 9;
+  const int64_t rA = 2 * static_cast<int64_t>(blockIdx.x);
+  const bool liveA = rA < args.rows, liveB = rA + 1 < args.rows, storeB = rA + 1 < args.rows_pad;
+  unsigned char* tile = act8_smem + warp * act8::kTileBytes;
+  const int h = lane >> 4;
+
+  float2 v[PASSES][16];
+  const __nv_bfloat16* xa = static_cast<const __nv_bfloat16*>(args.x) + rA * K;
+  const __nv_bfloat16* xb = xa + K;
+#pragma unroll
+  for (int s = 0; s < PASSES; ++s) {
+    const int j = warp + s * nwarps;
+    const int e = 512 * j + 16 * lane;
+    const bool valid = j < nchunks && 512 * j + 256 * h < K;
+    uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
+    if (valid && liveA) { a0 = __ldg(reinterpret_cast<const uint4*>(xa + e)); a1 = __ldg(reinterpret_cast<const uint4*>(xa + e + 8)); }
+    if (valid && liveB) { b0 = __ldg(reinterpret_cast<const uint4*>(xb + e)); b1 = __ldg(reinterpret_cast<const uint4*>(xb + e + 8)); }
+    const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      v[s][2 * k] = make_float2(__uint_as_float(wa[k] << 16), __uint_as_float(wb[k] << 16));
+      v[s][2 * k + 1] = make_float2(__uint_as_float(wa[k] & 0xFFFF0000u), __uint_as_float(wb[k] & 0xFFFF0000u));
+    }
+  }
+
+  if constexpr (ROT >= 16) {
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s) stages_1_4_x2(v[s]);
+  }
+  if constexpr (ROT >= 64) {
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s)
+      if (warp + s * nwarps < nchunks) stages_cross_x2<ROT>(v[s], tile, lane);   // warp-uniform
+  }
+
+  // per-token absolute maximum (NaN-propagating: a NaN or infinity anywhere makes it non-finite)
+  float pa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pb[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four chains per token
+#pragma unroll
+  for (int s = 0; s < PASSES; ++s)
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const int a = (i >> 1) & 3;
+      pa[a] = max3_nan(pa[a], fabsf(v[s][i].x), fabsf(v[s][i + 1].x));
+      pb[a] = max3_nan(pb[a], fabsf(v[s][i].y), fabsf(v[s][i + 1].y));
+    }
+  float ma = max_nan(max3_nan(pa[0], pa[1], pa[2]), pa[3]);
+  float mb = max_nan(max3_nan(pb[0], pb[1], pb[2]), pb[3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ma = max_nan(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+    mb = max_nan(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+  }
+  if (nwarps > 1) {
+    if (lane == 0) { red[0][warp] = ma; red[1][warp] = mb; }
+    __syncthreads();
+    ma = red[0][0]; mb = red[1][0];
+    for (int w = 1; w < nwarps; ++w) { ma = max_nan(ma, red[0][w]); mb = max_nan(mb, red[1][w]); }
+  }
+  const bool finite = ma <= 3.402823466e38f && mb <= 3.402823466e38f;   // false for NaN and infinity
+  if (!finite) {
+    // the scalar kernel's maximum: fmaxf ignores NaN; an infinity gives scale inf and reciprocal 0
+    ma = 0.0f; mb = 0.0f;
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) { ma = fmaxf(ma, fabsf(v[s][i].x)); mb = fmaxf(mb, fabsf(v[s][i].y)); }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+      mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    }
+    if (nwarps > 1) {
+      __syncthreads();                              // every warp has read red[] above
+      if (lane == 0) { red[0][warp] = ma; red[1][warp] = mb; }
+      __syncthreads();
+      ma = red[0][0]; mb = red[1][0];
+      for (int w = 1; w < nwarps; ++w) { ma = fmaxf(ma, red[0][w]); mb = fmaxf(mb, red[1][w]); }
+    }
+  }
+  const float sa = fmaxf(__fmul_rn(ma, 1.0f / 127.0f), 1e-10f), sb = fmaxf(__fmul_rn(mb, 1.0f / 127.0f), 1e-10f);
+  const float2 inv = make_float2(__frcp_rn(sa), __frcp_rn(sb));
+  if (threadIdx.x == 0) {
+    float* scale = static_cast<float*>(args.scale);
+    scale[rA] = liveA ? sa : 0.0f;
+    if (storeB) scale[rA + 1] = liveB ? sb : 0.0f;
+  }
+  if (args.rsplit != nullptr) {
+    const int G = K >> 7;
+    for (int jj = 2 * G + threadIdx.x; jj < args.rs_cols; jj += blockDim.x) {
+      args.rsplit[rA * args.rs_cols + jj] = __float2bfloat16_rn(0.0f);
+      if (storeB) args.rsplit[(rA + 1) * args.rs_cols + jj] = __float2bfloat16_rn(0.0f);
+    }
+  }
+  if (finite) act8_quant_store<ROT, PASSES, false>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile);
+  else act8_quant_store<ROT, PASSES, true>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile);
+}
+
+template <int ROT>
+static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
+  // Three chunks per warp.  Measured on B200 at K = 3072 and 12288, M = 4096-65536: one or two chunks per warp
+  // (more, smaller warps) were slower or equal, and so was a persistent variant that prefetched the next token
+  // pair into shared memory (cp.async) while working on the current one.
+  constexpr int kPasses = 3;
+  const int nchunks = (a.K + 511) / 512;
+  const int warps = (nchunks + kPasses - 1) / kPasses;
+  const size_t smem = static_cast<size_t>(warps) * act8::kTileBytes;
+  auto k = act8_kernel<ROT, kPasses>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  k<<<static_cast<unsigned>((a.rows_pad + 1) / 2), warps * 32, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+static bool act8_fits(const RotQuantArgs& a) {
+  return a.K % 256 == 0 && (a.K + 511) / 512 <= act8::kMaxPasses * act8::kMaxTeamWarps;
+}
+
 template <typename IN_T, int ROT, bool SWIGLU, int MODE>
 static cudaError_t launch_rq(const RotQuantArgs& a, cudaStream_t st) {
   const int npairs = (a.K + 511) / 512;
@@ -365,7 +706,18 @@ cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantAr
     if (mode == MODE_ACT_INT4_ROW) return launch_rq_rot<__nv_bfloat16, true, MODE_ACT_INT4_ROW>(rot, a, st);
     return launch_rq_rot<__nv_bfloat16, true, MODE_ACT_INT4_GROUP>(rot, a, st);
   }
-  if (mode == MODE_ACT_INT8_ROW) return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT8_ROW>(rot, a, st);
+  if (mode == MODE_ACT_INT8_ROW) {
+    if (a.rows_pad == 0) return cudaSuccess;
+    if (act8_fits(a)) {
+      switch (rot) {
+        case 0: return launch_act8<0>(a, st);
+        case 16: return launch_act8<16>(a, st);
+        case 64: return launch_act8<64>(a, st);
+        default: return launch_act8<256>(a, st);
+      }
+    }
+    return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT8_ROW>(rot, a, st);
+  }
   if (mode == MODE_ACT_INT4_ROW) return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_ROW>(rot, a, st);
   return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_GROUP>(rot, a, st);
 }

@@ -64,7 +64,7 @@ def _check_status():
 # activation rotation + quantization
 # ----------------------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("m,k", [(1, 256), (37, 768), (64, 3072), (5, 16384), (3, 20480)])
+@pytest.mark.parametrize("m,k", [(1, 256), (37, 768), (64, 3072), (256, 3072), (5, 16384), (3, 20480), (2, 32768)])
 @pytest.mark.parametrize("rot", [0, 16, 64, 256])
 def test_rotquant_int8_rowwise_bit_exact(ops, m, k, rot):
     x = ref.synth_activations(m, k, seed=m + k + rot)
@@ -78,6 +78,45 @@ def test_rotquant_int8_rowwise_bit_exact(ops, m, k, rot):
     perm = np.concatenate([np.arange(0, 8, 2), np.arange(1, 8, 2)])
     want = qr.reshape(m, k // 8, 8)[:, :, perm].reshape(m, k).astype(np.int8)
     assert np.array_equal(qp.cpu().numpy(), want)
+    _check_status()
+
+
+@pytest.mark.parametrize("m,m_pad", [(5, 16), (6, 7), (0, 3)])
+def test_rotquant_int8_padding_rows_are_zero(ops, m, m_pad):
+    k = 3072
+    x = ref.synth_activations(max(m, 1), k, seed=11 + m)[:m]
+    q, s, gs = ops.rotquant(bf16_dev(x), 256, 0, m_pad=m_pad, group_sums=True, kperm=True)
+    qr, sr = ref.rotquant(x, 256, "int8") if m else (np.zeros((0, k), np.int16), np.zeros(0, np.float32))
+    perm = np.concatenate([np.arange(0, 8, 2), np.arange(1, 8, 2)])
+    q_np, s_np, g_np = q.cpu().numpy(), s.cpu().numpy(), f32_of(gs)
+    assert np.array_equal(q_np[:m], qr.reshape(m, k // 8, 8)[:, :, perm].reshape(m, k).astype(np.int8))
+    assert np.array_equal(s_np[:m].view(np.uint32), sr.view(np.uint32))
+    assert np.array_equal(g_np[:m], ref.group_sums_split(qr, 128))
+    assert not q_np[m:].any() and not s_np[m:].any() and not g_np[m:].any()
+    _check_status()
+
+
+@pytest.mark.parametrize("k", [1024, 32768])
+def test_rotquant_int8_nonfinite_tokens(ops, k):
+    """A NaN is ignored by the token's maximum and its rotation block quantizes to 0; an infinity gives the token
+    scale inf and all codes 0.  The other token of a two-token CTA is unaffected."""
+    x = ref.synth_activations(4, k, seed=5)
+    nan_bits = np.uint16(0x7FC0)
+    inf_bits = np.uint16(0x7F80)
+    x[1, 600] = nan_bits
+    x[2, 77] = inf_bits
+    q, s, gs = ops.rotquant(bf16_dev(x), 256, 0, group_sums=True)
+    q_np, s_np = q.cpu().numpy(), s.cpu().numpy()
+    clean = x.copy()
+    clean[1, 512:768] = 0           # the NaN's rotation block
+    qr, sr = ref.rotquant(clean, 256, "int8")
+    for r in (0, 1, 3):
+        assert np.array_equal(q_np[r], qr[r].astype(np.int8)), r
+        assert s_np[r].view(np.uint32) == sr[r].view(np.uint32), r
+    assert not q_np[2].any() and np.isposinf(s_np[2])
+    want_codes = qr.copy()
+    want_codes[2] = 0
+    assert np.array_equal(f32_of(gs), ref.group_sums_split(want_codes, 128))
     _check_status()
 
 
