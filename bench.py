@@ -211,7 +211,9 @@ def run_ours(args, world, rank, local):
     from comfy_quant_bench_b200 import ops, _lib
     dev = torch.device("cuda", local)
     m, k, n, rot, desc = WORKLOADS[args.workload]
-    x, x_bits, weights, bias = make_problem(args.workload, seed=rank, dev=dev)
+    # data-parallel replicas draw their own inputs; a column-parallel layer shares one weight and one activation
+    x, x_bits, weights, bias = make_problem(args.workload, seed=0 if args.mode in ("tp", "tp_fused") else rank,
+                                            dev=dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -390,8 +392,14 @@ def run_tp(args, world, rank, local, x, weights, bias):
     mp = (m + 15) // 16 * 16
     gbuf = torch.empty(world * m, nl, dtype=torch.bfloat16, device=dev)
 
+    align = torch.zeros(1, device=dev)
+
     def one_step(ev):
         torch.cuda._sleep(1_000_000)
+        if world > 1:
+            # line the ranks up on the device (outside the events), so that a rank whose host enqueued late does
+            # not count as gather or barrier time on the others
+            dist.all_reduce(align)
         ev[0].record(stream)
         if fused is not None:   # the GEMM writes every rank's output; the barriers are the only synchronization
             out = fused(x)

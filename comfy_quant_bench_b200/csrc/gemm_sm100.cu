@@ -27,6 +27,7 @@
 // int8 weights (W8A8) skip the converters: TMA loads them straight into the operand layout.
 // Every mbarrier wait is bounded (see cq_common.cuh).  No cluster launch, no multicast.
 #include <cstdio>
+#include <type_traits>
 #include <cstring>
 
 #include "kernels.cuh"
@@ -86,6 +87,8 @@ struct GemmArgs {
   int tma_out;           // affine: outputs leave through the TMA store maps (N % 8 == 0, 16-byte aligned out)
   int n_out;             // affine with tma_out: number of output maps (1, or the ranks of a column-parallel layer)
   int out_col0;          // affine with tma_out: column of the output maps where this launch's N columns start
+  int out_w64;           // affine with tma_out: two epilogue warps (adjacent lane quadrants) share one 64-column
+                         // box per pass (128-byte rows) instead of one 32-column box each (N % 64 == 0)
 };
 
 __device__ __forceinline__ void setmaxnreg_dec() {
@@ -157,7 +160,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   uint64_t* tmem_full = empty_conv + kConvStages;
   uint64_t* tmem_empty = tmem_full + 2;
   uint64_t* zt_full = tmem_empty + 2;   // affine: per converter pair, the TMA load of its zero-point operand
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(zt_full + kConvStages);
+  uint64_t* box_free = zt_full + kConvStages;   // affine, 64-column boxes: per epilogue warp pair, staging free
+  uint64_t* box_full = box_free + 4;            //   and both halves of the box written
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(box_full + 4);
+  static_assert((2 * kTmaStages + 3 * kConvStages + 2 + 2 + 8) * 8 + 4 <= P::kSaStage - P::kData,
+                "the barriers and the TMEM address fit the 256-byte region before the scale staging");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -181,6 +188,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 8);
+    }
+    for (int p = 0; p < 4; ++p) {
+      mbar_init(&box_free[p], 1);
+      mbar_init(&box_full[p], 2);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -369,6 +380,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     const float wscale_fold = (BFMT == BF_S8) ? 1.0f : 0.0625f;
     // this warp's 128 token scales for the store phase (read back as broadcast float4 loads)
     float* sa_stage = reinterpret_cast<float*>(smem + P::kSaStage) + e * 128;
+    uint32_t box_pass = 0;                // output store passes so far (phase of this warp pair's box barriers)
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
@@ -460,33 +472,59 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         if (!ok) break;
         stage_sa();
         if (args.tma_out) {
-          // two passes of 64 tokens: bf16 results into this warp's staging buffer ([token][32 columns]), then one
-          // TMA tensor store per pass.  The store drains in the background while the warp moves on; rows past M
-          // and columns past N are clipped by the tensor map.
-          unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOutStage + e * P::kOutWarpBytes);
-          const uint32_t ost_lane = smem_u32(ost) + 2u * lane;
-          const int x0 = nt * kBW + quad * 32;
+          // two passes of 64 tokens: bf16 results into a staging buffer ([token][columns]), then one TMA tensor store
+          // per pass and output buffer.  The store drains in the background while the warp moves on; rows past M
+          // and columns past N are clipped by the tensor map.  With out_w64 the warps of quadrants 2k and 2k+1 (same
+          // token half) fill the two halves of a 64-column box in their joint 8 KB buffer, synchronized by a named
+          // barrier, and the even warp issues the stores: each box row is 128 contiguous bytes, which a remote
+          // (NVLink) write moves more efficiently than 64-byte rows.
+          auto store_passes = [&](auto row_bytes_c) -> bool {
+            constexpr uint32_t kRow = decltype(row_bytes_c)::value;
+            constexpr bool kPair = kRow == 128;
+            const int owner = kPair ? (e & ~1) : e;
+            unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOutStage + owner * P::kOutWarpBytes);
+            const uint32_t ost_lane = smem_u32(ost) + (kPair ? 64u * (e & 1) : 0u) + 2u * lane;
+            const bool issuer = !kPair || (e & 1) == 0;
+            const int x0 = nt * kBW + (kPair ? (quad & 2) : quad) * 32;
+            const int pr = e >> 1;
 #pragma unroll
-          for (int pass = 0; pass < 2; ++pass) {
-            if (lane == 0) bulk_wait_group_read0();   // the previous store has finished reading the buffer
-            __syncwarp();
+            for (int pass = 0; pass < 2; ++pass, ++box_pass) {
+              const uint32_t par = box_pass & 1u;
+              if (issuer) {
+                if (lane == 0) {
+                  bulk_wait_group_read0();            // the previous store has finished reading the buffer
+                  if (kPair) mbar_arrive(&box_free[pr]);
+                }
+                __syncwarp();
+              } else if (!mbar_wait(&box_free[pr], par, abort_flag, 17)) {
+                return false;
+              }
 #pragma unroll
-            for (int j4 = 0; j4 < 16; ++j4) {
-              const int t = 64 * pass + 4 * j4;
-              const float4 c = *reinterpret_cast<const float4*>(sa_stage + t);
-              const float v0 = __fmaf_rn(acc[t / 2].x, c.x, bias), v1 = __fmaf_rn(acc[t / 2].y, c.y, bias);
-              const float v2 = __fmaf_rn(acc[t / 2 + 1].x, c.z, bias), v3 = __fmaf_rn(acc[t / 2 + 1].y, c.w, bias);
-              sts_bf16_pair(ost_lane + (4 * j4) * 64u, ost_lane + (4 * j4 + 1) * 64u, v0, v1);
-              sts_bf16_pair(ost_lane + (4 * j4 + 2) * 64u, ost_lane + (4 * j4 + 3) * 64u, v2, v3);
+              for (int j4 = 0; j4 < 16; ++j4) {
+                const int t = 64 * pass + 4 * j4;
+                const float4 c = *reinterpret_cast<const float4*>(sa_stage + t);
+                const float v0 = __fmaf_rn(acc[t / 2].x, c.x, bias), v1 = __fmaf_rn(acc[t / 2].y, c.y, bias);
+                const float v2 = __fmaf_rn(acc[t / 2 + 1].x, c.z, bias), v3 = __fmaf_rn(acc[t / 2 + 1].y, c.w, bias);
+                sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v0, v1);
+                sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v2, v3);
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (kPair && lane == 0) mbar_arrive(&box_full[pr]);
+              if (issuer && lane == 0) {
+                if (kPair && !mbar_wait(&box_full[pr], par, abort_flag, 18)) return false;
+                if (x0 < N && m0 + 64 * pass < M) {   // boxes wholly past the edge are not issued
+                  // one store per output buffer (column-parallel layers: this rank's columns into every rank's output)
+                  for (int i = 0; i < args.n_out; ++i) tma_store_2d(&tm_out.m[i], ost, args.out_col0 + x0, m0 + 64 * pass);
+                  bulk_commit_group();
+                }
+              }
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0 && x0 < N && m0 + 64 * pass < M) {   // boxes wholly past the edge are not issued
-              // one store per output buffer (column-parallel layers: this rank's columns into every rank's output)
-              for (int i = 0; i < args.n_out; ++i) tma_store_2d(&tm_out.m[i], ost, args.out_col0 + x0, m0 + 64 * pass);
-              bulk_commit_group();
-            }
-          }
+            return true;
+          };
+          const bool stored = args.out_w64 ? store_passes(std::integral_constant<uint32_t, 128>{})
+                                           : store_passes(std::integral_constant<uint32_t, 64>{});
+          if (!__all_sync(0xffffffffu, stored)) { ok = false; break; }
         } else if (n_ok) {
           // column n of the output for tokens m0..m0+127: one pointer walked down the rows
           __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
@@ -682,15 +720,19 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
   ga.n_out = 0;
   ga.out_col0 = 0;
   std::memset(&tm_out, 0, sizeof(tm_out));
-  // box = one store pass of an epilogue warp: 32 columns x 64 tokens (its 4 KB staging buffer)
+  // box = one store pass: 64 tokens x 32 columns (one epilogue warp).  Column-parallel launches, whose boxes also
+  // cross NVLink, use 64 x 64 boxes (128-byte rows, two epilogue warps) when their N is a multiple of 64 (a box
+  // never reaches into another rank's columns).  Measured for the local output: the pairing costs ~10 %.
+  ga.out_w64 = (outs != nullptr && args.N % 64 == 0) ? 1 : 0;
+  const int box_cols = ga.out_w64 ? 64 : 32;
   if (EPI == EPI_AFFINE && outs != nullptr) {
     for (int i = 0; i < outs->n; ++i)
-      if (!make_map_bf16(&tm_out.m[i], outs->ptrs[i], args.M, outs->ldo, 32, 64)) return CQ_ERR_CUDA;
+      if (!make_map_bf16(&tm_out.m[i], outs->ptrs[i], args.M, outs->ldo, box_cols, 64)) return CQ_ERR_CUDA;
     ga.tma_out = 1;
     ga.n_out = outs->n;
     ga.out_col0 = outs->col0;
   } else if (EPI == EPI_AFFINE && args.N % 8 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0) {
-    if (!make_map_bf16(&tm_out.m[0], args.out, args.M, args.N, 32, 64)) return CQ_ERR_CUDA;
+    if (!make_map_bf16(&tm_out.m[0], args.out, args.M, args.N, box_cols, 64)) return CQ_ERR_CUDA;
     ga.tma_out = 1;
     ga.n_out = 1;
   }

@@ -428,7 +428,9 @@ def test_errors_raise(ops):
                                 torch.ones(8, device="cuda"), linear_dtype="fp8")
 
 
-@pytest.mark.parametrize("m,n,k,col0,ldo", [(300, 256, 1024, 256, 768), (1000, 640, 3072, 0, 1280)])
+# n % 64 == 0: 64-column boxes shared by two epilogue warps; n = 96: 32-column boxes (one warp each)
+@pytest.mark.parametrize("m,n,k,col0,ldo", [(300, 256, 1024, 256, 768), (1000, 640, 3072, 0, 1280),
+                                            (130, 96, 1024, 32, 256), (77, 128, 512, 40, 256)])
 def test_affine_linear_into_several_buffers_at_an_offset(ops, m, n, k, col0, ldo):
     """The column-parallel form writes this shard's columns into every output buffer at col0; the rest stays."""
     x = bf16_dev(ref.synth_activations(m, k, seed=11))
