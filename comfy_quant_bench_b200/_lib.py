@@ -39,6 +39,7 @@ CQ_B_INT8 = 1
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _vp = ctypes.c_void_p
+_f32 = ctypes.c_float
 
 # name -> (restype, argtypes), one line per declaration of include/cq_b200.h
 SIGNATURES = {
@@ -62,6 +63,10 @@ SIGNATURES = {
                                     _int, _vp]),
     "cq_linear_w4a8_affine_peers": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _int,
                                            _i64, _i64, _vp, _i64, _vp]),
+    "cq_rotquant_lnmod": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _f32, _i64, _int, _vp, _vp, _vp, _vp]),
+    "cq_linear_w4a8_affine_lnmod": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _f32, _vp, _vp, _vp, _int, _vp,
+                                           _vp, _vp, _i64, _vp]),
+    "cq_qkv_rmsnorm_rope": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
 }
 
 

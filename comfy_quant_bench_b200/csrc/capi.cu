@@ -27,6 +27,7 @@ bool valid_rot(int r) { return r == 0 || r == 16 || r == 64 || r == 256; }
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
 constexpr int64_t kMaxK = 32768;
+constexpr int64_t kMaxLnModK = 24576;   // the two-token activation kernel: 16 warps x 3 chunks x 512 columns
 constexpr int64_t kMaxRows = 0x7FFFFFFF;
 
 }  // namespace
@@ -95,6 +96,45 @@ int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, 
                      (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
                      static_cast<__nv_bfloat16*>(group_sums), cq::rsplit_cols(static_cast<int>(K))};
   return cuda_status(cq::launch_act_rotquant(rot_group, swiglu != 0, mode, a, static_cast<cudaStream_t>(stream)));
+}
+
+int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
+                      float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream) {
+  if (M < 0 || M_pad < M || M_pad > kMaxRows) return CQ_ERR_SHAPE;
+  if (K < 256 || K % 256 != 0 || K > kMaxLnModK) return CQ_ERR_SHAPE;
+  if (!valid_rot(rot_group)) return CQ_ERR_ARG;
+  if (flags & ~CQ_Q_KPERM) return CQ_ERR_ARG;
+  if (!(eps >= 0.0f)) return CQ_ERR_ARG;
+  if (M_pad == 0) return CQ_OK;
+  if ((M > 0 && x == nullptr) || q == nullptr || scale == nullptr || shift == nullptr || scale1p == nullptr)
+    return CQ_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(group_sums, 16) || !aligned(shift, 16) ||
+      !aligned(scale1p, 16))
+    return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), 0, 0, (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
+                     static_cast<__nv_bfloat16*>(group_sums), cq::rsplit_cols(static_cast<int>(K)),
+                     static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale1p), eps};
+  return cuda_status(cq::launch_act_rotquant(rot_group, false, CQ_ACT_INT8_ROW, a, static_cast<cudaStream_t>(stream)));
+}
+
+int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm, float eps,
+                        const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0, void* stream) {
+  if (S < 0 || S > kMaxRows || H < 1 || H > 4096 || (D != 64 && D != 128)) return CQ_ERR_SHAPE;
+  if (s0 < 0 || s_all < s0 + S || s_all > kMaxRows) return CQ_ERR_SHAPE;
+  if (!(eps >= 0.0f)) return CQ_ERR_ARG;
+  if (S == 0) return CQ_OK;
+  if (y == nullptr || q_norm == nullptr || k_norm == nullptr || rope == nullptr || q == nullptr || k == nullptr ||
+      v == nullptr)
+    return CQ_ERR_ARG;
+  if (!aligned(y, 8) || !aligned(q, 8) || !aligned(k, 8) || !aligned(v, 8) || !aligned(rope, 8) ||
+      !aligned(q_norm, 8) || !aligned(k_norm, 8))
+    return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::QkvRopeArgs a{static_cast<const __nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(q_norm),
+                    static_cast<const __nv_bfloat16*>(k_norm), rope, static_cast<__nv_bfloat16*>(q),
+                    static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), S, s_all, s0, H, D, eps};
+  return cuda_status(cq::launch_qkv_rmsnorm_rope(a, static_cast<cudaStream_t>(stream)));
 }
 
 int cq_weight_rotquant(const void* w, int w_is_bf16, int64_t N, int64_t K, int rot_group, int mode, int group,
@@ -258,6 +298,19 @@ int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int ro
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
   if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
                           stream))
+    return e;
+  return cq_gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, out, M, N, K, group, stream);
+}
+
+int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
+                                const void* scale1p, float eps, const void* qweight, const void* s_bf16,
+                                const void* zt_bf16, int group, const void* bias, void* out, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
+  if (M == 0) return CQ_OK;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  if (int e = cq_rotquant_lnmod(x, M, K, rot_group, shift, scale1p, eps, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
+                                stream))
     return e;
   return cq_gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, out, M, N, K, group, stream);
 }

@@ -1,0 +1,82 @@
+// DiT-step glue kernels, sm_100a: the work between the quantized linears of a dual-stream MMDiT block that would
+// otherwise run as several torch kernels with bf16 round trips through HBM.
+//
+// qkv_rmsnorm_rope_kernel: one token's QKV linear output y [3, H, D] (bf16) ->
+//   q = rope(rmsnorm(y[0]) * w_q), k = rope(rmsnorm(y[1]) * w_k), v = y[2], each written at token s0 + s of the
+//   joint attention layout [H, S_all, D] (batch 1).  RMSNorm per head in fp32 (x * rsqrt(mean(x^2) + eps) * w,
+//   rounded once to bf16, as torch's fused rms_norm does); the rotary rotation acts on interleaved pairs
+//   (x[2p], x[2p+1]) with (cos, sin) of the token's position, in fp32 on the bf16 normalized values, rounded to
+//   bf16.  It replaces, per stream and block, rms_norm + float copy + complex multiply + bf16 copy + the
+//   transposing copies of q, k and v.
+#include "kernels.cuh"
+
+namespace cq {
+
+template <int D>
+__global__ void __launch_bounds__(256) qkv_rmsnorm_rope_kernel(const QkvRopeArgs a) {
+  constexpr int E = D / 32;                       // elements per lane: 2 or 4 (whole rotary pairs)
+  static_assert(E == 2 || E == 4, "head dim 64 or 128");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int64_t s = blockIdx.x;
+  const int part = blockIdx.y;                    // 0: q, 1: k, 2: v
+  const int H = a.H;
+  const __nv_bfloat16* src = a.y + (s * 3 + part) * static_cast<int64_t>(H) * D + lane * E;
+  __nv_bfloat16* dst = (part == 0 ? a.q : part == 1 ? a.k : a.v) + (a.s0 + s) * D + lane * E;
+  const int64_t head_stride = a.s_all * D;
+
+  float w[E], cs[E / 2], sn[E / 2];
+  if (part < 2) {
+    const __nv_bfloat16* wp = (part == 0 ? a.qw : a.kw) + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) w[i] = __bfloat162float(wp[i]);
+    const float* rp = a.rope + (s * (D / 2) + lane * (E / 2)) * 2;
+#pragma unroll
+    for (int p = 0; p < E / 2; ++p) { cs[p] = rp[2 * p]; sn[p] = rp[2 * p + 1]; }
+  }
+  for (int h = warp; h < H; h += nwarps) {
+    const __nv_bfloat16* xp = src + static_cast<int64_t>(h) * D;
+    uint32_t raw[E / 2];
+    if constexpr (E == 4) {
+      const uint2 r = *reinterpret_cast<const uint2*>(xp);
+      raw[0] = r.x; raw[1] = r.y;
+    } else {
+      raw[0] = *reinterpret_cast<const uint32_t*>(xp);
+    }
+    __nv_bfloat16* op = dst + h * head_stride;
+    if (part == 2) {
+      if constexpr (E == 4) *reinterpret_cast<uint2*>(op) = make_uint2(raw[0], raw[1]);
+      else *reinterpret_cast<uint32_t*>(op) = raw[0];
+      continue;
+    }
+    float x[E];
+#pragma unroll
+    for (int p = 0; p < E / 2; ++p) { x[2 * p] = bf16_bits_to_f32(raw[p] & 0xFFFFu); x[2 * p + 1] = bf16_bits_to_f32(raw[p] >> 16); }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / static_cast<float>(D) + a.eps);
+    uint32_t out[E / 2];
+#pragma unroll
+    for (int p = 0; p < E / 2; ++p) {
+      const float x0 = bf16_round(x[2 * p] * r * w[2 * p]), x1 = bf16_round(x[2 * p + 1] * r * w[2 * p + 1]);
+      const float y0 = x0 * cs[p] - x1 * sn[p], y1 = x0 * sn[p] + x1 * cs[p];
+      const __nv_bfloat162 b = __floats2bfloat162_rn(y0, y1);
+      out[p] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    if constexpr (E == 4) *reinterpret_cast<uint2*>(op) = make_uint2(out[0], out[1]);
+    else *reinterpret_cast<uint32_t*>(op) = out[0];
+  }
+}
+
+cudaError_t launch_qkv_rmsnorm_rope(const QkvRopeArgs& a, cudaStream_t st) {
+  if (a.S == 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>(a.S), 3);
+  const int threads = 32 * (a.H < 8 ? a.H : 8);
+  if (a.D == 128) qkv_rmsnorm_rope_kernel<128><<<grid, threads, 0, st>>>(a);
+  else qkv_rmsnorm_rope_kernel<64><<<grid, threads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace cq

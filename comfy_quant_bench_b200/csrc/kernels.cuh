@@ -19,10 +19,30 @@ struct RotQuantArgs {
   __nv_bfloat16* rsplit;  // bf16 [rows_pad, rs_cols] or null: per-token code sums over 128-wide K groups, split
                           // exactly into hi = 128*floor(R/128) (columns [0, G)) and lo = R - hi (columns [G, 2G))
   int rs_cols;            // 64 * ceil(G / 32), G = K / 128; columns [2G, rs_cols) are zero
+  // per-token int8 activations only: if ln_shift is set, the kernel quantizes the modulated layer norm
+  // bf16(ln_shift + bf16((x - mean) * rsqrt(var + ln_eps)) * ln_scale1p) instead of x (bf16 [K] vectors)
+  const __nv_bfloat16* ln_shift;
+  const __nv_bfloat16* ln_scale1p;
+  float ln_eps;
 };
 
 // columns of the split group-sum array for a K (the affine GEMM's zero-point operand)
 __host__ __device__ constexpr int rsplit_cols(int K) { return 64 * ((K / 128 + 31) / 32); }
+
+// DiT glue: per-head RMSNorm + rotary embedding of q and k, and the joint-attention layout of q, k, v
+struct QkvRopeArgs {
+  const __nv_bfloat16* y;     // [S, 3, H, D]: one stream's QKV linear output
+  const __nv_bfloat16* qw;    // [D] RMSNorm weight of q
+  const __nv_bfloat16* kw;    // [D] RMSNorm weight of k
+  const float* rope;          // [S, D/2, 2]: (cos, sin) of each token's position
+  __nv_bfloat16* q;           // [H, s_all, D]
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  int64_t S, s_all, s0;       // tokens of this stream, tokens of the joint sequence, this stream's first token
+  int H, D;
+  float eps;
+};
+cudaError_t launch_qkv_rmsnorm_rope(const QkvRopeArgs& a, cudaStream_t st);
 
 cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_weight_rotquant(int rot, bool w_bf16, int mode, const RotQuantArgs& a, cudaStream_t st);

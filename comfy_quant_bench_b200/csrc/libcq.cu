@@ -2,5 +2,6 @@
 // same module (no relocatable device code needed).
 #include "rotquant.cu"
 #include "gemm_sm100.cu"
+#include "dit.cu"
 #include "capi.cu"
 #include "noalloc.cu"

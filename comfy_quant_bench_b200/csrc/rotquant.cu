@@ -548,10 +548,34 @@ __device__ __forceinline__ void act8_quant_store(const RotQuantArgs& args, float
   }
 }
 
-template <int ROT, int PASSES>
+// Sum of both tokens' values over the team: warp shuffles, then one slot per warp in `slots` (2 x kMaxTeamWarps
+// floats) and a CTA barrier.  `slots` must not be read by any warp still using it from an earlier call.
+__device__ __forceinline__ float2 act8_team_sum(float2 t, float* slots, int lane, int warp, int nwarps) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    t.x += __shfl_xor_sync(0xffffffffu, t.x, o);
+    t.y += __shfl_xor_sync(0xffffffffu, t.y, o);
+  }
+  if (nwarps > 1) {
+    if (lane == 0) { slots[warp] = t.x; slots[act8::kMaxTeamWarps + warp] = t.y; }
+    __syncthreads();
+    t = make_float2(slots[0], slots[act8::kMaxTeamWarps]);
+    for (int w = 1; w < nwarps; ++w) { t.x += slots[w]; t.y += slots[act8::kMaxTeamWarps + w]; }
+  }
+  return t;
+}
+
+__device__ __forceinline__ float2 bf16x2_round(float2 v) {
+  const __nv_bfloat162 b = __floats2bfloat162_rn(v.x, v.y);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&b);
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+
+template <int ROT, int PASSES, bool LNMOD>
 __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
   extern __shared__ __align__(16) unsigned char act8_smem[];
   __shared__ float red[2][act8::kMaxTeamWarps];
+  __shared__ float red_ln[2][2][act8::kMaxTeamWarps];   // layer-norm prologue: sums, then centered squares
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int K = args.K;
   const int nchunks = (K + 511) >> 9;
@@ -577,6 +601,63 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
     for (int k = 0; k < 8; ++k) {
       v[s][2 * k] = make_float2(__uint_as_float(wa[k] << 16), __uint_as_float(wb[k] << 16));
       v[s][2 * k + 1] = make_float2(__uint_as_float(wa[k] & 0xFFFF0000u), __uint_as_float(wb[k] & 0xFFFF0000u));
+    }
+  }
+
+  if constexpr (LNMOD) {
+    // layer norm over the K columns of each token (two passes over the registers: mean, then centered squares),
+    // rounded to bf16, then the modulation shift + ln * (1 + scale) rounded to bf16 (torch's layer_norm and
+    // addcmul on bf16 tensors); padding tokens and columns past K stay 0
+    const float inv_k = 1.0f / static_cast<float>(K);
+    float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i & 3] = f2_add(acc[i & 3], v[s][i]);
+    float2 sum = act8_team_sum(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), &red_ln[0][0][0], lane, warp,
+                               nwarps);
+    const float2 mean = make_float2(sum.x * inv_k, sum.y * inv_k);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) acc[a] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s) {
+      const int j = warp + s * nwarps;
+      const bool valid = j < nchunks && 512 * j + 256 * h < K;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[s][i] = valid ? f2_sub(v[s][i], mean) : make_float2(0.f, 0.f);
+        acc[i & 3] = f2_fma(v[s][i], v[s][i], acc[i & 3]);
+      }
+    }
+    const float2 ssq = act8_team_sum(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), &red_ln[1][0][0], lane,
+                                     warp, nwarps);
+    const float2 rstd = make_float2(rsqrtf(ssq.x * inv_k + args.ln_eps), rsqrtf(ssq.y * inv_k + args.ln_eps));
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s) {
+      const int j = warp + s * nwarps;
+      const bool valid = j < nchunks && 512 * j + 256 * h < K;
+      const int e = 512 * j + 16 * lane;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        uint4 sh = make_uint4(0, 0, 0, 0), sc = sh;
+        if (valid) {
+          sh = __ldg(reinterpret_cast<const uint4*>(args.ln_shift + e + 8 * k));
+          sc = __ldg(reinterpret_cast<const uint4*>(args.ln_scale1p + e + 8 * k));
+        }
+        const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w}, scw[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+        for (int i2 = 0; i2 < 8; ++i2) {
+          const int i = 8 * k + i2;
+          const uint32_t shb = (i2 & 1) ? (shw[i2 >> 1] & 0xFFFF0000u) : (shw[i2 >> 1] << 16);
+          const uint32_t scb = (i2 & 1) ? (scw[i2 >> 1] & 0xFFFF0000u) : (scw[i2 >> 1] << 16);
+          const float2 ln = bf16x2_round(f2_mul(v[s][i], rstd));
+          float2 xn = bf16x2_round(f2_fma(ln, make_float2(__uint_as_float(scb), __uint_as_float(scb)),
+                                          make_float2(__uint_as_float(shb), __uint_as_float(shb))));
+          if (!valid || !liveA) xn.x = 0.0f;
+          if (!valid || !liveB) xn.y = 0.0f;
+          v[s][i] = xn;
+        }
+      }
     }
   }
 
@@ -652,7 +733,7 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
   else act8_quant_store<ROT, PASSES, true>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile);
 }
 
-template <int ROT>
+template <int ROT, bool LNMOD = false>
 static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   // Three chunks per warp.  Measured on B200 at K = 3072 and 12288, M = 4096-65536: one or two chunks per warp
   // (more, smaller warps) were slower or equal, and so was a persistent variant that prefetched the next token
@@ -661,7 +742,7 @@ static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   const int nchunks = (a.K + 511) / 512;
   const int warps = (nchunks + kPasses - 1) / kPasses;
   const size_t smem = static_cast<size_t>(warps) * act8::kTileBytes;
-  auto k = act8_kernel<ROT, kPasses>;
+  auto k = act8_kernel<ROT, kPasses, LNMOD>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   k<<<static_cast<unsigned>((a.rows_pad + 1) / 2), warps * 32, smem, st>>>(a);
   return cudaGetLastError();
@@ -708,6 +789,15 @@ cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantAr
   }
   if (mode == MODE_ACT_INT8_ROW) {
     if (a.rows_pad == 0) return cudaSuccess;
+    if (a.ln_shift != nullptr) {                    // modulated layer norm prologue (callers check act8_fits)
+      if (!act8_fits(a)) return cudaErrorInvalidValue;
+      switch (rot) {
+        case 0: return launch_act8<0, true>(a, st);
+        case 16: return launch_act8<16, true>(a, st);
+        case 64: return launch_act8<64, true>(a, st);
+        default: return launch_act8<256, true>(a, st);
+      }
+    }
     if (act8_fits(a)) {
       switch (rot) {
         case 0: return launch_act8<0>(a, st);

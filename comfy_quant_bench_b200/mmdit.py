@@ -12,8 +12,10 @@ per-128-group scale/zero, tcgen05 GEMM).  The block follows the usual MMDiT layo
     x     = x + gate1 * Linear_out(attn)
     x     = x + gate2 * Linear_fc2(gelu_tanh(Linear_fc1(LayerNorm(x) * (1 + scale2) + shift2)))
 
-Norms, rotary embedding, GELU and attention are plain torch ops: they are not part of the quantized-linear path
-(fused attention/normalisation kernels are a separate work item).  Weights are drawn N(0, 0.02) per linear from a
+Attention, GELU and the gated residuals are torch ops.  The layer norm + modulation before the QKV and MLP-up
+linears run inside the library's activation kernel (``ops.w4a8_affine_linear_lnmod``) and the q/k RMSNorm + rotary
+embedding + joint attention layout run as one library kernel (``ops.qkv_rmsnorm_rope``); ``fused_glue=False``
+runs them as torch ops instead.  Weights are drawn N(0, 0.02) per linear from a
 seeded generator, quantized on the device with the library's weight kernel, and only the packed form is kept.
 
 ``MMDiT.step(..., reference=True)`` runs the same step with every linear replaced by a torch fp32 product of the
@@ -42,6 +44,8 @@ class MMDiTConfig:
     group_size: int = 128
     convrot_groupsize: int = 256
     quantize_modulation: bool = True   # BASELINE: every linear W4A8; the reference excludes modulation layers
+    fused_glue: bool = True            # kernel path: layer norm + modulation inside the activation kernel of the
+                                       # QKV and MLP-up linears, q/k RMSNorm + rotary + attention layout in one kernel
 
     @property
     def head_dim(self) -> int:
@@ -63,6 +67,12 @@ class QLinear:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return ops.w4a8_affine_linear(x, self.qweight, self.scale, self.zeros, self.bias, self.cfg.group_size,
                                       self.cfg.convrot_groupsize, zeros_prepared=self.zt)
+
+    def lnmod(self, x: torch.Tensor, shift: torch.Tensor, scale1p: torch.Tensor) -> torch.Tensor:
+        """This linear of bf16(shift + bf16(layer_norm(x)) * scale1p), the norm and modulation fused into the
+        activation kernel."""
+        return ops.w4a8_affine_linear_lnmod(x, shift, scale1p, self.qweight, self.scale, self.zt, self.bias,
+                                            self.cfg.group_size, self.cfg.convrot_groupsize, eps=1e-6)
 
     def dequantized_weight(self) -> torch.Tensor:
         """W in the rotated basis, fp32 [N, K]: (q - 8) * scale + zeros per 128-wide group."""
@@ -171,9 +181,12 @@ class MMDiT:
 
         The glue around the linears stays in bf16 (fp32 inside the norms and the rotary rotation): layer norm,
         modulation as one fused multiply-add, q/k/v written straight into the joint [heads, tokens, dim]
-        attention layout, GELU on bf16, gated residual as one fused multiply-add."""
+        attention layout, GELU on bf16, gated residual as one fused multiply-add.  With ``fused_glue`` (kernel path
+        only) the layer norm + modulation run inside the activation kernel of the QKV and MLP-up linears and the
+        q/k RMSNorm + rotary + layout copies are one kernel; the reference path always runs the torch ops."""
         c = self.cfg
         h, nh, d = c.hidden, c.heads, c.head_dim
+        fused = c.fused_glue and not reference
         st_txt, st_img = txt.shape[0], img.shape[0]
         s_all = st_txt + st_img
         temb_act = F.silu(temb.float()).to(torch.bfloat16)
@@ -185,6 +198,10 @@ class MMDiT:
             mt = self._mod(st, temb_act, reference).chunk(6, dim=-1)
             for x, s, m, rot, lo, hi in ((txt, st, mt, self.rope_txt, 0, st_txt),
                                          (img, si, mi, self.rope_img, st_txt, s_all)):
+                if fused:
+                    y = s.qkv.lnmod(x, m[0], 1.0 + m[1])
+                    ops.qkv_rmsnorm_rope(y, s.q_norm, s.k_norm, rot, q, k, v, lo, eps=1e-6)
+                    continue
                 xn = torch.addcmul(m[0], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[1])
                 y = self._lin(s.qkv, xn, reference).view(x.shape[0], 3, nh, d)
                 q[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 0], (d,), s.q_norm, eps=1e-6), rot).transpose(0, 1)
@@ -194,8 +211,11 @@ class MMDiT:
             new = []
             for x, s, m, att in ((txt, st, mt, a[:st_txt]), (img, si, mi, a[st_txt:])):
                 x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
-                xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
-                f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
+                if fused:
+                    f = F.gelu(s.fc1.lnmod(x, m[3], 1.0 + m[4]), approximate="tanh")
+                else:
+                    xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
+                    f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
                 new.append(torch.addcmul(x, m[5], self._lin(s.fc2, f, reference)))
             txt, img = new
         return img, txt

@@ -393,3 +393,85 @@ def gemm_affine(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qweight
     _lib.call("cq_gemm_affine", _ptr(a), int(bool(a_kperm)), _ptr(sa), _ptr(gsplit), _ptr(qweight),
               _ptr(scale.contiguous()), _ptr(zt), _ptr(bias), _ptr(out), m, n, k, 128, _stream(dev))
     return out
+
+
+# ----------------------------------------------------------------------------------------------
+# DiT-step glue: the modulated layer norm fused into the activation kernel, and q/k RMSNorm + rotary
+# embedding + the joint attention layout in one kernel (see cq_rotquant_lnmod / cq_qkv_rmsnorm_rope)
+# ----------------------------------------------------------------------------------------------
+
+def _vec_bf16(v: torch.Tensor, k: int, name: str) -> torch.Tensor:
+    v = v.reshape(-1)
+    if v.numel() != k:
+        raise ValueError(f"{name} must hold {k} values, got {v.numel()}")
+    v = v.to(torch.bfloat16).contiguous()
+    if v.data_ptr() % 16:
+        v = v.clone()
+    return v
+
+
+def rotquant_lnmod(x: torch.Tensor, rot_group: int, shift: torch.Tensor, scale1p: torch.Tensor, *, eps: float = 1e-6,
+                   m_pad: int | None = None, group_sums: bool = False, kperm: bool = False):
+    """Per-token int8 quantization (``rotquant`` mode CQ_ACT_INT8_ROW) of the modulated layer norm
+    bf16(shift + bf16(layer_norm(x)) * scale1p), computed inside the activation kernel.  Returns (q, scale, gsplit)."""
+    dev = _require_cuda(x, shift, scale1p)
+    x2 = _as2d(x)
+    m, k = x2.shape
+    mp = m if m_pad is None else int(m_pad)
+    sh, sc = _vec_bf16(shift, k, "shift"), _vec_bf16(scale1p, k, "scale1p")
+    q = torch.empty(mp, k, dtype=torch.int8, device=dev)
+    scale = torch.empty(mp, dtype=torch.float32, device=dev)
+    gs = torch.empty(mp, int(_lib.load().cq_group_sum_cols(k)), dtype=torch.bfloat16, device=dev) if group_sums else None
+    _lib.call("cq_rotquant_lnmod", _ptr(x2), m, k, _check_rot(rot_group), _ptr(sh), _ptr(sc), float(eps), mp,
+              _lib.CQ_Q_KPERM if kperm else 0, _ptr(q), _ptr(scale), _ptr(gs), _stream(dev))
+    return q, scale, gs
+
+
+def w4a8_affine_linear_lnmod(x: torch.Tensor, shift: torch.Tensor, scale1p: torch.Tensor, qweight: torch.Tensor,
+                             scale: torch.Tensor, zeros_prepared: torch.Tensor, bias: torch.Tensor | None = None,
+                             group_size: int = 128, convrot_groupsize: int = 0, eps: float = 1e-6) -> torch.Tensor:
+    """``w4a8_affine_linear(bf16(shift + bf16(layer_norm(x, eps)) * scale1p), ...)`` with the layer norm and the
+    modulation done inside the activation kernel (no normalized copy of x in HBM).  ``scale1p`` is 1 + scale,
+    rounded to bf16 (as the torch expression ``1 + scale`` on a bf16 tensor gives)."""
+    if group_size != 128:
+        raise ValueError("the W4A8 affine kernel supports group_size 128")
+    k = x.shape[-1]
+    if k != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
+    n = qweight.shape[0]
+    dev = _require_cuda(x, shift, scale1p, qweight, scale, zeros_prepared, bias)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    sh, sc = _vec_bf16(shift, k, "shift"), _vec_bf16(scale1p, k, "scale1p")
+    _lib.call("cq_linear_w4a8_affine_lnmod", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc),
+              float(eps), _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
+              int(group_size), _ptr(_bias_bf16(bias)), _ptr(out), wp, wn, _stream(dev))
+    return out.reshape(*x.shape[:-1], n)
+
+
+def qkv_rmsnorm_rope(y: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, rope: torch.Tensor,
+                     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s0: int, eps: float = 1e-6) -> None:
+    """One stream's QKV output y [S, 3*H*D] (bf16) into the joint attention layout q, k, v [1, H, S_all, D] at
+    tokens [s0, s0 + S): q and k RMS-normalized per head (weights q_norm / k_norm [D]) and rotated by ``rope``
+    ([S, D/2] complex64, or its real view [S, D/2, 2] of (cos, sin)); v copied."""
+    dev = _require_cuda(y, q_norm, k_norm, rope, q, k, v)
+    if q.dim() != 4 or q.shape[0] != 1 or not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("q, k, v must be contiguous [1, H, S_all, D]")
+    _, h, s_all, d = q.shape
+    if k.shape != q.shape or v.shape != q.shape or q.dtype != torch.bfloat16:
+        raise ValueError("q, k, v must be bf16 of one shape")
+    y2 = _as2d(y)
+    s = y2.shape[0]
+    if y2.shape[1] != 3 * h * d:
+        raise ValueError(f"y must be [S, {3 * h * d}]")
+    if rope.is_complex():
+        rope = torch.view_as_real(rope)
+    rope = rope.to(torch.float32).contiguous()
+    if tuple(rope.shape) != (s, d // 2, 2):
+        raise ValueError(f"rope must be [{s}, {d // 2}] complex (or [{s}, {d // 2}, 2] real)")
+    qn, kn = q_norm.to(torch.bfloat16).contiguous(), k_norm.to(torch.bfloat16).contiguous()
+    _lib.call("cq_qkv_rmsnorm_rope", _ptr(y2), s, h, d, _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(q), _ptr(k),
+              _ptr(v), s_all, int(s0), _stream(dev))

@@ -232,6 +232,35 @@ CQ_API int cq_linear_w4a8_affine_noalloc(const void* x, int64_t M, int64_t K, in
                                          const void* qweight, const void* s_bf16, const void* zt_bf16, int group,
                                          const void* bias, void* out, void* stream);
 
+/*
+ * DiT-step glue around the quantized linears of a dual-stream MMDiT block (SD3 / Flux / Qwen-Image layout).
+ * No counterpart in the reference, whose model code runs these steps as torch ops on bf16 tensors
+ * (layer_norm, addcmul, rms_norm, the rotary multiply and the copies into the attention layout).
+ *
+ * cq_rotquant_lnmod: cq_rotquant (per-token int8, CQ_ACT_INT8_ROW) of the modulated layer norm
+ *   xn = bf16( shift + bf16( (x - mean) * rsqrt(var + eps) ) * scale1p )
+ * per token over its K columns (biased variance, no affine), shift and scale1p bf16 [K] (scale1p = 1 + scale,
+ * rounded to bf16 by the caller), computed in fp32 with the two bf16 roundings of the torch ops it replaces.
+ * Writes the same outputs as cq_rotquant (flags: CQ_Q_KPERM only).  K % 256 == 0, K <= 24576.
+ * cq_linear_w4a8_affine_lnmod: cq_linear_w4a8_affine of that xn.
+ *
+ * cq_qkv_rmsnorm_rope: y bf16 [S, 3, H, D] (one stream's QKV linear output, q | k | v) ->
+ *   q[h, s0+s, :] = rope(bf16(rmsnorm(y[s,0,h,:]) * q_norm)),  k likewise with k_norm,  v[h, s0+s, :] = y[s,2,h,:]
+ * with q, k, v bf16 [H, s_all, D] (the joint attention layout, batch 1), rmsnorm(x) = x * rsqrt(mean(x^2) + eps)
+ * in fp32, and rope rotating the interleaved pairs (x[2p], x[2p+1]) by rope[s, p] = (cos, sin) (f32 [S, D/2, 2]),
+ * in fp32, rounded to bf16.  D = 64 or 128.
+ */
+CQ_API int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift,
+                             const void* scale1p, float eps, int64_t M_pad, int flags, void* q, float* scale,
+                             void* group_sums, void* stream);
+CQ_API int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, int rot_group,
+                                       const void* shift, const void* scale1p, float eps, const void* qweight,
+                                       const void* s_bf16, const void* zt_bf16, int group, const void* bias,
+                                       void* out, void* workspace, int64_t workspace_bytes, void* stream);
+CQ_API int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm,
+                               float eps, const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

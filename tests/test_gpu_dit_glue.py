@@ -1,0 +1,127 @@
+"""DiT-step glue kernels against the torch ops they replace (bf16 tensors on the GPU).
+
+* ``qkv_rmsnorm_rope``: per-head RMSNorm of q and k (fp32, one bf16 rounding), rotary rotation of interleaved pairs
+  (fp32, one bf16 rounding), and the joint [1, H, S_all, D] attention layout.  v is a pure copy (bit-exact); q and k
+  may differ from the torch composite by one bf16 rounding where fp32 summation order differs.
+* ``rotquant_lnmod`` / ``w4a8_affine_linear_lnmod``: the modulated layer norm bf16(shift + bf16(LN(x)) * scale1p)
+  formed inside the activation kernel.  Its mean and variance are summed in a different order than torch's Welford
+  kernel, so a normalized value can land one bf16 rounding away; the codes then differ by at most 1 at a few
+  positions and the linear's output agrees to rel-L2 <= 1e-3 (the bounds written below).
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from comfy_quant_bench_b200 import ops as _ops, _lib
+    _lib.load()
+    return _ops
+
+
+def _status_clear():
+    from comfy_quant_bench_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.take_device_status() == (0, 0)
+
+
+def _rope_table(n, d, offset, device):
+    inv = 1.0 / (10000.0 ** (torch.arange(0, d, 2, device=device, dtype=torch.float32) / d))
+    ang = torch.outer(torch.arange(offset, offset + n, device=device, dtype=torch.float32), inv)
+    return torch.complex(torch.cos(ang), torch.sin(ang))
+
+
+def _torch_rope(x, rot):
+    xc = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+    return torch.view_as_real(xc * rot[:, None, :]).reshape(x.shape).to(torch.bfloat16)
+
+
+def _within_one_rounding(got, want):
+    g, w = got.float(), want.float()
+    tol = w.abs() * 2.0 ** -7 + 1e-6
+    assert bool(((g - w).abs() <= tol).all()), float(((g - w).abs() - tol).max())
+    assert float((g != w).float().mean()) <= 0.02
+
+
+@pytest.mark.parametrize("s,h,d,s0,s_all", [(300, 24, 128, 40, 345), (17, 4, 64, 0, 17)])
+def test_qkv_rmsnorm_rope_matches_torch(ops, s, h, d, s0, s_all):
+    g = torch.Generator(device="cuda").manual_seed(s + h)
+    y = torch.randn(s, 3 * h * d, generator=g, device="cuda").to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
+    rot = _rope_table(s, d, s0, "cuda")
+    q, k, v = (torch.full((1, h, s_all, d), 3.0, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    ops.qkv_rmsnorm_rope(y, qn, kn, rot, q, k, v, s0, eps=1e-6)
+    yv = y.view(s, 3, h, d)
+    want_q = _torch_rope(F.rms_norm(yv[:, 0], (d,), qn, eps=1e-6), rot).transpose(0, 1)
+    want_k = _torch_rope(F.rms_norm(yv[:, 1], (d,), kn, eps=1e-6), rot).transpose(0, 1)
+    _status_clear()
+    assert torch.equal(v[0, :, s0:s0 + s], yv[:, 2].transpose(0, 1))
+    _within_one_rounding(q[0, :, s0:s0 + s], want_q)
+    _within_one_rounding(k[0, :, s0:s0 + s], want_k)
+    for t in (q, k, v):   # tokens of the other stream are untouched
+        assert bool((t[0, :, :s0] == 3.0).all()) and bool((t[0, :, s0 + s:] == 3.0).all())
+
+
+def _lnmod_inputs(m, k, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(m, k, generator=g, device="cuda")
+    x[:, torch.randperm(k, generator=g, device="cuda")[: k // 100]] *= 20.0   # outlier channels
+    x = (x + 0.5).to(torch.bfloat16)
+    shift = (0.3 * torch.randn(k, generator=g, device="cuda")).to(torch.bfloat16)
+    scale1p = (1.0 + 0.3 * torch.randn(k, generator=g, device="cuda")).to(torch.bfloat16)
+    return x, shift, scale1p
+
+
+def _torch_lnmod(x, shift, scale1p):
+    return torch.addcmul(shift, F.layer_norm(x, (x.shape[-1],), eps=1e-6), scale1p)
+
+
+@pytest.mark.parametrize("m,k,rot,m_pad", [(300, 3072, 256, 304), (37, 1024, 64, 37), (8, 12288, 256, 16),
+                                           (5, 768, 0, 8)])
+def test_rotquant_lnmod_matches_torch_composite(ops, m, k, rot, m_pad):
+    from comfy_quant_bench_b200 import _lib
+    x, shift, scale1p = _lnmod_inputs(m, k, seed=m + k)
+    q, s, gs = ops.rotquant_lnmod(x, rot, shift, scale1p, m_pad=m_pad, group_sums=True, kperm=True)
+    qr, sr, gr = ops.rotquant(_torch_lnmod(x, shift, scale1p), rot, _lib.CQ_ACT_INT8_ROW, m_pad=m_pad,
+                              group_sums=True, kperm=True)
+    _status_clear()
+    d = (q[:m].int() - qr[:m].int()).abs()
+    assert int(d.max()) <= 1 and float((d > 0).float().mean()) <= 1e-3
+    assert float(((s[:m] - sr[:m]).abs() / sr[:m]).max()) <= 1e-3
+    assert float((gs[:m].float() - gr[:m].float()).abs().max()) <= 128.0   # split sums of codes within +-1
+    assert not q[m:].any() and not s[m:].any() and not gs[m:].float().any()
+
+
+def test_w4a8_affine_linear_lnmod_matches_composite(ops):
+    m, k, n = 257, 3072, 1024
+    x, shift, scale1p = _lnmod_inputs(m, k, seed=3)
+    w = torch.randn(n, k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4)) * 0.02
+    qw, sc, z = ops.quantize_affine_w4_weight(w, 128, 256)
+    zt = ops.prepare_affine_zeros(z, 128)
+    bias = (0.01 * torch.randn(n, device="cuda")).to(torch.bfloat16)
+    got = ops.w4a8_affine_linear_lnmod(x, shift, scale1p, qw, sc, zt, bias, 128, 256)
+    want = ops.w4a8_affine_linear(_torch_lnmod(x, shift, scale1p), qw, sc, z, bias, 128, 256, zeros_prepared=zt)
+    _status_clear()
+    rel = float((got.float() - want.float()).norm() / want.float().norm())
+    assert rel <= 1e-3, rel
+
+
+def test_dit_glue_rejects_bad_arguments(ops):
+    from comfy_quant_bench_b200 import _lib
+    x = torch.zeros(4, 1000, dtype=torch.bfloat16, device="cuda")       # K not a multiple of 256
+    v = torch.zeros(1000, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.CQShapeError):
+        ops.rotquant_lnmod(x, 256, v, v)
+    with pytest.raises(ValueError):
+        ops.rotquant_lnmod(torch.zeros(4, 1024, dtype=torch.bfloat16, device="cuda"), 256, v, v)   # wrong length
+    y = torch.zeros(8, 3 * 2 * 96, dtype=torch.bfloat16, device="cuda")   # head dim 96: not supported
+    q = torch.zeros(1, 2, 8, 96, dtype=torch.bfloat16, device="cuda")
+    w = torch.ones(96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.CQShapeError):
+        ops.qkv_rmsnorm_rope(y, w, w, torch.zeros(8, 48, 2, device="cuda"), q, q.clone(), q.clone(), 0)

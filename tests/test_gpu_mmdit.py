@@ -1,8 +1,9 @@
 """MMDiT denoise step on the W4A8 affine path: the kernel path against the torch fp32 reference of the same step.
 
 The reference replaces every linear by an fp32 product of its dequantized weight (W = (q - 8) * scale + zeros,
-rotated basis) and the dequantized activation codes, with the rest of the block (norms, rotary embedding,
-attention, GELU, modulation) shared.  Each linear's bf16 output agrees to within bf16 rounding, so after a few
+rotated basis) and the dequantized activation codes, and runs the rest of the block (norms, rotary embedding,
+attention, GELU, modulation) as torch ops; the kernel path runs the fused glue kernels (``fused_glue``) or the
+same torch ops.  Each linear's bf16 output agrees to within bf16 rounding, so after a few
 blocks the step outputs agree to a relative L2 error well under 1e-2 (the bound written below).
 """
 import pytest
@@ -19,10 +20,10 @@ def mmdit():
     return mm
 
 
-@pytest.mark.parametrize("quantize_modulation", [True, False])
-def test_mmdit_step_matches_reference(mmdit, quantize_modulation):
+@pytest.mark.parametrize("quantize_modulation,fused_glue", [(True, True), (False, True), (True, False)])
+def test_mmdit_step_matches_reference(mmdit, quantize_modulation, fused_glue):
     cfg = mmdit.MMDiTConfig(blocks=2, hidden=512, heads=4, mlp=1024, img_tokens=300, txt_tokens=40,
-                            quantize_modulation=quantize_modulation)
+                            quantize_modulation=quantize_modulation, fused_glue=fused_glue)
     model = mmdit.MMDiT(cfg, device="cuda", seed=3)
     img, txt, temb = model.inputs(seed=4)
     out_img, out_txt = model.step(img, txt, temb)
