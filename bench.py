@@ -1,7 +1,8 @@
 """Benchmark of the W4A8 quantized linear (BASELINE north-star workload) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload w4a8|w4a4|c1|mmdit|sweep]
-                    [--mode dp|tp]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload w4a8|w4a4|c1|mmdit|wan|sweep]
+                    [--mode dp|tp|tp_fused]
 
 One step = one pass of the hot path over one synthetic batch: activation rotation (ConvRot g256) + per-token
 int8 quantization, then the packed-int4 x int8 tcgen05 GEMM with the per-group affine epilogue, bf16 out.
@@ -19,6 +20,10 @@ and quantizes the full activation, runs its N/P columns, and an NCCL all-gather 
 ``--workload mmdit`` times one denoise step of a Qwen-Image-like 60-block dual-stream MMDiT with every linear on
 the W4A8 affine path (4096 image + 256 text tokens, hidden 3072, MLP 12288; random init; graph-replayed), as
 data-parallel replicas across ranks: value = steps/s over all ranks, ms_per_step = the step latency.
+``--workload wan`` does the same for a Wan-2.2-5B-like 30-block video DiT (27,280 tokens, hidden 3072, FFN 14336)
+whose linears follow the mixed plan: a seeded 35 % ConvRot W4A4 (Hadamard g64), the rest W8A8 int8_tensorwise.
+``--workload sweep`` prints one line per case of the GEMM M sweep, the activation kernel at large M and the W4A4
+rotation-group / SwiGLU cases.
 
 ``--impl reference`` times the reference's CPU path (dequantize-and-matmul, oracle port) on the host cores.
 """
@@ -470,23 +475,62 @@ def run_tp(args, world, rank, local, x, weights, bias):
 
 def run_mmdit(args, world, rank, local):
     """One MMDiT denoise step per replica per iteration, graph-replayed; data-parallel over ranks."""
-    from comfy_quant_bench_b200 import mmdit as mm, _lib
+    from comfy_quant_bench_b200 import mmdit as mm
     dev = torch.device("cuda", local)
     cfg = mm.MMDiTConfig(blocks=args.mmdit_blocks)
     model = mm.MMDiT(cfg, device=dev, seed=0)
     img, txt, temb = model.inputs(seed=1 + rank)
-    stream = torch.cuda.current_stream(dev)
+    launches = 2 * len(model.linears()) + (2 * cfg.blocks if cfg.fused_glue else 0)
+    config = {"workload": "mmdit_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads,
+              "mlp": cfg.mlp, "img_tokens": cfg.img_tokens, "txt_tokens": cfg.txt_tokens, "batch": 1,
+              "linears": "every linear W4A8 affine g128, ConvRot g256 (modulation included)",
+              "glue": "layer norm + modulation fused into the QKV / MLP-up activation kernels, q/k RMSNorm + rotary "
+                      "+ attention layout in one kernel" if cfg.fused_glue else "torch ops"}
+    _run_dit(args, world, rank, local, model, (img, txt, temb), lambda o: o[0], "MMDiT denoise steps/s", config,
+             launches)
+
+
+def run_wan(args, world, rank, local):
+    """One Wan-like video DiT denoise step (mixed W4A4 / W8A8 plan) per replica per iteration, graph-replayed."""
+    from comfy_quant_bench_b200 import wan
+    dev = torch.device("cuda", local)
+    cfg = wan.WanConfig(blocks=args.wan_blocks)
+    model = wan.WanDiT(cfg, device=dev, seed=0)
+    x, ctx = model.inputs(seed=1 + rank)
+    plan = model.plan()
+    config = {"workload": "wan_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads, "ffn": cfg.ffn,
+              "tokens": cfg.tokens, "grid": [cfg.frames, cfg.height, cfg.width], "ctx_tokens": cfg.ctx_tokens,
+              "batch": 1,
+              "linears": f"{plan['w4a4']} ConvRot W4A4 (Hadamard g{cfg.w4a4_rot}, per-row int4 weights, per-token "
+                         f"int4 acts) + {plan['w8a8']} W8A8 int8_tensorwise (per-token int8 acts), seeded choice",
+              "glue": "torch ops"}
+    def block_check():
+        errs = model.block_errors(x, ctx)
+        return {"max_block_rel_l2": max(errs), "mean_block_rel_l2": sum(errs) / len(errs),
+                "note": "teacher-forced: every block run by both paths on the kernel path's input to that block. "
+                        "The step-level rel_l2 grows over the 30 blocks because per-token int4 requantization turns "
+                        "a one-rounding difference in a linear's input into a code flip of 1/7 of the token scale"}
+
+    _run_dit(args, world, rank, local, model, (x, ctx), lambda o: o, "Wan DiT denoise steps/s", config,
+             2 * len(model.linears()), block_check)
+
+
+def _run_dit(args, world, rank, local, model, inputs, main_out, metric, config, launches_per_step, extra_check=None):
+    """Time model.step(*inputs) replayed from one CUDA graph (max over ranks), its end-to-end form with pinned host
+    copies, and a reference check of rank 0's output against the fp32-linear reference step."""
+    from comfy_quant_bench_b200 import _lib, mmdit as mm
+    stream = torch.cuda.current_stream(torch.device("cuda", local))
     for _ in range(args.warmup):
-        model.step(img, txt, temb)
+        model.step(*inputs)
     torch.cuda.synchronize()
-    side = torch.cuda.Stream(dev)
+    side = torch.cuda.Stream(stream.device)
     side.wait_stream(stream)
     with torch.cuda.stream(side):
-        model.step(img, txt, temb)
+        model.step(*inputs)
     stream.wait_stream(side)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        out_img, out_txt = model.step(img, txt, temb)
+        out = main_out(model.step(*inputs))
     graph.replay()
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -501,18 +545,18 @@ def run_mmdit(args, world, rank, local):
     barrier(world)
     total_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in evs), world)
     step_ms = total_ms / args.steps
-    # e2e: the step's inputs from pinned host memory into the graph's input buffers, the step, its image output back
-    h_img, h_txt, h_temb = img.cpu().pin_memory(), txt.cpu().pin_memory(), temb.cpu().pin_memory()
-    y_host = torch.empty_like(out_img, device="cpu").pin_memory()
-    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(3, min(args.steps, 10)))]
+    # e2e: the step's inputs from pinned host memory into the graph's input buffers, the step, its main output back
+    hosts = [t.cpu().pin_memory() for t in inputs]
+    y_host = torch.empty_like(out, device="cpu").pin_memory()
+    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(max(3, min(args.steps, 10)))]
     barrier(world)
     for e0, e1 in ee:
         e0.record(stream)
-        img.copy_(h_img, non_blocking=True)
-        txt.copy_(h_txt, non_blocking=True)
-        temb.copy_(h_temb, non_blocking=True)
+        for t, hst in zip(inputs, hosts):
+            t.copy_(hst, non_blocking=True)
         graph.replay()
-        y_host.copy_(out_img, non_blocking=True)
+        y_host.copy_(out, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in ee), world) / len(ee)
@@ -521,34 +565,34 @@ def run_mmdit(args, world, rank, local):
         raise RuntimeError(f"device status {st}")
     lin_ops = model.linear_int_ops()
     peaks = _peaks()
+    config = dict(config, parallelism=f"dp{world}", l2="weights (%.1f GB) larger than L2" % (model.weight_bytes() / 1e9),
+                  graph="one CUDA graph per step")
     line = {
-        "metric": "MMDiT denoise steps/s", "value": world * args.steps / (total_ms / 1e3), "unit": "steps/s",
+        "metric": metric, "value": world * args.steps / (total_ms / 1e3), "unit": "steps/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 linears, bf16 glue",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int4 linears, bf16 glue",
         "data": "synthetic (random-init weights N(0,0.02), inputs N(0,1))",
-        "config": {"workload": "mmdit_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads,
-                   "mlp": cfg.mlp, "img_tokens": cfg.img_tokens, "txt_tokens": cfg.txt_tokens, "batch": 1,
-                   "linears": "every linear W4A8 affine g128, ConvRot g256 (modulation included)",
-                   "parallelism": f"dp{world}", "l2": "weights (%.1f GB) larger than L2" % (model.weight_bytes() / 1e9),
-                   "graph": "one CUDA graph per step"},
+        "config": config,
         "step_latency_ms": step_ms,
         "linear_int_ops_per_step": lin_ops, "attention_flops_per_step": model.attention_flops(),
-        "roofline": {"bound": "tensor", "kernel": "step-level: linear int-ops / step time (the GEMM kernel alone is "
-                                                  "measured by the w4a8 workload)",
+        "roofline": {"bound": "tensor", "kernel": "step-level: linear int-ops / step time (the GEMM kernels alone are "
+                                                  "measured by the linear workloads)",
                      "achieved": lin_ops / (step_ms / 1e3) / 1e12, "peak": 2.0 * peaks["bf16_tflops"], "unit": "TOPS",
                      "frac": lin_ops / (step_ms / 1e3) / 1e12 / (2.0 * peaks["bf16_tflops"]), "traffic": None},
         "e2e": {"value": world / (e2e_ms / 1e3), "unit": "steps/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": (img.numel() + txt.numel() + temb.numel()) * 2,
-                "d2h_bytes_per_step": out_img.numel() * 2,
-                "path": "graph-replayed MMDiT step with pinned-host input/output copies"},
-        "gpu_launches": 2 * len(model.linears()) * args.steps,
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in inputs),
+                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "path": "graph-replayed step with pinned-host input/output copies"},
+        "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_reference_check:
-        ref_img, _ = model.step(img, txt, temb, reference=True)
-        line["reference_check"] = {"rel_l2_img": mm.rel_l2(out_img, ref_img),
+        ref = main_out(model.step(*inputs, reference=True))
+        line["reference_check"] = {"rel_l2": mm.rel_l2(out, ref),
                                    "against": "the same step with every linear as a torch fp32 product of the "
                                               "dequantized weight and the dequantized activation codes"}
+        if extra_check is not None:
+            line["reference_check"].update(extra_check())
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline("w4a8", args.cpu_rows, args.cpu_steps)
         line["cpu_baseline"] = {"value": cb["value"] * 1e12 / lin_ops, "unit": "steps/s", "cores": cb["cores"],
@@ -640,9 +684,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit", "sweep"], default="w4a8")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit", "wan", "sweep"], default="w4a8")
     ap.add_argument("--mode", choices=["dp", "tp", "tp_fused"], default="dp")
     ap.add_argument("--mmdit-blocks", type=int, default=60)
+    ap.add_argument("--wan-blocks", type=int, default=30)
     ap.add_argument("--no-reference-check", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--cpu-steps", type=int, default=5)
@@ -656,6 +701,8 @@ def main():
             run_reference(args, world, rank)
         elif args.workload == "mmdit":
             run_mmdit(args, world, rank, local)
+        elif args.workload == "wan":
+            run_wan(args, world, rank, local)
         elif args.workload == "sweep":
             run_sweep(args, world, rank, local)
         else:

@@ -331,7 +331,8 @@ __global__ void __launch_bounds__(1024) rotquant_kernel(const RotQuantArgs args)
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// Per-token int8 activations (the W4A8 / W8A8 activation kernel): two rows per CTA, packed f32x2 arithmetic.
+// Per-token int8 activations (the W4A8 / W8A8 activation kernel, and per-token int4 values held in int8 codes
+// for the W4A4 GEMM): two rows per CTA, packed f32x2 arithmetic.
 //
 // A CTA of W warps ("team") owns rows 2b and 2b+1.  Every register holds a float2 (row A value, row B value) of
 // the same column, so each butterfly, scale multiply and rounding step is one f32x2 instruction for two tokens,
@@ -571,7 +572,7 @@ __device__ __forceinline__ float2 bf16x2_round(float2 v) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
 }
 
-template <int ROT, int PASSES, bool LNMOD>
+template <int ROT, int PASSES, bool LNMOD, int QMAX>
 __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
   extern __shared__ __align__(16) unsigned char act8_smem[];
   __shared__ float red[2][act8::kMaxTeamWarps];
@@ -715,7 +716,9 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
       for (int w = 1; w < nwarps; ++w) { ma = fmaxf(ma, red[0][w]); mb = fmaxf(mb, red[1][w]); }
     }
   }
-  const float sa = fmaxf(__fmul_rn(ma, 1.0f / 127.0f), 1e-10f), sb = fmaxf(__fmul_rn(mb, 1.0f / 127.0f), 1e-10f);
+  // per-token scale max(absmax / QMAX, 1e-10) (QMAX 127: int8 codes; 7: int4 values held in int8 codes)
+  constexpr float kInvQ = 1.0f / static_cast<float>(QMAX);
+  const float sa = fmaxf(__fmul_rn(ma, kInvQ), 1e-10f), sb = fmaxf(__fmul_rn(mb, kInvQ), 1e-10f);
   const float2 inv = make_float2(__frcp_rn(sa), __frcp_rn(sb));
   if (threadIdx.x == 0) {
     float* scale = static_cast<float*>(args.scale);
@@ -733,7 +736,7 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
   else act8_quant_store<ROT, PASSES, true>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile);
 }
 
-template <int ROT, bool LNMOD = false>
+template <int ROT, bool LNMOD = false, int QMAX = 127>
 static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   // Three chunks per warp.  Measured on B200 at K = 3072 and 12288, M = 4096-65536: one or two chunks per warp
   // (more, smaller warps) were slower or equal, and so was a persistent variant that prefetched the next token
@@ -742,7 +745,7 @@ static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   const int nchunks = (a.K + 511) / 512;
   const int warps = (nchunks + kPasses - 1) / kPasses;
   const size_t smem = static_cast<size_t>(warps) * act8::kTileBytes;
-  auto k = act8_kernel<ROT, kPasses, LNMOD>;
+  auto k = act8_kernel<ROT, kPasses, LNMOD, QMAX>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   k<<<static_cast<unsigned>((a.rows_pad + 1) / 2), warps * 32, smem, st>>>(a);
   return cudaGetLastError();
@@ -808,7 +811,18 @@ cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantAr
     }
     return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT8_ROW>(rot, a, st);
   }
-  if (mode == MODE_ACT_INT4_ROW) return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_ROW>(rot, a, st);
+  if (mode == MODE_ACT_INT4_ROW) {
+    if (a.rows_pad == 0) return cudaSuccess;
+    if (a.int4_as_int8 && act8_fits(a)) {        // int4 values as int8 codes (the W4A4 GEMM's operand)
+      switch (rot) {
+        case 0: return launch_act8<0, false, 7>(a, st);
+        case 16: return launch_act8<16, false, 7>(a, st);
+        case 64: return launch_act8<64, false, 7>(a, st);
+        default: return launch_act8<256, false, 7>(a, st);
+      }
+    }
+    return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_ROW>(rot, a, st);
+  }
   return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_GROUP>(rot, a, st);
 }
 

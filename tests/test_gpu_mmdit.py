@@ -53,3 +53,22 @@ def test_mmdit_step_is_deterministic_and_graph_capturable(mmdit):
     torch.cuda.synchronize()
     assert torch.equal(graphed, eager)
     assert torch.equal(model.step(img, txt, temb)[0], eager)
+
+
+def test_wan_step_matches_reference():
+    """Wan-like block stack on the mixed plan (W4A4 ConvRot g64 and W8A8 linears) against the fp32-linear
+    reference of the same step (the same rel-L2 bound as the MMDiT step)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from comfy_quant_bench_b200 import wan, _lib
+    cfg = wan.WanConfig(blocks=2, hidden=512, heads=4, ffn=1536, frames=3, height=5, width=20, ctx_tokens=64)
+    model = wan.WanDiT(cfg, device="cuda", seed=7)
+    assert model.plan()["w4a4"] == round(0.35 * 20) and model.plan()["w8a8"] == 20 - round(0.35 * 20)
+    x, ctx = model.inputs(seed=8)
+    out = model.step(x, ctx)
+    ref = model.step(x, ctx, reference=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert wan.rel_l2(out, ref) <= 1e-2
+    assert max(model.block_errors(x, ctx)) <= 1e-2
+    assert _lib.take_device_status() == (0, 0)
