@@ -1,7 +1,7 @@
 """Benchmark of the W4A8 quantized linear (BASELINE north-star workload) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload w4a8|w4a4|c1|mmdit|wan|sweep]
+                    [--workload w4a8|w4a4|c1|mmdit|wan|ltx|sweep]
                     [--mode dp|tp|tp_fused]
 
 One step = one pass of the hot path over one synthetic batch: activation rotation (ConvRot g256) + per-token
@@ -22,6 +22,9 @@ the W4A8 affine path (4096 image + 256 text tokens, hidden 3072, MLP 12288; rand
 data-parallel replicas across ranks: value = steps/s over all ranks, ms_per_step = the step latency.
 ``--workload wan`` does the same for a Wan-2.2-5B-like 30-block video DiT (27,280 tokens, hidden 3072, FFN 14336)
 whose linears follow the mixed plan: a seeded 35 % ConvRot W4A4 (Hadamard g64), the rest W8A8 int8_tensorwise.
+``--workload ltx`` times one step of an LTX-like 48-block video DiT (hidden 4096, 32,768 tokens, every linear W4A8)
+on one GPU, or tensor-parallel over the N ranks (head-parallel attention, column-parallel projections and MLP with
+the gather inside the GEMM): value = the step latency in ms, "scaling": "strong".
 ``--workload sweep`` prints one line per case of the GEMM M sweep, the activation kernel at large M and the W4A4
 rotation-group / SwiGLU cases.
 
@@ -515,6 +518,87 @@ def run_wan(args, world, rank, local):
              2 * len(model.linears()), block_check)
 
 
+def run_ltx(args, world, rank, local):
+    """One LTX-like video DiT step (48 blocks, hidden 4096, 32,768 tokens, every linear W4A8), tensor-parallel over
+    the ranks (head-parallel attention, column-parallel projections / MLP with the gather inside the GEMM).  Eager
+    (the symmetric-memory barriers are not captured in a graph); device-timed, max over ranks."""
+    from comfy_quant_bench_b200 import ltx, _lib, mmdit as mm
+    dev = torch.device("cuda", local)
+    cfg = ltx.LTXConfig(blocks=args.ltx_blocks)
+    model = ltx.LTXDiT(cfg, device=dev, seed=0, rank=rank, world=world)
+    x, ctx = model.inputs(seed=1)              # the same activation on every rank (one step, split by columns)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        out = model.step(x, ctx)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for e0, e1 in evs:
+            e0.record(stream)
+            out = model.step(x, ctx)
+            e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in evs), world)
+    step_ms = total_ms / args.steps
+    # e2e: the step's input from pinned host memory, the step, its output back to the host (rank 0's copy)
+    hx, hc = x.cpu().pin_memory(), ctx.cpu().pin_memory()
+    y_host = torch.empty_like(out, device="cpu").pin_memory()
+    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(2)]
+    barrier(world)
+    for e0, e1 in ee:
+        e0.record(stream)
+        x.copy_(hx, non_blocking=True)
+        ctx.copy_(hc, non_blocking=True)
+        out = model.step(x, ctx)
+        y_host.copy_(out, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in ee), world) / len(ee)
+    st = _lib.take_device_status()
+    if st != (0, 0):
+        raise RuntimeError(f"device status {st}")
+    lin_ops = model.linear_int_ops()
+    peaks = _peaks()
+    line = {
+        "metric": "LTX DiT step latency", "value": step_ms, "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 linears, bf16 glue",
+        "data": "synthetic (random-init weights N(0,0.02), inputs N(0,1))",
+        "config": {"workload": "ltx_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads,
+                   "ffn": cfg.ffn, "tokens": cfg.tokens, "grid": [cfg.frames, cfg.height, cfg.width],
+                   "ctx_tokens": cfg.ctx_tokens, "batch": 1,
+                   "linears": "every linear W4A8 affine g128, ConvRot g256",
+                   "parallelism": f"tp{world}" if world > 1 else "1 GPU",
+                   "sharding": "head-parallel attention (QKV / cross Q, KV rows by head, heads_to_rows peer gather); "
+                               "column-parallel out projections and MLP (gather inside the GEMM)" if world > 1 else None,
+                   "l2": "weights larger than L2", "graph": "none (eager)"},
+        "step_latency_ms": step_ms,
+        "linear_int_ops_per_step": lin_ops, "attention_flops_per_step": model.attention_flops(),
+        "roofline": {"bound": "tensor", "kernel": "step-level: linear int-ops over all ranks / step time",
+                     "achieved": lin_ops / (step_ms / 1e3) / 1e12, "peak": 2.0 * peaks["bf16_tflops"] * world,
+                     "unit": "TOPS", "frac": lin_ops / (step_ms / 1e3) / 1e12 / (2.0 * peaks["bf16_tflops"] * world),
+                     "traffic": None},
+        "e2e": {"value": e2e_ms, "unit": "ms", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": (x.numel() + ctx.numel()) * 2, "d2h_bytes_per_step": out.numel() * 2,
+                "path": "LTXDiT.step with pinned-host input/output copies"},
+        "gpu_launches": (2 * len(model.linears()) + 3 * cfg.blocks) * args.steps,
+        "clocks": clk.summary(),
+    }
+    if world > 1 and not args.no_reference_check:
+        # rank 0 runs the same step on one GPU (the full weights, same seed) and compares
+        if rank == 0:
+            single = ltx.LTXDiT(cfg, device=dev, seed=0)
+            ref = single.step(x, ctx)
+            line["tp_check"] = {"rel_l2_vs_one_gpu": mm.rel_l2(out, ref), "bit_identical": bool(torch.equal(out, ref))}
+            del single, ref
+        barrier(world)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def _run_dit(args, world, rank, local, model, inputs, main_out, metric, config, launches_per_step, extra_check=None):
     """Time model.step(*inputs) replayed from one CUDA graph (max over ranks), its end-to-end form with pinned host
     copies, and a reference check of rank 0's output against the fp32-linear reference step."""
@@ -684,10 +768,11 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit", "wan", "sweep"], default="w4a8")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit", "wan", "ltx", "sweep"], default="w4a8")
     ap.add_argument("--mode", choices=["dp", "tp", "tp_fused"], default="dp")
     ap.add_argument("--mmdit-blocks", type=int, default=60)
     ap.add_argument("--wan-blocks", type=int, default=30)
+    ap.add_argument("--ltx-blocks", type=int, default=48)
     ap.add_argument("--no-reference-check", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--cpu-steps", type=int, default=5)
@@ -703,6 +788,8 @@ def main():
             run_mmdit(args, world, rank, local)
         elif args.workload == "wan":
             run_wan(args, world, rank, local)
+        elif args.workload == "ltx":
+            run_ltx(args, world, rank, local)
         elif args.workload == "sweep":
             run_sweep(args, world, rank, local)
         else:

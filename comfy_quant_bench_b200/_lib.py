@@ -67,6 +67,7 @@ SIGNATURES = {
     "cq_linear_w4a8_affine_lnmod": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _f32, _vp, _vp, _vp, _int, _vp,
                                            _vp, _vp, _i64, _vp]),
     "cq_qkv_rmsnorm_rope": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "cq_heads_to_rows": (_int, [_vp, _i64, _int, _int, _vp, _int, _i64, _i64, _vp]),
 }
 
 

@@ -137,6 +137,31 @@ int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_no
   return cuda_status(cq::launch_qkv_rmsnorm_rope(a, static_cast<cudaStream_t>(stream)));
 }
 
+int cq_heads_to_rows(const void* o, int64_t S, int Hp, int D, void* const* outs, int n_outs, int64_t col0,
+                     int64_t ldo, void* stream) {
+  if (S < 0 || S > kMaxRows || Hp < 1 || (D != 64 && D != 128) || Hp * D > 8192) return CQ_ERR_SHAPE;
+  if (col0 < 0 || col0 % 8 != 0 || ldo % 8 != 0 || col0 + static_cast<int64_t>(Hp) * D > ldo) return CQ_ERR_SHAPE;
+  if (outs == nullptr || n_outs < 1 || n_outs > cq::kMaxOutBuffers) return CQ_ERR_ARG;
+  if (S == 0) return CQ_OK;
+  if (o == nullptr) return CQ_ERR_ARG;
+  if (!aligned(o, 16)) return CQ_ERR_ALIGN;
+  cq::HeadsToRowsArgs a{};
+  a.src = static_cast<const __nv_bfloat16*>(o);
+  for (int i = 0; i < n_outs; ++i) {
+    if (outs[i] == nullptr) return CQ_ERR_ARG;
+    if (!aligned(outs[i], 16)) return CQ_ERR_ALIGN;
+    a.outs[i] = static_cast<__nv_bfloat16*>(outs[i]);
+  }
+  if (int dv = check_device()) return dv;
+  a.n_out = n_outs;
+  a.S = S;
+  a.Hp = Hp;
+  a.D = D;
+  a.col0 = col0;
+  a.ldo = ldo;
+  return cuda_status(cq::launch_heads_to_rows(a, static_cast<cudaStream_t>(stream)));
+}
+
 int cq_weight_rotquant(const void* w, int w_is_bf16, int64_t N, int64_t K, int rot_group, int mode, int group,
                        void* q, void* scale, void* zeros, void* stream) {
   if (N < 0 || N > kMaxRows) return CQ_ERR_SHAPE;

@@ -79,4 +79,23 @@ cudaError_t launch_qkv_rmsnorm_rope(const QkvRopeArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// heads_to_rows_kernel: attention output o [Hp, S, D] (this rank's Hp heads, bf16) -> rows of [S, ldo] at columns
+// col0 + h*D + [0, D), written into every buffer of outs (the head-parallel attention's gather: peer buffers of a
+// symmetric allocation, or one local buffer, where it replaces the transposing copy to the [tokens, hidden] layout).
+// One CTA per token, 16 bytes per thread, plain stores.
+__global__ void __launch_bounds__(1024) heads_to_rows_kernel(const HeadsToRowsArgs a) {
+  const int64_t s = blockIdx.x;
+  const int per_head = a.D / 8;
+  const int h = threadIdx.x / per_head, c8 = threadIdx.x - h * per_head;
+  const uint4 v = *reinterpret_cast<const uint4*>(a.src + (static_cast<int64_t>(h) * a.S + s) * a.D + 8 * c8);
+  const int64_t off = s * a.ldo + a.col0 + static_cast<int64_t>(h) * a.D + 8 * c8;
+  for (int i = 0; i < a.n_out; ++i) *reinterpret_cast<uint4*>(a.outs[i] + off) = v;
+}
+
+cudaError_t launch_heads_to_rows(const HeadsToRowsArgs& a, cudaStream_t st) {
+  if (a.S == 0) return cudaSuccess;
+  heads_to_rows_kernel<<<static_cast<unsigned>(a.S), a.Hp * a.D / 8, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace cq

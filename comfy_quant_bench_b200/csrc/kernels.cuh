@@ -44,6 +44,17 @@ struct QkvRopeArgs {
 };
 cudaError_t launch_qkv_rmsnorm_rope(const QkvRopeArgs& a, cudaStream_t st);
 
+// DiT glue: head-major attention output -> [tokens, hidden] rows in up to kMaxOutBuffers buffers
+struct HeadsToRowsArgs {
+  const __nv_bfloat16* src;   // [Hp, S, D]
+  __nv_bfloat16* outs[8];     // [S, ldo] each
+  int n_out;
+  int64_t S;
+  int Hp, D;
+  int64_t col0, ldo;
+};
+cudaError_t launch_heads_to_rows(const HeadsToRowsArgs& a, cudaStream_t st);
+
 cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_weight_rotquant(int rot, bool w_bf16, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_unpack_int4(const void* src, int64_t n_bytes, void* dst, cudaStream_t st);

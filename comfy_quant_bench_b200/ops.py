@@ -475,3 +475,42 @@ def qkv_rmsnorm_rope(y: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor
     qn, kn = q_norm.to(torch.bfloat16).contiguous(), k_norm.to(torch.bfloat16).contiguous()
     _lib.call("cq_qkv_rmsnorm_rope", _ptr(y2), s, h, d, _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(q), _ptr(k),
               _ptr(v), s_all, int(s0), _stream(dev))
+
+
+def _out_ptrs(outs, rows: int, ldo: int):
+    ptrs = []
+    for o in outs:
+        if isinstance(o, torch.Tensor):
+            if o.dtype != torch.bfloat16 or o.dim() != 2 or o.shape[1] != ldo or o.shape[0] < rows or not o.is_contiguous():
+                raise ValueError(f"output buffers must be contiguous bf16 [>= {rows}, {ldo}]")
+            ptrs.append(o.data_ptr())
+        else:
+            ptrs.append(int(o))
+    return (ctypes.c_void_p * len(ptrs))(*ptrs), len(ptrs)
+
+
+def heads_to_rows(o: torch.Tensor, outs, col0: int, ldo: int) -> None:
+    """Attention output o [1, Hp, S, D] (bf16) into rows [S, ldo] at columns col0 + h*D of every buffer in ``outs``
+    (tensors or raw device pointers, e.g. the peer buffers of a symmetric allocation)."""
+    dev = _require_cuda(o)
+    if o.dim() != 4 or o.shape[0] != 1 or o.dtype != torch.bfloat16:
+        raise ValueError("o must be bf16 [1, Hp, S, D]")
+    o = o.contiguous()
+    _, hp, s, d = o.shape
+    arr, n = _out_ptrs(outs, s, ldo)
+    _lib.call("cq_heads_to_rows", _ptr(o), s, hp, d, arr, n, int(col0), int(ldo), _stream(dev))
+
+
+def gemm_affine_into(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qweight: torch.Tensor,
+                     scale: torch.Tensor, zeros_prepared: torch.Tensor, bias, outs, col0: int, ldo: int, *,
+                     m: int | None = None, a_kperm: bool = True) -> None:
+    """The affine GEMM on pre-quantized activations (``rotquant`` / ``rotquant_lnmod`` outputs; the first ``m`` rows)
+    writing its N = qweight.shape[0] columns into every buffer of ``outs`` at [col0, col0 + N)."""
+    dev = _require_cuda(a, sa, gsplit, qweight, scale, zeros_prepared, bias)
+    m = a.shape[0] if m is None else int(m)
+    k = a.shape[1]
+    n = qweight.shape[0]
+    arr, cnt = _out_ptrs(outs, m, ldo)
+    _lib.call("cq_gemm_affine_peers", _ptr(a), int(bool(a_kperm)), _ptr(sa), _ptr(gsplit), _ptr(qweight),
+              _ptr(scale), _ptr(zeros_prepared), _ptr(_bias_bf16(bias)), arr, cnt, int(col0), int(ldo), m, n, k, 128,
+              _stream(dev))

@@ -257,6 +257,14 @@ CQ_API int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int6
                                        const void* shift, const void* scale1p, float eps, const void* qweight,
                                        const void* s_bf16, const void* zt_bf16, int group, const void* bias,
                                        void* out, void* workspace, int64_t workspace_bytes, void* stream);
+/*
+ * cq_heads_to_rows: attention output o bf16 [Hp, S, D] (head-major, batch 1) -> outs[i][s, col0 + h*D + d] for
+ * every buffer outs[i] (bf16 [S, ldo], 16-byte aligned, 1..8 buffers).  With one local buffer it is the transpose
+ * to the [tokens, hidden] layout of the output projection; with the peer buffers of a head-parallel attention it
+ * gathers every rank's heads into every rank's rows.  D = 64 or 128, Hp * D <= 8192, col0 % 8 == 0, ldo % 8 == 0.
+ */
+CQ_API int cq_heads_to_rows(const void* o, int64_t S, int Hp, int D, void* const* outs, int n_outs, int64_t col0,
+                            int64_t ldo, void* stream);
 CQ_API int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm,
                                float eps, const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0,
                                void* stream);
