@@ -483,7 +483,7 @@ def run_mmdit(args, world, rank, local):
     cfg = mm.MMDiTConfig(blocks=args.mmdit_blocks)
     model = mm.MMDiT(cfg, device=dev, seed=0)
     img, txt, temb = model.inputs(seed=1 + rank)
-    launches = 2 * len(model.linears()) + (2 * cfg.blocks if cfg.fused_glue else 0)
+    launches = 2 * len(model.linears()) + (3 * cfg.blocks if cfg.fused_glue else 0)   # + qkv glue x2, head gather
     config = {"workload": "mmdit_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads,
               "mlp": cfg.mlp, "img_tokens": cfg.img_tokens, "txt_tokens": cfg.txt_tokens, "batch": 1,
               "linears": "every linear W4A8 affine g128, ConvRot g256 (modulation included)",

@@ -14,8 +14,9 @@ per-128-group scale/zero, tcgen05 GEMM).  The block follows the usual MMDiT layo
 
 Attention, GELU and the gated residuals are torch ops.  The layer norm + modulation before the QKV and MLP-up
 linears run inside the library's activation kernel (``ops.w4a8_affine_linear_lnmod``) and the q/k RMSNorm + rotary
-embedding + joint attention layout run as one library kernel (``ops.qkv_rmsnorm_rope``); ``fused_glue=False``
-runs them as torch ops instead.  Weights are drawn N(0, 0.02) per linear from a
+embedding + joint attention layout run as one library kernel (``ops.qkv_rmsnorm_rope``), and the attention output
+goes to the [tokens, hidden] layout through ``ops.heads_to_rows``; ``fused_glue=False`` runs them as torch ops
+instead.  Weights are drawn N(0, 0.02) per linear from a
 seeded generator, quantized on the device with the library's weight kernel, and only the packed form is kept.
 
 ``MMDiT.step(..., reference=True)`` runs the same step with every linear replaced by a torch fp32 product of the
@@ -207,7 +208,11 @@ class MMDiT:
                 q[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 0], (d,), s.q_norm, eps=1e-6), rot).transpose(0, 1)
                 k[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 1], (d,), s.k_norm, eps=1e-6), rot).transpose(0, 1)
                 v[0, :, lo:hi] = y[:, 2].transpose(0, 1)
-            a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
+            if fused:
+                a = torch.empty(s_all, h, dtype=torch.bfloat16, device=img.device)
+                ops.heads_to_rows(F.scaled_dot_product_attention(q, k, v), [a], 0, h)
+            else:
+                a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
             new = []
             for x, s, m, att in ((txt, st, mt, a[:st_txt]), (img, si, mi, a[st_txt:])):
                 x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
