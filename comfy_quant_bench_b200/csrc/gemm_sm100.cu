@@ -87,6 +87,8 @@ struct GemmArgs {
   int tma_out;           // affine: outputs leave through the TMA store maps (N % 8 == 0, 16-byte aligned out)
   int n_out;             // affine with tma_out: number of output maps (1, or the ranks of a column-parallel layer)
   int out_col0;          // affine with tma_out: column of the output maps where this launch's N columns start
+  int split;             // row/col epilogue: the last `split` tiles of the tile order run as two 128-token half
+                         // tiles each (a partial last wave of at most half the CTAs finishes in half a tile's time)
   int out_w64;           // affine with tma_out: two epilogue warps (adjacent lane quadrants) share one 64-column
                          // box per pass (128-byte rows) instead of one 32-column box each (N % 64 == 0)
 };
@@ -123,6 +125,24 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   const int rows = min(kRasterGroup, m_tiles - g * kRasterGroup);   // token tiles in this (possibly last) group
   mt = g * kRasterGroup + t % rows;
   nt = t / rows;
+}
+
+// Work item -> tile and token range.  Items [0, num_tiles - split) are whole tiles in raster order; each of the last
+// `split` tiles becomes two items, its tokens [0, 128) and [128, 256).  t0: first token of the item in its tile;
+// width: 256 (whole) or 128 (half).
+__device__ __forceinline__ void item_coords(int item, int num_tiles, int split, int m_tiles, int n_tiles, int& mt,
+                                            int& nt, int& t0, int& width) {
+  const int whole = num_tiles - split;
+  int tile = item;
+  t0 = 0;
+  width = kBT;
+  if (item >= whole) {
+    const int h = item - whole;
+    tile = whole + (h >> 1);
+    t0 = 128 * (h & 1);
+    width = 128;
+  }
+  tile_coords(tile, m_tiles, n_tiles, mt, nt);
 }
 
 // 8 packed bytes (16 nibbles, low nibble = even column) -> 16 bytes holding 16*v per column.
@@ -174,6 +194,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   const int m_tiles = (M + kBT - 1) / kBT;
   const int n_tiles = (N + kBW - 1) / kBW;
   const int num_tiles = m_tiles * n_tiles;
+  // Half tiles only for the row/col epilogue, which drains once per tile: the affine epilogue drains every group
+  // in each warp's own 128 token columns, so a half tile would take a whole tile's drain time (measured: no gain,
+  // and the extra control flow spills registers in the affine epilogue).
+  constexpr bool kSplit = (EPI == EPI_ROWCOL);
+  const int split = kSplit ? args.split : 0;
+  const int num_items = num_tiles + split;
+  auto coords = [&](int item, int& mt, int& nt, int& t0, int& width) {
+    if constexpr (kSplit) {
+      item_coords(item, num_tiles, split, m_tiles, n_tiles, mt, nt, t0, width);
+    } else {
+      tile_coords(item, m_tiles, n_tiles, mt, nt);
+      t0 = 0;
+      width = kBT;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTmaStages; ++s) {
@@ -217,10 +252,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       // ------------------------------ TMA producer ------------------------------
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(tile, m_tiles, n_tiles, mt, nt);
-        const int m0 = mt * kBT;
+      for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
+        int mt, nt, t0, width;
+        coords(item, mt, nt, t0, width);
+        const int m0 = mt * kBT + t0;    // a half tile loads 256 rows from its first token; the MMA reads 128
         const int n0 = nt * kBW;
         if (EPI == EPI_AFFINE) {
           // zero-point operand: the tokens' split group sums (bf16, 64 columns per block) into the X slot
@@ -244,13 +279,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       }
     } else if (warp == 1 && lane == 0) {
       // ------------------------------ MMA issuer ------------------------------
-      constexpr uint32_t idesc = idesc_i8(kBW, kBT);
       int stage = 0, cstage = 0;
       uint32_t phase = 0, cphase = 0;
       int buf = 0;
       uint32_t buf_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        int mt, nt, t0, width;
+        coords(item, mt, nt, t0, width);
+        const uint32_t idesc = width == kBT ? idesc_i8(kBW, kBT) : idesc_i8(kBW, 128);
         if (EPI == EPI_ROWCOL) {
           if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 2))) break;
           tc_fence_after();
@@ -259,7 +296,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // D = sum_j Zt[n, j] * Rsplit[m, j] in fp32: the zero-point term, the accumulator's starting value
           if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 11))) break;
           tc_fence_after();
-          constexpr uint32_t idesc_z = idesc_bf16(kBW, kBT);
+          const uint32_t idesc_z = width == kBT ? idesc_bf16(kBW, kBT) : idesc_bf16(kBW, 128);
           for (int p = 0; p < args.nz && ok; ++p) {
             if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 12))) break;
             if (!(ok = mbar_wait(&full_conv[cstage], cphase, abort_flag, 13))) break;
@@ -278,6 +315,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           }
           if (!ok) break;
           tc_commit(&tmem_full[buf]);
+          if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);   // the idle second-half epilogue warps
           if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
         for (int kb = 0; kb < kblocks && ok; ++kb) {
@@ -304,6 +342,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (kConv) tc_commit(&empty_conv[cstage]);
           if (EPI == EPI_AFFINE) {
             tc_commit(&tmem_full[buf]);
+            if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);
             if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
           }
           if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
@@ -311,6 +350,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         }
         if (EPI == EPI_ROWCOL && ok) {
           tc_commit(&tmem_full[buf]);
+          if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);
           if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
         }
       }
@@ -332,10 +372,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       uint8_t* const drow0 = dst + rr * 128;
       const uint32_t dlo = static_cast<uint32_t>(((2 * c4) ^ (rr & 7)) << 4), dhi = static_cast<uint32_t>(((2 * c4 + 1) ^ (rr & 7)) << 4);
       // block j = pair + 3 i: its tile, its index b inside the tile and its TMA stage advance incrementally
-      int tile = blockIdx.x, b = pair, stage = pair;
+      int item = blockIdx.x, b = pair, stage = pair;
       uint32_t phase = 0, cphase = 0, zphase = 0;
-      while (b >= bpt) { b -= bpt; tile += gridDim.x; }
-      for (; tile < num_tiles; cphase ^= 1u) {
+      while (b >= bpt) { b -= bpt; item += gridDim.x; }
+      for (; item < num_items; cphase ^= 1u) {
         if (!mbar_wait(&empty_conv[pair], cphase ^ 1u, abort_flag, 9)) break;
         if (EPI == EPI_AFFINE && b < nzb) {
           // zero-point weight operand: rows n0..n0+127 of the prepared Zt, 64 bf16 columns per pseudo block, one TMA
@@ -343,8 +383,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // stage carries the activation-side operand.
           if (warp == 2 + 2 * pair && lane == 0) {
             mbar_arrive_expect_tx(&zt_full[pair], kWuBytes);
-            int mt, nt;
-            tile_coords(tile, m_tiles, n_tiles, mt, nt);
+            int mt, nt, t0, width;
+            coords(item, mt, nt, t0, width);
             tma_load_2d(dst, &tm_z, &zt_full[pair], 128 * b, nt * kBW);
           }
           if (!mbar_wait(&zt_full[pair], zphase, abort_flag, 16)) break;
@@ -364,7 +404,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_conv[pair]);
         b += kConvStages;
-        while (b >= bpt) { b -= bpt; tile += gridDim.x; }
+        while (b >= bpt) { b -= bpt; item += gridDim.x; }
         stage += kConvStages;
         if (stage >= kTmaStages) { stage -= kTmaStages; phase ^= 1u; }
       }
@@ -390,10 +430,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
     }
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int mt, nt;
-      tile_coords(tile, m_tiles, n_tiles, mt, nt);
-      const int m0 = mt * kBT + half * 128;
+    for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      int mt, nt, t0, width;
+      coords(item, mt, nt, t0, width);
+      if (half * 128 >= width) {
+        // a half tile holds tokens for the first half's warps only; the MMA issuer arrives on this warp's behalf on
+        // each of the item's accumulator buffers, so the warp only steps its buffer position past the item
+        const int total = buf + ((EPI == EPI_AFFINE) ? 1 + kblocks : 1);
+        buf = total & 1;
+        buf_phase ^= static_cast<uint32_t>(total >> 1) & 1u;
+        continue;
+      }
+      const int m0 = mt * kBT + t0 + half * 128;
       const int n = nt * kBW + quad * 32 + lane;
       const bool n_ok = n < N;
       const bool m_full = m0 + 128 <= M;     // every token of this half-tile exists: no per-element checks
@@ -737,7 +785,17 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     ga.n_out = 1;
   }
   const int tiles = ((args.M + kBT - 1) / kBT) * ((args.N + kBW - 1) / kBW);
-  const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+  // Half tiles for a partial last wave: with R = tiles mod SMs whole tiles left after the full waves, running them
+  // as 2R half tiles ends the launch half a tile earlier whenever 2R <= SMs (R > SMs / 2 gains nothing at half-tile
+  // granularity).  With fewer tiles than SMs, all tiles split when that at most fills the SMs.
+  int split = 0;
+  if (EPI == EPI_ROWCOL) {
+    if (tiles < g_num_sms) split = 2 * tiles <= g_num_sms ? tiles : 0;
+    else if (2 * (tiles % g_num_sms) <= g_num_sms) split = tiles % g_num_sms;
+  }
+  ga.split = split;
+  const int items = tiles + split;
+  const int grid = items < g_num_sms ? items : g_num_sms;
   if (grid == 0) return CQ_OK;
   kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_out, ga);
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
