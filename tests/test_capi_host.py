@@ -69,6 +69,44 @@ def test_host_side_argument_checks_need_no_device(lib):
     assert lib.cq_linear_workspace_bytes(-1, 3072) == -1
 
 
+def test_dit_glue_argument_checks_need_no_device(lib):
+    from comfy_quant_bench_b200 import _lib
+    vp = ctypes.c_void_p(16)
+    f = ctypes.c_float(1e-6)
+    # layer-norm prologue: K multiple of 256 and at most 24576; only CQ_Q_KPERM; negative eps; misaligned shift
+    assert lib.cq_rotquant_lnmod(vp, 4, 300, 256, vp, vp, f, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_rotquant_lnmod(vp, 4, 32768, 256, vp, vp, f, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_rotquant_lnmod(vp, 4, 512, 256, vp, vp, f, 4, 1, vp, vp, None, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_rotquant_lnmod(vp, 4, 512, 256, vp, vp, ctypes.c_float(-1.0), 4, 0, vp, vp, None, None) == \
+        _lib.CQ_ERR_ARG
+    assert lib.cq_rotquant_lnmod(vp, 4, 512, 256, ctypes.c_void_p(18), vp, f, 4, 0, vp, vp, None, None) == \
+        _lib.CQ_ERR_ALIGN
+    assert lib.cq_rotquant_lnmod(vp, 4, 512, 256, None, vp, f, 4, 0, vp, vp, None, None) == _lib.CQ_ERR_ARG
+    # q/k RMSNorm + rotary: head dim 64 or 128; the stream's tokens inside the joint sequence
+    assert lib.cq_qkv_rmsnorm_rope(vp, 8, 4, 96, vp, vp, f, vp, vp, vp, vp, 8, 0, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_qkv_rmsnorm_rope(vp, 8, 4, 128, vp, vp, f, vp, vp, vp, vp, 10, 4, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_qkv_rmsnorm_rope(vp, 0, 4, 128, None, None, f, None, None, None, None, 10, 4, None) == _lib.CQ_OK
+    # head gather: 1..8 buffers, 16-byte aligned, columns inside the rows
+    outs = (ctypes.c_void_p * 2)(16, 32)
+    assert lib.cq_heads_to_rows(vp, 8, 4, 128, outs, 0, 0, 512, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_heads_to_rows(vp, 8, 4, 128, outs, 9, 0, 512, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_heads_to_rows(vp, 8, 4, 128, outs, 2, 8, 512, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_heads_to_rows(vp, 8, 4, 128, outs, 2, 4, 1024, None) == _lib.CQ_ERR_SHAPE
+    bad = (ctypes.c_void_p * 2)(16, 40)
+    assert lib.cq_heads_to_rows(vp, 8, 4, 128, bad, 2, 0, 512, None) == _lib.CQ_ERR_ALIGN
+
+
+def test_dit_glue_ops_reject_bad_layouts_on_the_host():
+    import torch
+    from comfy_quant_bench_b200 import ops
+    with pytest.raises(ValueError):
+        ops.heads_to_rows(torch.zeros(2, 4, 8, 128, dtype=torch.bfloat16), [], 0, 512)   # CPU tensor
+    with pytest.raises(ValueError):
+        ops.qkv_rmsnorm_rope(torch.zeros(8, 1536, dtype=torch.bfloat16), torch.ones(128), torch.ones(128),
+                             torch.zeros(8, 64, 2), torch.zeros(1, 4, 8, 128), torch.zeros(1, 4, 8, 128),
+                             torch.zeros(1, 4, 8, 128), 0)
+
+
 def test_python_errors_map_to_exceptions():
     from comfy_quant_bench_b200 import _lib
     with pytest.raises(_lib.CQShapeError):

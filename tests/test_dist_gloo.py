@@ -112,3 +112,19 @@ def test_shard_bounds_reject_uneven_split():
     from comfy_quant_bench_b200.dist import shard_bounds
     with pytest.raises(ValueError):
         shard_bounds(10, 0, 4)
+
+
+def test_head_parallel_rows_partition_the_fused_weight():
+    """The head-parallel shards of a fused [parts * hidden, K] weight (q | k | v) cover every row exactly once, and
+    each rank's rows come out part by part, heads in order (the local output layout [S, parts, H/P, D])."""
+    from comfy_quant_bench_b200.ltx import _head_rows
+    hidden, heads, world = 512, 8, 4
+    d, hp = hidden // heads, heads // world
+    for parts in (1, 2, 3):
+        shards = [_head_rows(hidden, parts, r * hp, (r + 1) * hp, d) for r in range(world)]
+        rows = sorted(x for sh in shards for x in sh)
+        assert rows == list(range(parts * hidden))
+        for r, sh in enumerate(shards):
+            for p in range(parts):
+                block = sh[p * hp * d:(p + 1) * hp * d]
+                assert block == list(range(p * hidden + r * hp * d, p * hidden + (r + 1) * hp * d))
