@@ -35,7 +35,11 @@
 namespace cq {
 
 constexpr int kBW = 128;       // weight rows per tile (MMA M, TMEM lanes)
-constexpr int kBT = 256;       // tokens per tile (MMA N, TMEM columns per accumulator buffer)
+constexpr int kBT = 256;       // tokens per tile (MMA N, TMEM columns per accumulator buffer; 128 also builds and
+                               // passes the tests, but measured ~40 % slower)
+constexpr int kNumBufs = 512 / kBT;    // accumulator buffers in the 512 TMEM columns
+constexpr int kWarpTok = kBT / 2;      // tokens per epilogue warp (two warps per TMEM lane quadrant)
+constexpr int kChunks = kWarpTok / 32; // 32-column TMEM loads per epilogue warp per drain
 constexpr int kBK = 128;       // K elements (bytes of int8) per stage
 constexpr int kConvStages = 3;
 constexpr int kThreads = 512;
@@ -56,13 +60,13 @@ enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 // staging buffers of its asynchronous (TMA) output stores.
 template <int EPI, int BFMT>
 struct SmemPlan {
-  static constexpr int kStages = (EPI == EPI_AFFINE) ? 3 : 4;       // TMA ring depth
+  static constexpr int kStages = (EPI == EPI_AFFINE) ? (kBT == 256 ? 3 : 4) : (kBT == 256 ? 4 : 6);   // TMA ring
   static constexpr int kWStageBytes = (BFMT == BF_S8) ? kWuBytes : kWpBytes;   // weight bytes in the TMA ring
   static constexpr int kTmaStageBytes = kXBytes + kWStageBytes;
   static constexpr int kConvBytes = (BFMT == BF_S8) ? 0 : kConvStages * kWuBytes;
   static constexpr int kData = kStages * kTmaStageBytes + kConvBytes;
-  static constexpr int kSaStage = kData + 256;                    // after the barriers: per-token scales
-  static constexpr int kSaBytes = 8 * 128 * 4;                    // 128 fp32 per epilogue warp
+  static constexpr int kSaStage = kData + 512;                    // after the barriers: per-token scales
+  static constexpr int kSaBytes = 8 * kWarpTok * 4;               // kWarpTok fp32 per epilogue warp
   static constexpr int kOutStage = kSaStage + kSaBytes;           // output staging: 64 tokens x 32 columns bf16
   static constexpr int kOutWarpBytes = 64 * 32 * 2;               //   per epilogue warp (affine only)
   static constexpr int kOutBytes = (EPI == EPI_AFFINE) ? 8 * kOutWarpBytes : 0;
@@ -128,8 +132,8 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
 }
 
 // Work item -> tile and token range.  Items [0, num_tiles - split) are whole tiles in raster order; each of the last
-// `split` tiles becomes two items, its tokens [0, 128) and [128, 256).  t0: first token of the item in its tile;
-// width: 256 (whole) or 128 (half).
+// `split` tiles becomes two items, the two halves of its tokens.  t0: first token of the item in its tile; width:
+// kBT (whole) or kBT / 2 (half).
 __device__ __forceinline__ void item_coords(int item, int num_tiles, int split, int m_tiles, int n_tiles, int& mt,
                                             int& nt, int& t0, int& width) {
   const int whole = num_tiles - split;
@@ -139,8 +143,8 @@ __device__ __forceinline__ void item_coords(int item, int num_tiles, int split, 
   if (item >= whole) {
     const int h = item - whole;
     tile = whole + (h >> 1);
-    t0 = 128 * (h & 1);
-    width = 128;
+    t0 = (kBT / 2) * (h & 1);
+    width = kBT / 2;
   }
   tile_coords(tile, m_tiles, n_tiles, mt, nt);
 }
@@ -178,13 +182,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   uint64_t* full_conv = bars + 2 * kTmaStages;
   uint64_t* empty_conv = full_conv + kConvStages;
   uint64_t* tmem_full = empty_conv + kConvStages;
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* zt_full = tmem_empty + 2;   // affine: per converter pair, the TMA load of its zero-point operand
+  uint64_t* tmem_empty = tmem_full + kNumBufs;
+  uint64_t* zt_full = tmem_empty + kNumBufs;   // affine: per converter pair, the TMA load of its zero-point operand
   uint64_t* box_free = zt_full + kConvStages;   // affine, 64-column boxes: per epilogue warp pair, staging free
   uint64_t* box_full = box_free + 4;            //   and both halves of the box written
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(box_full + 4);
-  static_assert((2 * kTmaStages + 3 * kConvStages + 2 + 2 + 8) * 8 + 4 <= P::kSaStage - P::kData,
-                "the barriers and the TMEM address fit the 256-byte region before the scale staging");
+  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 8) * 8 + 8 <= P::kSaStage - P::kData,
+                "the barriers, the TMEM address and the abort flag fit the region before the scale staging");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -220,7 +224,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       mbar_init(&empty_conv[s], 1);
       mbar_init(&zt_full[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kNumBufs; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 8);
     }
@@ -287,7 +291,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
         int mt, nt, t0, width;
         coords(item, mt, nt, t0, width);
-        const uint32_t idesc = width == kBT ? idesc_i8(kBW, kBT) : idesc_i8(kBW, 128);
+        const uint32_t idesc = width == kBT ? idesc_i8(kBW, kBT) : idesc_i8(kBW, kBT / 2);
         if (EPI == EPI_ROWCOL) {
           if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 2))) break;
           tc_fence_after();
@@ -296,7 +300,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // D = sum_j Zt[n, j] * Rsplit[m, j] in fp32: the zero-point term, the accumulator's starting value
           if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 11))) break;
           tc_fence_after();
-          const uint32_t idesc_z = width == kBT ? idesc_bf16(kBW, kBT) : idesc_bf16(kBW, 128);
+          const uint32_t idesc_z = width == kBT ? idesc_bf16(kBW, kBT) : idesc_bf16(kBW, kBT / 2);
           for (int p = 0; p < args.nz && ok; ++p) {
             if (!(ok = mbar_wait(&full_tma[stage], phase, abort_flag, 12))) break;
             if (!(ok = mbar_wait(&full_conv[cstage], cphase, abort_flag, 13))) break;
@@ -316,7 +320,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (!ok) break;
           tc_commit(&tmem_full[buf]);
           if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);   // the idle second-half epilogue warps
-          if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
+          if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
         for (int kb = 0; kb < kblocks && ok; ++kb) {
           if (EPI == EPI_AFFINE) {
@@ -343,7 +347,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (EPI == EPI_AFFINE) {
             tc_commit(&tmem_full[buf]);
             if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);
-            if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
+            if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
           }
           if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
           if (kConv && ++cstage == kConvStages) { cstage = 0; cphase ^= 1u; }
@@ -351,7 +355,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         if (EPI == EPI_ROWCOL && ok) {
           tc_commit(&tmem_full[buf]);
           if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);
-          if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
+          if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
       }
     } else if (warp >= 2 && kConv) {
@@ -419,13 +423,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     // the int4 unpack stores 16*v; fold the 1/16 into the weight scale (exact)
     const float wscale_fold = (BFMT == BF_S8) ? 1.0f : 0.0625f;
     // this warp's 128 token scales for the store phase (read back as broadcast float4 loads)
-    float* sa_stage = reinterpret_cast<float*>(smem + P::kSaStage) + e * 128;
+    float* sa_stage = reinterpret_cast<float*>(smem + P::kSaStage) + e * kWarpTok;
     uint32_t box_pass = 0;                // output store passes so far (phase of this warp pair's box barriers)
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
     // hand both accumulator buffers to the MMA issuer
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kNumBufs; ++b) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
@@ -433,39 +437,39 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
       int mt, nt, t0, width;
       coords(item, mt, nt, t0, width);
-      if (half * 128 >= width) {
+      if (half * kWarpTok >= width) {
         // a half tile holds tokens for the first half's warps only; the MMA issuer arrives on this warp's behalf on
         // each of the item's accumulator buffers, so the warp only steps its buffer position past the item
-        const int total = buf + ((EPI == EPI_AFFINE) ? 1 + kblocks : 1);
-        buf = total & 1;
-        buf_phase ^= static_cast<uint32_t>(total >> 1) & 1u;
+        const int uses = (EPI == EPI_AFFINE) ? 1 + kblocks : 1;
+        for (int u = 0; u < uses; ++u)
+          if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         continue;
       }
-      const int m0 = mt * kBT + t0 + half * 128;
+      const int m0 = mt * kBT + t0 + half * kWarpTok;
       const int n = nt * kBW + quad * 32 + lane;
       const bool n_ok = n < N;
-      const bool m_full = m0 + 128 <= M;     // every token of this half-tile exists: no per-element checks
+      const bool m_full = m0 + kWarpTok <= M;   // every token of the warp exists: no per-element checks
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
       // the tokens' activation scales, one per lane and 32-token chunk, loaded when the tile starts so that their
       // latency hides behind the tile's MMAs (indices past the last token clamp to it; those rows are not stored)
-      float sa_pre[4];
+      float sa_pre[kChunks];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) sa_pre[c] = __ldg(args.sa + min(m0 + 32 * c + lane, M - 1));
+      for (int c = 0; c < kChunks; ++c) sa_pre[c] = __ldg(args.sa + min(m0 + 32 * c + lane, M - 1));
       auto stage_sa = [&]() {
         __syncwarp();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sa_stage[32 * c + lane] = sa_pre[c];
+        for (int c = 0; c < kChunks; ++c) sa_stage[32 * c + lane] = sa_pre[c];
         __syncwarp();
       };
       if (EPI == EPI_AFFINE) {
-        float2 acc[64];
+        float2 acc[kWarpTok / 2];
         {
           // starting value: the zero-point term sum_g z[g, n] * R[g, m], accumulated in fp32 by the tensor core
           if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 15))) break;
           tc_fence_after();
-          const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
+          const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * kWarpTok);
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int ch = 0; ch < kChunks; ++ch) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(taddr + 32 * ch, r);
             tmem_wait_ld_dep(r);
@@ -475,7 +479,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[buf]);
-          if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
+          if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
         // the weight scale of the next group is loaded one group ahead as raw bf16 bits and converted only when it
         // is used, so its latency hides behind a drain instead of stalling the warp at the load
@@ -488,7 +492,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           tc_fence_after();
           const float s = bf16_bits_to_f32(s_bits) * wscale_fold;
           const float2 s2 = make_float2(s, s);
-          const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
+          const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * kWarpTok);
           // software-pipelined drain: chunk c+1 is in flight while chunk c is scaled, and the buffer goes back to
           // the MMA as soon as the last chunk is in registers
           uint32_t ra[32], rb[32];
@@ -500,22 +504,35 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
               acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
             }
           };
-          tmem_ld_32x32b_x32(taddr, ra);
-          tmem_wait_ld_dep(ra);
-          tmem_ld_32x32b_x32(taddr + 32, rb);
-          scale_chunk(ra, 0);
-          tmem_wait_ld_dep(rb);
-          tmem_ld_32x32b_x32(taddr + 64, ra);
-          scale_chunk(rb, 1);
-          tmem_wait_ld_dep(ra);
-          tmem_ld_32x32b_x32(taddr + 96, rb);
-          scale_chunk(ra, 2);
-          tmem_wait_ld_dep(rb);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tmem_empty[buf]);
-          scale_chunk(rb, 3);
-          if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
+          if constexpr (kChunks == 4) {
+            tmem_ld_32x32b_x32(taddr, ra);
+            tmem_wait_ld_dep(ra);
+            tmem_ld_32x32b_x32(taddr + 32, rb);
+            scale_chunk(ra, 0);
+            tmem_wait_ld_dep(rb);
+            tmem_ld_32x32b_x32(taddr + 64, ra);
+            scale_chunk(rb, 1);
+            tmem_wait_ld_dep(ra);
+            tmem_ld_32x32b_x32(taddr + 96, rb);
+            scale_chunk(ra, 2);
+            tmem_wait_ld_dep(rb);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+            scale_chunk(rb, 3);
+          } else {
+            // two chunks: both loads in flight together, the buffer back to the MMA before the math
+            tmem_ld_32x32b_x32(taddr, ra);
+            tmem_ld_32x32b_x32(taddr + 32, rb);
+            tmem_wait_ld_dep(ra);
+            tmem_wait_ld_dep(rb);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+            scale_chunk(ra, 0);
+            scale_chunk(rb, 1);
+          }
+          if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
         if (!ok) break;
         stage_sa();
@@ -536,7 +553,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             const int x0 = nt * kBW + (kPair ? (quad & 2) : quad) * 32;
             const int pr = e >> 1;
 #pragma unroll
-            for (int pass = 0; pass < 2; ++pass, ++box_pass) {
+            for (int pass = 0; pass < kWarpTok / 64; ++pass, ++box_pass) {
               const uint32_t par = box_pass & 1u;
               if (issuer) {
                 if (lane == 0) {
@@ -577,7 +594,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // column n of the output for tokens m0..m0+127: one pointer walked down the rows
           __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
 #pragma unroll
-          for (int j4 = 0; j4 < 32; ++j4) {
+          for (int j4 = 0; j4 < kWarpTok / 4; ++j4) {
             const float4 c = *reinterpret_cast<const float4*>(sa_stage + 4 * j4);
             const int m = m0 + 4 * j4;
             const float v0 = __fmaf_rn(acc[2 * j4].x, c.x, bias), v1 = __fmaf_rn(acc[2 * j4].y, c.y, bias);
@@ -600,11 +617,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 8))) break;
         tc_fence_after();
         const float sb = n_ok ? args.sb[n] * wscale_fold : 0.0f;
-        const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * 128);
+        const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * kWarpTok);
         __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
         stage_sa();
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < kChunks; ++ch) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + 32 * ch, r);
           tmem_wait_ld_dep(r);
@@ -631,7 +648,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tmem_empty[buf]);
-        if (++buf == 2) { buf = 0; buf_phase ^= 1u; }
+        if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
       }
     }
   }
