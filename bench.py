@@ -292,25 +292,49 @@ def run_ours(args, world, rank, local):
     ops_per_step = 2.0 * m * n * k
     value = ops_per_step * args.steps * world / (total_ms / 1e3) / 1e12
 
-    # e2e through the public API with host buffers: H2D of x from pinned memory, the op, D2H of the output
+    # e2e through the public API with host buffers, as a pipeline: every step copies its x from pinned host memory
+    # (copy stream), runs the op (compute stream; L2 flushed first), and copies its output back to pinned host memory
+    # (a second copy stream).  Double buffers let step i's output copy overlap step i+1's input copy and op (the copy
+    # engines run both directions at once); every step's copies are inside the timed region.
     x_host = x.cpu().pin_memory()
-    y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
-    xin = torch.empty_like(x)
+    y_hosts = [torch.empty(m, n, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    x_devs = [torch.empty_like(x) for _ in range(2)]
+    s_in, s_c, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     e2e_steps = max(3, min(args.steps, 50))
-    for _ in range(2):
-        xin.copy_(x_host, non_blocking=True)
-        y_host.copy_(public(xin), non_blocking=True)
+
+    def pipeline(nsteps):
+        ev_in = [torch.cuda.Event() for _ in range(nsteps)]
+        ev_c = [torch.cuda.Event() for _ in range(nsteps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(s_in)
+        s_c.wait_event(t0)
+        s_out.wait_event(t0)
+        for i in range(nsteps):
+            b = i % 2
+            if i >= 2:
+                s_in.wait_event(ev_c[i - 2])            # step i-2's op has read this input buffer
+            with torch.cuda.stream(s_in):
+                x_devs[b].copy_(x_host, non_blocking=True)
+                ev_in[i].record(s_in)
+            s_c.wait_event(ev_in[i])
+            with torch.cuda.stream(s_c):
+                flush.zero_()
+                y = public(x_devs[b])
+                ev_c[i].record(s_c)
+            s_out.wait_event(ev_c[i])
+            with torch.cuda.stream(s_out):
+                y_hosts[b].copy_(y, non_blocking=True)   # y_hosts[b]'s previous copy is earlier on this stream
+                y.record_stream(s_out)
+        s_out.wait_event(ev_c[-1])
+        t1.record(s_out)
+        return t0, t1
+
+    pipeline(2)
     torch.cuda.synchronize()
-    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(e2e_steps)]
     barrier(world)
-    for i in range(e2e_steps):
-        flush.zero_()
-        ee[i][0].record(stream)
-        xin.copy_(x_host, non_blocking=True)
-        y_host.copy_(public(xin), non_blocking=True)
-        ee[i][1].record(stream)
+    t0, t1 = pipeline(e2e_steps)
     torch.cuda.synchronize()
-    e2e_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in ee), world) / e2e_steps
+    e2e_ms = allreduce_max(t0.elapsed_time(t1), world) / e2e_steps
     e2e_val = ops_per_step * world / (e2e_ms / 1e3) / 1e12
 
     # library int8 GEMM on the same shape, for context (cuBLASLt through torch._int_mm)
@@ -371,8 +395,10 @@ def run_ours(args, world, rank, local):
         "library_int8_gemm": lib_int8,
         "e2e": {"value": e2e_val, "unit": "TOPS", "ms_per_step": e2e_ms, "h2d_bytes_per_step": m * k * 2,
                 "d2h_bytes_per_step": m * n * 2,
-                "path": "ops.w4a8_affine_linear (C ABI cq_linear_w4a8_affine) with pinned host buffers"
-                        if args.workload != "w4a4" else "ops.convrot_w4a4_linear (C ABI cq_linear_convrot_w4a4)"},
+                "path": ("ops.w4a8_affine_linear (C ABI cq_linear_w4a8_affine)" if args.workload != "w4a4" else
+                         "ops.convrot_w4a4_linear (C ABI cq_linear_convrot_w4a4)") +
+                        " with pinned host buffers; each step's input copy, op (after an L2 flush) and output copy run "
+                        "as a three-stream pipeline over the steps"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
