@@ -777,6 +777,19 @@ def run_sweep(args, world, rank, local):
         ms = timed(lambda: ops.convrot_w4a4_linear(x, qw, sw, None, convrot_groupsize=rot), args.steps)
         emit({"case": "convrot_w4a4_linear", "M": m, "N": n, "K": k, "rot": rot, "ms": ms,
               "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12})
+    # SwiGLU epilogue variant: the N=12288 up projection with silu(y[:, :6144]) * y[:, 6144:] formed in the epilogue
+    qw, sw = ops.quantize_convrot_w4a4_weight(w, 256)
+    qg, sg, _ = ops.prepare_swiglu_output_weight(qw, sw)
+    ms = timed(lambda: ops.convrot_w4a4_linear_swiglu(x, qg, sg, None, convrot_groupsize=256), args.steps)
+    emit({"case": "convrot_w4a4_linear_swiglu_epilogue", "M": m, "N": n, "K": k, "rot": 256, "out_cols": n // 2,
+          "ms": ms, "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12})
+    def unfused():
+        y = ops.convrot_w4a4_linear(x, qw, sw, None, convrot_groupsize=256)
+        return torch.nn.functional.silu(y[:, :n // 2]) * y[:, n // 2:]
+
+    ms = timed(unfused, args.steps)
+    emit({"case": "convrot_w4a4_linear_then_torch_swiglu", "M": m, "N": n, "K": k, "rot": 256, "out_cols": n // 2,
+          "ms": ms, "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12})
     kd, nd = 6144, 3072   # down projection after SwiGLU: h [M, 2*6144] -> silu(g)*u -> [M, 6144] @ W^T
     wd = torch.randn(nd, kd, generator=gen, device=dev) * 0.02
     qd, sd = ops.quantize_convrot_w4a4_weight(wd, 256)

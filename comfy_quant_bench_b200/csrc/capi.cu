@@ -277,6 +277,31 @@ int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int r
   return cq_gemm_rowcol(w.xq, 1, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream);
 }
 
+int cq_gemm_rowcol_swiglu(const int8_t* a, const float* sa, const void* b_glu, const float* sb, const void* bias,
+                          void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (N % 128 != 0) return CQ_ERR_SHAPE;            // whole 64-gate + 64-up row tiles
+  if (int e = check_gemm(a, b_glu, out, M, N, K)) return e;
+  if (M == 0) return CQ_OK;
+  if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
+  if (int dv = check_device()) return dv;
+  return cq::launch_gemm_rowcol_glu(a, sa, b_glu, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
+                                    static_cast<int>(K), static_cast<cudaStream_t>(stream));
+}
+
+int cq_linear_convrot_w4a4_swiglu(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int act_bits,
+                                  const void* qweight_glu, const float* wscale_glu, const void* bias_glu, void* out,
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
+  if (act_bits != 4 && act_bits != 8) return CQ_ERR_ARG;
+  if (M == 0) return CQ_OK;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  const int mode = act_bits == 4 ? CQ_ACT_INT4_ROW : CQ_ACT_INT8_ROW;
+  if (int e = cq_rotquant(x, M, K, rot_group, 0, mode, 0, w.mpad, CQ_Q_INT8_CODES | CQ_Q_KPERM, w.xq, w.sx, nullptr,
+                          stream))
+    return e;
+  return cq_gemm_rowcol_swiglu(w.xq, w.sx, qweight_glu, wscale_glu, bias_glu, out, M, N, K, stream);
+}
+
 int cq_gemm_affine_peers(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                          const void* s_bf16, const void* zt_bf16, const void* bias, void* const* outs, int n_outs,
                          int64_t col0, int64_t ldo, int64_t M, int64_t N, int64_t K, int group, void* stream) {

@@ -58,9 +58,10 @@ enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 
 // shared-memory plan per epilogue and weight format.  The affine kernel trades one TMA stage for the output
 // staging buffers of its asynchronous (TMA) output stores.
-template <int EPI, int BFMT>
+template <int EPI, int BFMT, bool GLU = false>
 struct SmemPlan {
-  static constexpr int kStages = (EPI == EPI_AFFINE) ? (kBT == 256 ? 3 : 4) : (kBT == 256 ? 4 : 6);   // TMA ring
+  // TMA ring depth (the SwiGLU-output kernel gives one stage to its gate/up exchange buffers)
+  static constexpr int kStages = (EPI == EPI_AFFINE || GLU) ? (kBT == 256 ? 3 : 4) : (kBT == 256 ? 4 : 6);
   static constexpr int kWStageBytes = (BFMT == BF_S8) ? kWuBytes : kWpBytes;   // weight bytes in the TMA ring
   static constexpr int kTmaStageBytes = kXBytes + kWStageBytes;
   static constexpr int kConvBytes = (BFMT == BF_S8) ? 0 : kConvStages * kWuBytes;
@@ -70,7 +71,11 @@ struct SmemPlan {
   static constexpr int kOutStage = kSaStage + kSaBytes;           // output staging: 64 tokens x 32 columns bf16
   static constexpr int kOutWarpBytes = 64 * 32 * 2;               //   per epilogue warp (affine only)
   static constexpr int kOutBytes = (EPI == EPI_AFFINE) ? 8 * kOutWarpBytes : 0;
-  static constexpr int kBytes = kOutStage + kOutBytes + 1024 /*align slack*/;
+  // SwiGLU output: per (gate warp, up warp) pair, two 32-token x 32-row fp32 exchange buffers
+  static constexpr int kXchg = kOutStage + kOutBytes;
+  static constexpr int kXchgPairBytes = 2 * 32 * 32 * 4;
+  static constexpr int kXchgBytes = GLU ? 4 * kXchgPairBytes : 0;
+  static constexpr int kBytes = kXchg + kXchgBytes + 1024 /*align slack*/;
 };
 
 // Output tensor maps of the affine epilogue: map i covers buffer i ([M, ldo] bf16); every staged output box is
@@ -163,12 +168,13 @@ __device__ __forceinline__ uint4 unpack16(uint2 p) {
                     prmt(lo1, hi1, 0x7362u));
 }
 
-template <int EPI, int BFMT, bool KPERM>
+template <int EPI, int BFMT, bool KPERM, bool GLU = false>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
             const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_z,
             const __grid_constant__ OutMaps tm_out, const GemmArgs args) {
-  using P = SmemPlan<EPI, BFMT>;
+  using P = SmemPlan<EPI, BFMT, GLU>;
+  static_assert(!GLU || (EPI == EPI_ROWCOL && BFMT == BF_S4), "the SwiGLU output is a row/col W4A4 epilogue");
   constexpr int kTmaStages = P::kStages;
   constexpr bool kConv = BFMT != BF_S8;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -186,8 +192,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   uint64_t* zt_full = tmem_empty + kNumBufs;   // affine: per converter pair, the TMA load of its zero-point operand
   uint64_t* box_free = zt_full + kConvStages;   // affine, 64-column boxes: per epilogue warp pair, staging free
   uint64_t* box_full = box_free + 4;            //   and both halves of the box written
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(box_full + 4);
-  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 8) * 8 + 8 <= P::kSaStage - P::kData,
+  uint64_t* x_full = box_full + 4;              // SwiGLU output: per pair and exchange buffer, up values written
+  uint64_t* x_free = x_full + 8;                //   and read by the gate warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(x_free + 8);
+  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 8 + 16) * 8 + 8 <= P::kSaStage - P::kData,
                 "the barriers, the TMEM address and the abort flag fit the region before the scale staging");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -227,6 +235,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     for (int b = 0; b < kNumBufs; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 8);
+    }
+    for (int p = 0; p < 8; ++p) {
+      mbar_init(&x_full[p], 1);
+      mbar_init(&x_free[p], 1);
     }
     for (int p = 0; p < 4; ++p) {
       mbar_init(&box_free[p], 1);
@@ -425,6 +437,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     // this warp's 128 token scales for the store phase (read back as broadcast float4 loads)
     float* sa_stage = reinterpret_cast<float*>(smem + P::kSaStage) + e * kWarpTok;
     uint32_t box_pass = 0;                // output store passes so far (phase of this warp pair's box barriers)
+    uint32_t xchunk = 0;                  // SwiGLU output: exchanged chunks so far (buffer and phase)
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
@@ -618,6 +631,52 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         tc_fence_after();
         const float sb = n_ok ? args.sb[n] * wscale_fold : 0.0f;
         const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * kWarpTok);
+        if constexpr (GLU) {
+          // SwiGLU output: the tile's weight rows are 64 gate rows (quadrants 0, 1) then the 64 matching up rows
+          // (quadrants 2, 3), so out[m, 64 nt + r] = bf16(bf16(silu(gate)) * up) with gate = bf16(row r's value)
+          // and up = bf16(row 64 + r's value), the roundings of torch's silu and mul on the bf16 linear output.
+          // Each up warp hands its 32-token chunks to the gate warp of the same rows and tokens through shared
+          // memory.
+          stage_sa();
+          const bool up = quad >= 2;
+          const int pr = half * 2 + (quad & 1);
+          float* xbuf = reinterpret_cast<float*>(smem + P::kXchg + pr * P::kXchgPairBytes);
+          const int ncols = N / 2;
+          const int j = nt * (kBW / 2) + (quad & 1) * 32 + lane;   // output column of a gate row
+#pragma unroll 1
+          for (int ch = 0; ch < kChunks; ++ch, ++xchunk) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr + 32 * ch, r);
+            tmem_wait_ld_dep(r);
+            const int xb = static_cast<int>(xchunk & 1u);
+            const uint32_t xpar = (xchunk >> 1) & 1u;
+            float* xc = xbuf + xb * 1024;
+            if (up) {
+              if (!(ok = mbar_wait(&x_free[2 * pr + xb], xpar ^ 1u, abort_flag, 20))) break;
+#pragma unroll
+              for (int t = 0; t < 32; ++t) {
+                const float v = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb), sa_stage[32 * ch + t], bias);
+                xc[t * 32 + lane] = bf16_round(v);
+              }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&x_full[2 * pr + xb]);
+            } else {
+              if (!(ok = mbar_wait(&x_full[2 * pr + xb], xpar, abort_flag, 21))) break;
+#pragma unroll
+              for (int t = 0; t < 32; ++t) {
+                const int m = m0 + 32 * ch + t;
+                const float g = bf16_round(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb),
+                                                     sa_stage[32 * ch + t], bias));
+                const float silu = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+                const float o = __fmul_rn(silu, xc[t * 32 + lane]);
+                if (m < M && j < ncols) args.out[static_cast<int64_t>(m) * ncols + j] = __float2bfloat16_rn(o);
+              }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&x_free[2 * pr + xb]);
+            }
+          }
+          if (!ok) break;
+        } else {
         __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
         stage_sa();
 #pragma unroll 1
@@ -644,6 +703,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
               }
             }
           }
+        }
         }
         tc_fence_before();
         __syncwarp();
@@ -740,11 +800,11 @@ struct OutSpec {
   int64_t ldo;
 };
 
-template <int EPI, int BFMT, bool KPERM>
+template <int EPI, int BFMT, bool KPERM, bool GLU = false>
 static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args, cudaStream_t st,
                          const OutSpec* outs = nullptr) {
-  auto kern = gemm_kernel<EPI, BFMT, KPERM>;
-  constexpr int smem_bytes = SmemPlan<EPI, BFMT>::kBytes;
+  auto kern = gemm_kernel<EPI, BFMT, KPERM, GLU>;
+  constexpr int smem_bytes = SmemPlan<EPI, BFMT, GLU>::kBytes;
   static bool configured = false;
   static bool regs_ok = false;
   if (!configured) {
@@ -829,6 +889,19 @@ int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void
   if (b_format == CQ_B_INT8) return launch_gemm_t<EPI_ROWCOL, BF_S8, false>(a, b, nullptr, g, st);
   if (a_kperm) return launch_gemm_t<EPI_ROWCOL, BF_S4, true>(a, b, nullptr, g, st);
   return launch_gemm_t<EPI_ROWCOL, BF_S4, false>(a, b, nullptr, g, st);
+}
+
+// W4A4 row/col GEMM with the SwiGLU output: b holds the weight rows tile-interleaved (each 128-row tile = 64 gate
+// rows then their 64 up rows); out is bf16 [M, N / 2].
+int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
+                           void* out, int M, int N, int K, cudaStream_t st) {
+  GemmArgs g{};
+  g.sa = sa;
+  g.sb = sb;
+  g.bias = static_cast<const __nv_bfloat16*>(bias);
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.M = M; g.N = N; g.K = K;
+  return launch_gemm_t<EPI_ROWCOL, BF_S4, true, true>(a, b, nullptr, g, st);
 }
 
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,

@@ -60,6 +60,8 @@ cudaError_t launch_weight_rotquant(int rot, bool w_bf16, int mode, const RotQuan
 cudaError_t launch_unpack_int4(const void* src, int64_t n_bytes, void* dst, cudaStream_t st);
 int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
                        const void* bias, void* out, int M, int N, int K, cudaStream_t st);
+int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
+                           void* out, int M, int N, int K, cudaStream_t st);
 constexpr int kMaxOutBuffers = 8;   // output buffers of one column-parallel affine launch
 
 // outs != nullptr: write the result into n_outs (<= kMaxOutBuffers) buffers of [M, ldo] bf16 at columns [col0, col0 + N)

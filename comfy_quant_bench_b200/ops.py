@@ -514,3 +514,50 @@ def gemm_affine_into(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qw
     _lib.call("cq_gemm_affine_peers", _ptr(a), int(bool(a_kperm)), _ptr(sa), _ptr(gsplit), _ptr(qweight),
               _ptr(scale), _ptr(zeros_prepared), _ptr(_bias_bf16(bias)), arr, cnt, int(col0), int(ldo), m, n, k, 128,
               _stream(dev))
+
+
+# ----------------------------------------------------------------------------------------------
+# ConvRot W4A4 linear with the SwiGLU output fused into the GEMM epilogue (epilogue variant)
+# ----------------------------------------------------------------------------------------------
+
+def swiglu_output_rows(n: int, device=None) -> torch.Tensor:
+    """Row order of a SwiGLU-output weight: each 128-row tile holds 64 gate rows (of y[:, :n/2]) then the matching
+    64 up rows (of y[:, n/2:]); entry p is the original row."""
+    if n % 128:
+        raise ValueError(f"the SwiGLU output needs N % 128 == 0, got {n}")
+    p = torch.arange(n, device=device)
+    t, r = p // 128, p % 128
+    return torch.where(r < 64, 64 * t + r, n // 2 + 64 * t + (r - 64))
+
+
+def prepare_swiglu_output_weight(qweight: torch.Tensor, wscales: torch.Tensor, bias: torch.Tensor | None = None):
+    """ConvRot W4A4 weight (packed [N, K/2], scales [N], bias [N]) in the tile-interleaved row order of
+    ``convrot_w4a4_linear_swiglu``, built once per weight."""
+    n = qweight.shape[0]
+    idx = swiglu_output_rows(n, qweight.device)
+    qw = qweight.index_select(0, idx).contiguous()
+    ws = wscales.float().reshape(-1).index_select(0, idx.to(wscales.device)).contiguous()
+    b = None if bias is None else _bias_bf16(bias).index_select(0, idx.to(bias.device)).contiguous()
+    return qw, ws, b
+
+
+def convrot_w4a4_linear_swiglu(x: torch.Tensor, qweight_glu: torch.Tensor, wscales_glu: torch.Tensor,
+                               bias_glu: torch.Tensor | None = None, convrot_groupsize: int = 256,
+                               linear_dtype: str = "int4") -> torch.Tensor:
+    """silu(y[..., :N/2]) * y[..., N/2:] of the ConvRot W4A4 linear y = convrot_w4a4_linear(x, W, ...), with the
+    SwiGLU computed in the GEMM's epilogue (weights from ``prepare_swiglu_output_weight``): [..., N/2] bf16."""
+    if linear_dtype not in {"int4", "int8"}:
+        raise ValueError(f"ConvRot W4A4 linear_dtype must be 'int4' or 'int8', got {linear_dtype!r}")
+    k = x.shape[-1]
+    if k != qweight_glu.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight_glu.shape[-1] * 2}")
+    dev = _require_cuda(x, qweight_glu, wscales_glu, bias_glu)
+    x2 = _as2d(x)
+    m, n = x2.shape[0], qweight_glu.shape[0]
+    out = torch.empty(m, n // 2, dtype=torch.bfloat16, device=dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    _lib.call("cq_linear_convrot_w4a4_swiglu", _ptr(x2), m, k, n, _check_rot(convrot_groupsize),
+              4 if linear_dtype == "int4" else 8, _ptr(qweight_glu), _ptr(wscales_glu.float().contiguous()),
+              _ptr(_bias_bf16(bias_glu)), _ptr(out), wp, wn, _stream(dev))
+    return out.reshape(*x.shape[:-1], n // 2)

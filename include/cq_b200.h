@@ -200,6 +200,22 @@ CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int ro
                    void* stream);
 
 /*
+ * W4A4 row/col GEMM / ConvRot W4A4 linear with the SwiGLU output fused into the epilogue (the
+ * epilogue variant: silu(y[:, :N/2]) * y[:, N/2:] of the N-column linear y):
+ *   out[m, j] = bf16( bf16(silu(y[m, j])) * y[m, N/2 + j] ),  y = bf16(linear output),  out bf16 [M, N/2]
+ * (torch's silu and mul on the bf16 linear output).  The weight rows, scales and bias are passed tile-interleaved:
+ * row p of b_glu / sb / bias is original row (p / 128) * 64 + p % 128 for p % 128 < 64 (gate) and
+ * N/2 + (p / 128) * 64 + p % 128 - 64 otherwise (up); ops.prepare_swiglu_output_weight builds them once.
+ * N % 128 == 0.  a: int4 values held as int8 codes with CQ_Q_KPERM; b: packed signed int4.  No counterpart in the
+ * reference, which applies the activation to the linear's output afterwards.
+ */
+CQ_API int cq_gemm_rowcol_swiglu(const int8_t* a, const float* sa, const void* b_glu, const float* sb,
+                                 const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream);
+CQ_API int cq_linear_convrot_w4a4_swiglu(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int act_bits,
+                                         const void* qweight_glu, const float* wscale_glu, const void* bias_glu,
+                                         void* out, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Column-parallel forms of cq_gemm_affine / cq_linear_w4a8_affine: the launch computes N output columns (one rank's
  * shard of a layer with ldo = N_total outputs) and writes them, as they are produced, into each of the n_outs
  * (1..8) output buffers outs[i] (bf16 [M, ldo], 16-byte aligned) at columns [col0, col0 + N).  Passing every

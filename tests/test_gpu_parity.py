@@ -461,3 +461,30 @@ def test_affine_linear_into_rejects_bad_layouts(ops):
         ops.w4a8_affine_linear_into(x, qw, s, zt, None, [out], 4, 512)
     with pytest.raises(_lib.CQError):           # more than 8 buffers
         ops.w4a8_affine_linear_into(x, qw, s, zt, None, [out] * 9, 0, 512)
+
+
+@pytest.mark.parametrize("m,n,k,rot,dtype", [(300, 384, 1024, 256, "int4"), (4096, 12288, 3072, 64, "int4"),
+                                             (77, 256, 512, 16, "int8")])
+def test_convrot_w4a4_swiglu_output_matches_torch_composite(ops, m, n, k, rot, dtype):
+    """The SwiGLU output fused into the W4A4 GEMM's epilogue equals torch's silu(y[:, :N/2]) * y[:, N/2:] on the
+    bf16 output of the plain linear (same codes, same int32 sums, the same two bf16 roundings)."""
+    import torch.nn.functional as F
+    x = bf16_dev(ref.synth_activations(m, k, seed=m + n))
+    w = torch.from_numpy(ref.synth_weight(n, k, seed=n)).cuda()
+    qw, sw = ops.quantize_convrot_w4a4_weight(w, rot)
+    bias = bf16_dev(ref.synth_bias(n, seed=3))
+    y = ops.convrot_w4a4_linear(x, qw, sw, bias, convrot_groupsize=rot, linear_dtype=dtype)
+    want = F.silu(y[:, : n // 2]) * y[:, n // 2:]
+    qg, sg, bg = ops.prepare_swiglu_output_weight(qw, sw, bias)
+    got = ops.convrot_w4a4_linear_swiglu(x, qg, sg, bg, convrot_groupsize=rot, linear_dtype=dtype)
+    _check_status()
+    assert got.shape == (m, n // 2)
+    g, w_ = got.float(), want.float()
+    assert float((g - w_).abs().max()) <= float(w_.abs().max()) * 2.0 ** -7
+    assert float((got != want).float().mean()) <= 1e-3
+
+
+def test_swiglu_output_rows_interleave_tiles(ops):
+    idx = ops.swiglu_output_rows(256)
+    assert idx[:64].tolist() == list(range(64)) and idx[64:128].tolist() == list(range(128, 192))
+    assert idx[128:192].tolist() == list(range(64, 128)) and idx[192:].tolist() == list(range(192, 256))
