@@ -667,7 +667,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
                 const int m = m0 + 32 * ch + t;
                 const float g = bf16_round(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb),
                                                      sa_stage[32 * ch + t], bias));
-                const float silu = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+                // silu with the hardware exponential and an approximate divide: a few fp32 ulp from torch's
+                // expf/IEEE-divide form, which the bf16 rounding that follows hides except at rare rounding ties
+                const float silu = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
                 const float o = __fmul_rn(silu, xc[t * 32 + lane]);
                 if (m < M && j < ncols) args.out[static_cast<int64_t>(m) * ncols + j] = __float2bfloat16_rn(o);
               }
