@@ -60,8 +60,8 @@ enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 // staging buffers of its asynchronous (TMA) output stores.
 template <int EPI, int BFMT, bool GLU = false>
 struct SmemPlan {
-  // TMA ring depth (the SwiGLU-output kernel gives one stage to its gate/up exchange buffers)
-  static constexpr int kStages = (EPI == EPI_AFFINE || GLU) ? (kBT == 256 ? 3 : 4) : (kBT == 256 ? 4 : 6);
+  // TMA ring depth
+  static constexpr int kStages = (EPI == EPI_AFFINE) ? (kBT == 256 ? 3 : 4) : (kBT == 256 ? 4 : 6);
   static constexpr int kWStageBytes = (BFMT == BF_S8) ? kWuBytes : kWpBytes;   // weight bytes in the TMA ring
   static constexpr int kTmaStageBytes = kXBytes + kWStageBytes;
   static constexpr int kConvBytes = (BFMT == BF_S8) ? 0 : kConvStages * kWuBytes;
@@ -71,11 +71,7 @@ struct SmemPlan {
   static constexpr int kOutStage = kSaStage + kSaBytes;           // output staging: 64 tokens x 32 columns bf16
   static constexpr int kOutWarpBytes = 64 * 32 * 2;               //   per epilogue warp (affine only)
   static constexpr int kOutBytes = (EPI == EPI_AFFINE) ? 8 * kOutWarpBytes : 0;
-  // SwiGLU output: per (gate warp, up warp) pair, two 32-token x 32-row fp32 exchange buffers
-  static constexpr int kXchg = kOutStage + kOutBytes;
-  static constexpr int kXchgPairBytes = 2 * 32 * 32 * 4;
-  static constexpr int kXchgBytes = GLU ? 4 * kXchgPairBytes : 0;
-  static constexpr int kBytes = kXchg + kXchgBytes + 1024 /*align slack*/;
+  static constexpr int kBytes = kOutStage + kOutBytes + 1024 /*align slack*/;
 };
 
 // Output tensor maps of the affine epilogue: map i covers buffer i ([M, ldo] bf16); every staged output box is
@@ -192,10 +188,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   uint64_t* zt_full = tmem_empty + kNumBufs;   // affine: per converter pair, the TMA load of its zero-point operand
   uint64_t* box_free = zt_full + kConvStages;   // affine, 64-column boxes: per epilogue warp pair, staging free
   uint64_t* box_full = box_free + 4;            //   and both halves of the box written
-  uint64_t* x_full = box_full + 4;              // SwiGLU output: per pair and exchange buffer, up values written
-  uint64_t* x_free = x_full + 8;                //   and read by the gate warp
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(x_free + 8);
-  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 8 + 16) * 8 + 8 <= P::kSaStage - P::kData,
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(box_full + 4);
+  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 8) * 8 + 8 <= P::kSaStage - P::kData,
                 "the barriers, the TMEM address and the abort flag fit the region before the scale staging");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -235,10 +229,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     for (int b = 0; b < kNumBufs; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 8);
-    }
-    for (int p = 0; p < 8; ++p) {
-      mbar_init(&x_full[p], 1);
-      mbar_init(&x_free[p], 1);
     }
     for (int p = 0; p < 4; ++p) {
       mbar_init(&box_free[p], 1);
@@ -437,7 +427,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     // this warp's 128 token scales for the store phase (read back as broadcast float4 loads)
     float* sa_stage = reinterpret_cast<float*>(smem + P::kSaStage) + e * kWarpTok;
     uint32_t box_pass = 0;                // output store passes so far (phase of this warp pair's box barriers)
-    uint32_t xchunk = 0;                  // SwiGLU output: exchanged chunks so far (buffer and phase)
     int buf = 0;
     uint32_t buf_phase = 0;
     bool ok = true;
@@ -632,52 +621,41 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         const float sb = n_ok ? args.sb[n] * wscale_fold : 0.0f;
         const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kBT + half * kWarpTok);
         if constexpr (GLU) {
-          // SwiGLU output: the tile's weight rows are 64 gate rows (quadrants 0, 1) then the 64 matching up rows
-          // (quadrants 2, 3), so out[m, 64 nt + r] = bf16(bf16(silu(gate)) * up) with gate = bf16(row r's value)
-          // and up = bf16(row 64 + r's value), the roundings of torch's silu and mul on the bf16 linear output.
-          // Each up warp hands its 32-token chunks to the gate warp of the same rows and tokens through shared
-          // memory.
+          // SwiGLU output: each 32-row lane quadrant holds 16 gate rows (lanes 0-15, of y[:, :N/2]) and their 16
+          // up rows (lanes 16-31, of y[:, N/2:]), so lanes l and l ^ 16 carry the two halves of one output
+          // column.  out[m, c] = bf16(bf16(silu(gate)) * up) with gate and up the bf16-rounded linear outputs,
+          // the roundings of torch's silu and mul on the bf16 linear output.  Per 32-token chunk, lanes 0-15
+          // write tokens 0-15 and lanes 16-31 tokens 16-31: one shuffle per token pair hands each lane the
+          // other half it needs.
           stage_sa();
-          const bool up = quad >= 2;
-          const int pr = half * 2 + (quad & 1);
-          float* xbuf = reinterpret_cast<float*>(smem + P::kXchg + pr * P::kXchgPairBytes);
+          const bool gate = lane < 16;
           const int ncols = N / 2;
-          const int j = nt * (kBW / 2) + (quad & 1) * 32 + lane;   // output column of a gate row
+          const int j = nt * (kBW / 2) + quad * 16 + (lane & 15);   // output column of this lane's row pair
+          const int tb = gate ? 0 : 16;                              // first token of this lane's 16
 #pragma unroll 1
-          for (int ch = 0; ch < kChunks; ++ch, ++xchunk) {
+          for (int ch = 0; ch < kChunks; ++ch) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(taddr + 32 * ch, r);
             tmem_wait_ld_dep(r);
-            const int xb = static_cast<int>(xchunk & 1u);
-            const uint32_t xpar = (xchunk >> 1) & 1u;
-            float* xc = xbuf + xb * 1024;
-            if (up) {
-              if (!(ok = mbar_wait(&x_free[2 * pr + xb], xpar ^ 1u, abort_flag, 20))) break;
+            float v[32];
 #pragma unroll
-              for (int t = 0; t < 32; ++t) {
-                const float v = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb), sa_stage[32 * ch + t], bias);
-                xc[t * 32 + lane] = bf16_round(v);
-              }
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&x_full[2 * pr + xb]);
-            } else {
-              if (!(ok = mbar_wait(&x_full[2 * pr + xb], xpar, abort_flag, 21))) break;
+            for (int t = 0; t < 32; ++t)
+              v[t] = bf16_round(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb), sa_stage[32 * ch + t],
+                                          bias));
 #pragma unroll
-              for (int t = 0; t < 32; ++t) {
-                const int m = m0 + 32 * ch + t;
-                const float g = bf16_round(__fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb),
-                                                     sa_stage[32 * ch + t], bias));
-                // silu with the hardware exponential and an approximate divide: a few fp32 ulp from torch's
-                // expf/IEEE-divide form, which the bf16 rounding that follows hides except at rare rounding ties
-                const float silu = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
-                const float o = __fmul_rn(silu, xc[t * 32 + lane]);
-                if (m < M && j < ncols) args.out[static_cast<int64_t>(m) * ncols + j] = __float2bfloat16_rn(o);
-              }
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&x_free[2 * pr + xb]);
+            for (int k = 0; k < 16; ++k) {
+              // gate lanes send token 16 + k (the up lane's) and receive the up value of token k; up lanes
+              // send token k and receive the gate value of token 16 + k
+              const float other = __shfl_xor_sync(0xffffffffu, gate ? v[16 + k] : v[k], 16);
+              const float g = gate ? v[k] : other;
+              const float u = gate ? other : v[16 + k];
+              // silu with the hardware exponential and an approximate divide: a few fp32 ulp from torch's
+              // expf/IEEE-divide form, which the bf16 rounding that follows hides except at rare rounding ties
+              const float silu = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
+              const int m = m0 + 32 * ch + tb + k;
+              if (m < M) args.out[static_cast<int64_t>(m) * ncols + j] = __float2bfloat16_rn(__fmul_rn(silu, u));
             }
           }
-          if (!ok) break;
         } else {
         __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
         stage_sa();
@@ -893,8 +871,8 @@ int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void
   return launch_gemm_t<EPI_ROWCOL, BF_S4, false>(a, b, nullptr, g, st);
 }
 
-// W4A4 row/col GEMM with the SwiGLU output: b holds the weight rows tile-interleaved (each 128-row tile = 64 gate
-// rows then their 64 up rows); out is bf16 [M, N / 2].
+// W4A4 row/col GEMM with the SwiGLU output: b holds the weight rows interleaved in groups of 32 (16 gate rows, then
+// their 16 up rows); out is bf16 [M, N / 2].
 int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
                            void* out, int M, int N, int K, cudaStream_t st) {
   GemmArgs g{};

@@ -521,13 +521,14 @@ def gemm_affine_into(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qw
 # ----------------------------------------------------------------------------------------------
 
 def swiglu_output_rows(n: int, device=None) -> torch.Tensor:
-    """Row order of a SwiGLU-output weight: each 128-row tile holds 64 gate rows (of y[:, :n/2]) then the matching
-    64 up rows (of y[:, n/2:]); entry p is the original row."""
+    """Row order of a SwiGLU-output weight: each group of 32 rows holds 16 gate rows (of y[:, :n/2]) then the
+    matching 16 up rows (of y[:, n/2:]), so one TMEM lane quadrant of the GEMM holds both halves of 16 outputs;
+    entry p is the original row."""
     if n % 128:
         raise ValueError(f"the SwiGLU output needs N % 128 == 0, got {n}")
     p = torch.arange(n, device=device)
-    t, r = p // 128, p % 128
-    return torch.where(r < 64, 64 * t + r, n // 2 + 64 * t + (r - 64))
+    t, r = p // 32, p % 32
+    return torch.where(r < 16, 16 * t + r, n // 2 + 16 * t + (r - 16))
 
 
 def prepare_swiglu_output_weight(qweight: torch.Tensor, wscales: torch.Tensor, bias: torch.Tensor | None = None):

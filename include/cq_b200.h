@@ -203,9 +203,9 @@ CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int ro
  * W4A4 row/col GEMM / ConvRot W4A4 linear with the SwiGLU output fused into the epilogue (the
  * epilogue variant: silu(y[:, :N/2]) * y[:, N/2:] of the N-column linear y):
  *   out[m, j] = bf16( bf16(silu(y[m, j])) * y[m, N/2 + j] ),  y = bf16(linear output),  out bf16 [M, N/2]
- * (torch's silu and mul on the bf16 linear output).  The weight rows, scales and bias are passed tile-interleaved:
- * row p of b_glu / sb / bias is original row (p / 128) * 64 + p % 128 for p % 128 < 64 (gate) and
- * N/2 + (p / 128) * 64 + p % 128 - 64 otherwise (up); ops.prepare_swiglu_output_weight builds them once.
+ * (torch's silu and mul on the bf16 linear output).  The weight rows, scales and bias are passed interleaved in
+ * groups of 32: row p of b_glu / sb / bias is original row (p / 32) * 16 + p % 32 for p % 32 < 16 (gate) and
+ * N/2 + (p / 32) * 16 + p % 32 - 16 otherwise (up); ops.prepare_swiglu_output_weight builds them once.
  * N % 128 == 0.  a: int4 values held as int8 codes with CQ_Q_KPERM; b: packed signed int4.  No counterpart in the
  * reference, which applies the activation to the linear's output afterwards.
  */

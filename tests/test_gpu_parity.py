@@ -486,5 +486,6 @@ def test_convrot_w4a4_swiglu_output_matches_torch_composite(ops, m, n, k, rot, d
 
 def test_swiglu_output_rows_interleave_tiles(ops):
     idx = ops.swiglu_output_rows(256)
-    assert idx[:64].tolist() == list(range(64)) and idx[64:128].tolist() == list(range(128, 192))
-    assert idx[128:192].tolist() == list(range(64, 128)) and idx[192:].tolist() == list(range(192, 256))
+    assert idx[:16].tolist() == list(range(16)) and idx[16:32].tolist() == list(range(128, 144))
+    assert idx[32:48].tolist() == list(range(16, 32)) and idx[240:].tolist() == list(range(240, 256))
+    assert sorted(idx.tolist()) == list(range(256))
