@@ -767,7 +767,21 @@ def run_sweep(args, world, rank, local):
         byts = m * k * 2 + m * k + m * 4 + m * 2 * 64 * ((k // 128 + 31) // 32)
         emit({"case": "rotquant_int8_convrot256", "M": m, "K": k, "ms": ms, "gbs": byts / (ms / 1e3) / 1e9,
               "frac_of_hbm": byts / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        # the reference's packed-int4 quantizer (quantize_int4_rowwise_convrot64): codes [M, K/2] + scales [M]
+        ms = timed(lambda: ops.quantize_int4_rowwise_convrot64(x, 256), args.steps)
+        byts = m * k * 2 + m * k // 2 + m * 4
+        emit({"case": "rotquant_int4_packed_convrot256", "M": m, "K": k, "ms": ms, "gbs": byts / (ms / 1e3) / 1e9,
+              "frac_of_hbm": byts / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
         del x
+    # the fused SwiGLU quantizer (swiglu_quantize_int4_rowwise_convrot64) on h [M, 2 * 12288]
+    for m in (4096, 32768):
+        k = 12288
+        h = torch.randn(m, 2 * k, generator=gen, device=dev).to(torch.bfloat16)
+        ms = timed(lambda: ops.swiglu_quantize_int4_rowwise_convrot64(h), args.steps)
+        byts = m * 2 * k * 2 + m * k // 2 + m * 4
+        emit({"case": "swiglu_rotquant_int4_packed_convrot256", "M": m, "K": k, "ms": ms,
+              "gbs": byts / (ms / 1e3) / 1e9, "frac_of_hbm": byts / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        del h
     # --- W4A4 ConvRot linears: rotation groups and the SwiGLU prologue ---
     m, k, n = 4096, 3072, 12288
     w = torch.randn(n, k, generator=gen, device=dev) * 0.02

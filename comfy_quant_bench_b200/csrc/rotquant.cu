@@ -77,6 +77,12 @@ __device__ __forceinline__ void stages_cross(float (&v)[16], float* tile, int la
   __syncwarp();
 }
 
+// silu(g) * u of comfy-kitchen's fused SwiGLU quantizer, rounded once to bf16: g / (1 + exp(-g)) * u with the
+// hardware exponential and the approximate division its fast-math build uses (tools/ck_swiglu/swiglu_quant.cu:65)
+__device__ __forceinline__ float swiglu_fused(float g, float u) {
+  return bf16_round(__fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u));
+}
+
 __device__ __forceinline__ void load_bf16x16(const __nv_bfloat16* p, float (&v)[16]) {
   const uint4 a = *reinterpret_cast<const uint4*>(p);
   const uint4 b = *reinterpret_cast<const uint4*>(p + 8);
@@ -172,9 +178,12 @@ __global__ void __launch_bounds__(1024) rotquant_kernel(const RotQuantArgs args)
         load_bf16x16(hrow + K + e, u);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float sv = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i]))), u[i]);
-          // comfy-kitchen's fused quantizer rounds the product once to bf16; the per-group quantizer keeps fp32
-          v[s][i] = (MODE == MODE_ACT_INT4_GROUP) ? sv : bf16_round(sv);
+          // comfy-kitchen's fused per-token quantizer rounds the product once to bf16; the per-group quantizer
+          // keeps fp32.  Both take the hardware exponential; the fused one is built with fast-math division
+          // (tools/ck_swiglu/swiglu_quant.cu:65 with --use_fast_math), the per-group one divides exactly
+          // (experiments/qwen21-kernel/kernels/g64_quant.cu:47-48)
+          v[s][i] = (MODE == MODE_ACT_INT4_GROUP) ? __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, __expf(-g[i]))), u[i])
+                                                  : swiglu_fused(g[i], u[i]);
         }
       } else if constexpr (sizeof(IN_T) == 2) {
         load_bf16x16(static_cast<const __nv_bfloat16*>(args.x) + row * static_cast<int64_t>(K) + e, v[s]);
@@ -432,13 +441,27 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint3
   return prmt(prmt(a, b, 0x0040u), prmt(c, d, 0x0040u), 0x5410u);
 }
 
-// One lane's 16 stored columns (512j + 256h + 16c + [0, 16)) of both rows: codes, group sums.
+// eight int4 codes (bytes of w0, w1 in column order) as packed nibbles, the low nibble the even column
+__device__ __forceinline__ uint32_t pack_nibbles(uint32_t w0, uint32_t w1) {
+  uint32_t x0 = w0 & 0x0F0F0F0Fu, x1 = w1 & 0x0F0F0F0Fu;
+  x0 |= x0 >> 4;                               // bytes 0 and 2: (column 2i) | (column 2i + 1) << 4
+  x1 |= x1 >> 4;
+  return prmt(x0, x1, 0x6420u);
+}
+
+// One lane's 16 stored columns (512j + 256h + 16c + [0, 16)) of both rows: codes (int8 bytes, or packed int4
+// nibbles with `pack`), group sums.
 __device__ __forceinline__ void act8_emit(const RotQuantArgs& args, int64_t rA, bool storeB, int j, int lane,
-                                          bool valid, const uint32_t (&wa)[4], const uint32_t (&wb)[4]) {
+                                          bool valid, bool pack, const uint32_t (&wa)[4], const uint32_t (&wb)[4]) {
   const int K = args.K;
   const int e0 = 512 * j + 16 * lane;          // 256h + 16c == 16 * lane
   int8_t* q = static_cast<int8_t*>(args.q);
-  if (valid) {
+  if (valid && pack) {
+    const int64_t kh = K >> 1;
+    *reinterpret_cast<uint2*>(q + rA * kh + (e0 >> 1)) = make_uint2(pack_nibbles(wa[0], wa[1]), pack_nibbles(wa[2], wa[3]));
+    if (storeB)
+      *reinterpret_cast<uint2*>(q + (rA + 1) * kh + (e0 >> 1)) = make_uint2(pack_nibbles(wb[0], wb[1]), pack_nibbles(wb[2], wb[3]));
+  } else if (valid) {
     *reinterpret_cast<uint4*>(q + rA * K + e0) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
     if (storeB) *reinterpret_cast<uint4*>(q + (rA + 1) * K + e0) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
   }
@@ -494,7 +517,7 @@ __device__ __forceinline__ uint2 act8_code(float2 v, float2 inv, float one) {
 template <int ROT, int PASSES, bool SAFE>
 __device__ __forceinline__ void act8_quant_store(const RotQuantArgs& args, float2 (&v)[PASSES][16],
                                                  float2 inv, int64_t rA, bool storeB, int warp, int nwarps,
-                                                 int nchunks, int lane, unsigned char* tile) {
+                                                 int nchunks, int lane, unsigned char* tile, bool pack) {
   const int K = args.K;
   const int h = lane >> 4, c = lane & 15;
   const float one = args.rows_pad > 0 ? 1.0f : 2.0f;   // 1.0 whenever the kernel runs (rows_pad > 0)
@@ -545,7 +568,7 @@ __device__ __forceinline__ void act8_quant_store(const RotQuantArgs& args, float
         }
       }
     }
-    act8_emit(args, rA, storeB, j, lane, valid, wa, wb);
+    act8_emit(args, rA, storeB, j, lane, valid, pack, wa, wb);
   }
 }
 
@@ -572,8 +595,9 @@ __device__ __forceinline__ float2 bf16x2_round(float2 v) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
 }
 
-template <int ROT, int PASSES, bool LNMOD, int QMAX>
+template <int ROT, int PASSES, bool LNMOD, int QMAX, bool SWIGLU>
 __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
+  static_assert(!(LNMOD && SWIGLU), "one prologue at a time");
   extern __shared__ __align__(16) unsigned char act8_smem[];
   __shared__ float red[2][act8::kMaxTeamWarps];
   __shared__ float red_ln[2][2][act8::kMaxTeamWarps];   // layer-norm prologue: sums, then centered squares
@@ -586,13 +610,40 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
   const int h = lane >> 4;
 
   float2 v[PASSES][16];
-  const __nv_bfloat16* xa = static_cast<const __nv_bfloat16*>(args.x) + rA * K;
-  const __nv_bfloat16* xb = xa + K;
+  const int64_t ld = SWIGLU ? 2 * static_cast<int64_t>(K) : K;   // SwiGLU rows are [gate | up], 2K wide
+  const __nv_bfloat16* xa = static_cast<const __nv_bfloat16*>(args.x) + rA * ld;
+  const __nv_bfloat16* xb = xa + ld;
 #pragma unroll
   for (int s = 0; s < PASSES; ++s) {
     const int j = warp + s * nwarps;
     const int e = 512 * j + 16 * lane;
     const bool valid = j < nchunks && 512 * j + 256 * h < K;
+    if constexpr (SWIGLU) {
+      // silu(gate) * up in fp32, rounded once to bf16 (comfy-kitchen's fused form, as in the scalar kernel)
+      uint4 r[8];                                          // gate A, up A, gate B, up B: 16 bf16 each
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = make_uint4(0, 0, 0, 0);
+      if (valid && liveA) {
+        r[0] = __ldg(reinterpret_cast<const uint4*>(xa + e)); r[1] = __ldg(reinterpret_cast<const uint4*>(xa + e + 8));
+        r[2] = __ldg(reinterpret_cast<const uint4*>(xa + K + e)); r[3] = __ldg(reinterpret_cast<const uint4*>(xa + K + e + 8));
+      }
+      if (valid && liveB) {
+        r[4] = __ldg(reinterpret_cast<const uint4*>(xb + e)); r[5] = __ldg(reinterpret_cast<const uint4*>(xb + e + 8));
+        r[6] = __ldg(reinterpret_cast<const uint4*>(xb + K + e)); r[7] = __ldg(reinterpret_cast<const uint4*>(xb + K + e + 8));
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int q = (i >> 3), w = (i >> 1) & 3;          // uint4 and word holding column i
+        auto word = [&](int k) {
+          const uint4 t = r[k + q];
+          return w == 0 ? t.x : (w == 1 ? t.y : (w == 2 ? t.z : t.w));
+        };
+        auto col = [&](uint32_t u) { return __uint_as_float((i & 1) ? (u & 0xFFFF0000u) : (u << 16)); };
+        const float ga = col(word(0)), ua = col(word(2)), gb = col(word(4)), ub = col(word(6));
+        v[s][i] = make_float2(swiglu_fused(ga, ua), swiglu_fused(gb, ub));
+      }
+      continue;
+    }
     uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
     if (valid && liveA) { a0 = __ldg(reinterpret_cast<const uint4*>(xa + e)); a1 = __ldg(reinterpret_cast<const uint4*>(xa + e + 8)); }
     if (valid && liveB) { b0 = __ldg(reinterpret_cast<const uint4*>(xb + e)); b1 = __ldg(reinterpret_cast<const uint4*>(xb + e + 8)); }
@@ -732,11 +783,12 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
       if (storeB) args.rsplit[(rA + 1) * args.rs_cols + jj] = __float2bfloat16_rn(0.0f);
     }
   }
-  if (finite) act8_quant_store<ROT, PASSES, false>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile);
-  else act8_quant_store<ROT, PASSES, true>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile);
+  const bool pack = QMAX == 7 && !args.int4_as_int8;   // int4 codes as packed nibbles [rows_pad, K/2]
+  if (finite) act8_quant_store<ROT, PASSES, false>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile, pack);
+  else act8_quant_store<ROT, PASSES, true>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile, pack);
 }
 
-template <int ROT, bool LNMOD = false, int QMAX = 127>
+template <int ROT, bool LNMOD = false, int QMAX = 127, bool SWIGLU = false>
 static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   // Three chunks per warp.  Measured on B200 at K = 3072 and 12288, M = 4096-65536: one or two chunks per warp
   // (more, smaller warps) were slower or equal, and so was a persistent variant that prefetched the next token
@@ -745,7 +797,7 @@ static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   const int nchunks = (a.K + 511) / 512;
   const int warps = (nchunks + kPasses - 1) / kPasses;
   const size_t smem = static_cast<size_t>(warps) * act8::kTileBytes;
-  auto k = act8_kernel<ROT, kPasses, LNMOD, QMAX>;
+  auto k = act8_kernel<ROT, kPasses, LNMOD, QMAX, SWIGLU>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   k<<<static_cast<unsigned>((a.rows_pad + 1) / 2), warps * 32, smem, st>>>(a);
   return cudaGetLastError();
@@ -784,8 +836,23 @@ static cudaError_t launch_rq_rot(int rot, const RotQuantArgs& a, cudaStream_t st
   }
 }
 
+template <int QMAX, bool SWIGLU>
+static cudaError_t launch_act8_rot(int rot, const RotQuantArgs& a, cudaStream_t st) {
+  switch (rot) {
+    case 0: return launch_act8<0, false, QMAX, SWIGLU>(a, st);
+    case 16: return launch_act8<16, false, QMAX, SWIGLU>(a, st);
+    case 64: return launch_act8<64, false, QMAX, SWIGLU>(a, st);
+    default: return launch_act8<256, false, QMAX, SWIGLU>(a, st);
+  }
+}
+
 cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantArgs& a, cudaStream_t st) {
   if (swiglu) {
+    // per-token modes on the two-token kernel; the per-group mode (fp32 product) stays on the scalar kernel
+    if ((mode == MODE_ACT_INT8_ROW || mode == MODE_ACT_INT4_ROW) && act8_fits(a)) {
+      if (a.rows_pad == 0) return cudaSuccess;
+      return mode == MODE_ACT_INT8_ROW ? launch_act8_rot<127, true>(rot, a, st) : launch_act8_rot<7, true>(rot, a, st);
+    }
     if (mode == MODE_ACT_INT8_ROW) return launch_rq_rot<__nv_bfloat16, true, MODE_ACT_INT8_ROW>(rot, a, st);
     if (mode == MODE_ACT_INT4_ROW) return launch_rq_rot<__nv_bfloat16, true, MODE_ACT_INT4_ROW>(rot, a, st);
     return launch_rq_rot<__nv_bfloat16, true, MODE_ACT_INT4_GROUP>(rot, a, st);
@@ -801,26 +868,13 @@ cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantAr
         default: return launch_act8<256, true>(a, st);
       }
     }
-    if (act8_fits(a)) {
-      switch (rot) {
-        case 0: return launch_act8<0>(a, st);
-        case 16: return launch_act8<16>(a, st);
-        case 64: return launch_act8<64>(a, st);
-        default: return launch_act8<256>(a, st);
-      }
-    }
+    if (act8_fits(a)) return launch_act8_rot<127, false>(rot, a, st);
     return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT8_ROW>(rot, a, st);
   }
   if (mode == MODE_ACT_INT4_ROW) {
     if (a.rows_pad == 0) return cudaSuccess;
-    if (a.int4_as_int8 && act8_fits(a)) {        // int4 values as int8 codes (the W4A4 GEMM's operand)
-      switch (rot) {
-        case 0: return launch_act8<0, false, 7>(a, st);
-        case 16: return launch_act8<16, false, 7>(a, st);
-        case 64: return launch_act8<64, false, 7>(a, st);
-        default: return launch_act8<256, false, 7>(a, st);
-      }
-    }
+    // int4 values as int8 codes (the W4A4 GEMM's operand) or as packed nibbles (the reference's format)
+    if (act8_fits(a)) return launch_act8_rot<7, false>(rot, a, st);
     return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_ROW>(rot, a, st);
   }
   return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_GROUP>(rot, a, st);

@@ -168,9 +168,24 @@ def test_swiglu_rotquant_within_ties(ops, mode, name):
     assert np.allclose(s.cpu().numpy(), sr, rtol=1e-5)
 
 
+def test_swiglu_fused_equals_quantizer_of_rounded_product_exactly(ops):
+    """test_comfyui_fase4_dispatch.py:100-110, the reference's own assertion: on 64 x 2048 standard-normal bf16
+    inputs the fused SwiGLU quantizer (hardware exponential, fast division, as comfy-kitchen's fast-math build)
+    gives codes and scales identical to the plain quantizer fed torch's silu(gate) * up rounded once to bf16.  The
+    two silu forms round a bf16 intermediate differently in about 1 of 1e8 elements; none of these 65k does."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(64, 2048, generator=g, device="cuda").to(torch.bfloat16)
+    k = x.shape[-1] // 2
+    qf, sf = ops.swiglu_quantize_int4_rowwise_convrot64(x)
+    qc, sc = ops.quantize_int4_rowwise_convrot64(
+        (torch.nn.functional.silu(x[:, :k].float()) * x[:, k:].float()).to(x.dtype), 256)
+    assert torch.equal(qf, qc) and torch.equal(sf.reshape(-1), sc.reshape(-1))
+
+
 def test_swiglu_fused_equals_quantizer_of_rounded_product(ops):
-    """test_comfyui_fase4_dispatch.py:108-110: the fused SwiGLU quantizer equals the plain quantizer fed
-    silu(gate)*up rounded once to bf16 (same device arithmetic on both sides)."""
+    """test_comfyui_fase4_dispatch.py:108-110 on the synthetic activations (outlier channels): the fused SwiGLU
+    quantizer equals the plain quantizer fed torch's silu(gate)*up rounded once to bf16, within rounding ties
+    (the fused silu takes the hardware exponential and fast division)."""
     m, k = 64, 1024
     h = bf16_dev(ref.synth_activations(m, 2 * k, seed=5))
     qf, sf = ops.swiglu_quantize_int4_rowwise_convrot64(h)
