@@ -279,7 +279,7 @@ int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int r
 
 int cq_gemm_rowcol_swiglu(const int8_t* a, const float* sa, const void* b_glu, const float* sb, const void* bias,
                           void* out, int64_t M, int64_t N, int64_t K, void* stream) {
-  if (N % 128 != 0) return CQ_ERR_SHAPE;            // whole 64-gate + 64-up row tiles
+  if (N % 128 != 0) return CQ_ERR_SHAPE;            // whole 128-row weight tiles of 16-gate + 16-up row groups
   if (int e = check_gemm(a, b_glu, out, M, N, K)) return e;
   if (M == 0) return CQ_OK;
   if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
@@ -292,6 +292,7 @@ int cq_linear_convrot_w4a4_swiglu(const void* x, int64_t M, int64_t K, int64_t N
                                   const void* qweight_glu, const float* wscale_glu, const void* bias_glu, void* out,
                                   void* workspace, int64_t workspace_bytes, void* stream) {
   if (act_bits != 4 && act_bits != 8) return CQ_ERR_ARG;
+  if (N % 128 != 0) return CQ_ERR_SHAPE;            // checked before the activations are quantized
   if (M == 0) return CQ_OK;
   Workspace w;
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;

@@ -69,6 +69,34 @@ def test_host_side_argument_checks_need_no_device(lib):
     assert lib.cq_linear_workspace_bytes(-1, 3072) == -1
 
 
+def test_swiglu_output_argument_checks_need_no_device(lib):
+    from comfy_quant_bench_b200 import _lib
+    vp = ctypes.c_void_p(16)
+    # whole 128-row weight tiles (N % 128); K a multiple of 128; activation bits 4 or 8
+    assert lib.cq_gemm_rowcol_swiglu(vp, vp, vp, vp, None, vp, 4, 192, 256, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_gemm_rowcol_swiglu(vp, vp, vp, vp, None, vp, 4, 256, 100, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_gemm_rowcol_swiglu(vp, None, vp, vp, None, vp, 4, 256, 256, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_gemm_rowcol_swiglu(None, None, None, None, None, None, 0, 256, 256, None) == _lib.CQ_OK
+    assert lib.cq_linear_convrot_w4a4_swiglu(vp, 4, 256, 256, 256, 5, vp, vp, None, vp, vp, 1 << 20, None) == \
+        _lib.CQ_ERR_ARG
+    # the N check comes before any work on the activations
+    assert lib.cq_linear_convrot_w4a4_swiglu(vp, 4, 256, 192, 256, 4, vp, vp, None, vp, vp, 1 << 20, None) == \
+        _lib.CQ_ERR_SHAPE
+    # too small a workspace
+    assert lib.cq_linear_convrot_w4a4_swiglu(vp, 4096, 256, 256, 256, 4, vp, vp, None, vp, vp, 64, None) != _lib.CQ_OK
+
+
+def test_swiglu_output_rows_are_a_permutation_of_whole_groups():
+    from comfy_quant_bench_b200 import ops
+    idx = ops.swiglu_output_rows(384).tolist()
+    assert sorted(idx) == list(range(384))
+    for p, r in enumerate(idx):
+        grp, i = divmod(p, 32)
+        assert r == (16 * grp + i if i < 16 else 192 + 16 * grp + i - 16)
+    with pytest.raises(ValueError):
+        ops.swiglu_output_rows(192)
+
+
 def test_dit_glue_argument_checks_need_no_device(lib):
     from comfy_quant_bench_b200 import _lib
     vp = ctypes.c_void_p(16)
