@@ -506,13 +506,16 @@ def run_mmdit(args, world, rank, local):
     """One MMDiT denoise step per replica per iteration, graph-replayed; data-parallel over ranks."""
     from comfy_quant_bench_b200 import mmdit as mm
     dev = torch.device("cuda", local)
-    cfg = mm.MMDiTConfig(blocks=args.mmdit_blocks)
+    cfg = mm.MMDiTConfig(blocks=args.mmdit_blocks, quantize_modulation=not args.mmdit_bf16_modulation)
     model = mm.MMDiT(cfg, device=dev, seed=0)
     img, txt, temb = model.inputs(seed=1 + rank)
     launches = 2 * len(model.linears()) + (3 * cfg.blocks if cfg.fused_glue else 0)   # + qkv glue x2, head gather
+    linears = ("every linear W4A8 affine g128, ConvRot g256 (modulation included)" if cfg.quantize_modulation else
+               "every linear but the adaLN modulation W4A8 affine g128, ConvRot g256; modulation bf16 (torch), as "
+               "the reference's quantization profiles leave it")
     config = {"workload": "mmdit_step", "blocks": cfg.blocks, "hidden": cfg.hidden, "heads": cfg.heads,
               "mlp": cfg.mlp, "img_tokens": cfg.img_tokens, "txt_tokens": cfg.txt_tokens, "batch": 1,
-              "linears": "every linear W4A8 affine g128, ConvRot g256 (modulation included)",
+              "linears": linears,
               "glue": "layer norm + modulation fused into the QKV / MLP-up activation kernels, q/k RMSNorm + rotary "
                       "+ attention layout in one kernel" if cfg.fused_glue else "torch ops"}
     _run_dit(args, world, rank, local, model, (img, txt, temb), lambda o: o[0], "MMDiT denoise steps/s", config,
@@ -824,6 +827,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["mmdit", "wan", "ltx", "sweep"], default="w4a8")
     ap.add_argument("--mode", choices=["dp", "tp", "tp_fused"], default="dp")
     ap.add_argument("--mmdit-blocks", type=int, default=60)
+    ap.add_argument("--mmdit-bf16-modulation", action="store_true",
+                    help="keep the adaLN modulation linears in bf16 (the reference's profiles exclude them)")
     ap.add_argument("--wan-blocks", type=int, default=30)
     ap.add_argument("--ltx-blocks", type=int, default=48)
     ap.add_argument("--no-reference-check", action="store_true")
