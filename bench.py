@@ -286,8 +286,8 @@ def run_ours(args, world, rank, local):
         raise RuntimeError(f"device status {st}")
     t_quant = [e[0].elapsed_time(e[1]) for e in evs]
     t_gemm = [e[1].elapsed_time(e[2]) for e in evs]
-    total_ms = sum(a + b for a, b in zip(t_quant, t_gemm))
-    total_ms = allreduce_max(total_ms, world)
+    per_step = [a + b for a, b in zip(t_quant, t_gemm)]
+    total_ms = allreduce_max(sum(per_step), world)
     ms_per_step = total_ms / args.steps
     ops_per_step = 2.0 * m * n * k
     value = ops_per_step * args.steps * world / (total_ms / 1e3) / 1e12
@@ -382,6 +382,8 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"dp{world}", "l2": "flushed before every step (256 MiB memset outside the events)",
                    "inputs": "x ~ N(0,1) bf16 with 1% outlier channels x20, W ~ N(0,0.02), bias ~ N(0,0.01), seeded"},
         "breakdown_ms": {"rotquant": quant_ms, "gemm": gemm_ms},
+        "step_ms_spread": {"median": statistics.median(per_step), "min": min(per_step), "max": max(per_step),
+                           "of": "rank 0's device-timed steps (activation kernel + GEMM)"},
         "roofline": {"bound": "tensor", "kernel": "gemm_kernel<rowcol>" if args.workload == "w4a4" else "gemm_kernel<affine>",
                      "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
                      "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16_tflops']} TFLOP/s; B200 int8 "
@@ -728,6 +730,8 @@ def run_sweep(args, world, rank, local):
     peaks = _peaks()
     int8_peak = 2.0 * peaks["bf16_tflops"]
 
+    spread = {}                           # the last timed case's fastest and slowest call, added to its line
+
     def timed(fn, reps):
         for _ in range(2):
             fn()
@@ -741,11 +745,12 @@ def run_sweep(args, world, rank, local):
             b.record(stream)
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
+        spread.update(ms_min=min(ts), ms_max=max(ts))
         return statistics.median(ts)
 
     def emit(d):
         if rank == 0:
-            print(json.dumps(d), flush=True)
+            print(json.dumps({**d, **spread}), flush=True)
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(0)
