@@ -767,6 +767,20 @@ def run_sweep(args, world, rank, local):
                   "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12, "frac_of_int8_peak": 2.0 * m * n * k / (ms / 1e3) / 1e12 / int8_peak})
             del x
         torch.cuda.empty_cache()
+    # --- a few tokens (adaLN modulation: M=1, N=6*3072, K=3072): the one-warp-per-row product, bound by reading
+    #     the packed weights, scales and zeros once ---
+    n, k = 6 * 3072, 3072
+    w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+    qw, sc, z = ops.quantize_affine_w4_weight(w, 128, 256)
+    zt = ops.prepare_affine_zeros(z, 128)
+    del w
+    for m in (1, 8):
+        x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+        ms = timed(lambda: ops.w4a8_affine_linear(x, qw, sc, z, None, 128, 256, zeros_prepared=zt), args.steps)
+        byts = n * k // 2 + 2 * (k // 128) * n * 2
+        emit({"case": "w4a8_affine_linear_few_tokens", "M": m, "N": n, "K": k, "ms": ms,
+              "weight_gbs": byts / (ms / 1e3) / 1e9, "frac_of_hbm": byts / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+              "note": "activation kernel + product; weight bytes = packed codes + bf16 scales and zeros"})
     # --- activation rotation + int8 quantization at large M (HBM-bound) ---
     for m in (4096, 32768, 65536):
         k = 3072

@@ -887,6 +887,9 @@ int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, cons
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st, void* const* outs, int n_outs, int col0, int64_t ldo) {
+  // a few tokens (adaLN modulation): read the weights once with a warp per row instead of 256-token MMA tiles
+  if (outs == nullptr && gemv_affine_fits(M, a_kperm))
+    return launch_gemv_affine(a, sa, b, s, zt, bias, out, M, N, K, st) == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
   GemmArgs g{};
   g.sa = sa;
   g.nz = rsplit_cols(K) / 64;

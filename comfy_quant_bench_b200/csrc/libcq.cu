@@ -2,6 +2,7 @@
 // same module (no relocatable device code needed).
 #include "rotquant.cu"
 #include "gemm_sm100.cu"
+#include "gemv.cu"
 #include "dit.cu"
 #include "capi.cu"
 #include "noalloc.cu"

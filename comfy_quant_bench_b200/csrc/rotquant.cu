@@ -146,7 +146,6 @@ constexpr int kMaxWarps = 32;
 
 template <typename IN_T, int ROT, bool SWIGLU, int MODE, int PPW>
 __global__ void __launch_bounds__(1024) rotquant_kernel(const RotQuantArgs args) {
-  constexpr bool IS_WEIGHT = MODE >= 10;
   constexpr bool ROWWISE = MODE == MODE_ACT_INT8_ROW || MODE == MODE_ACT_INT4_ROW || MODE == MODE_W_INT4_ROW ||
                            MODE == MODE_W_INT8_ROW;
   extern __shared__ float smem_tiles[];

@@ -443,6 +443,28 @@ def test_errors_raise(ops):
                                 torch.ones(8, device="cuda"), linear_dtype="fp8")
 
 
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9])
+@pytest.mark.parametrize("n,k", [(320, 1280), (392, 3072)])
+def test_w4a8_affine_linear_few_tokens_vs_oracle(ops, m, n, k):
+    """M <= 8 runs the one-warp-per-row product (K/32 chunks not a multiple of 32 at K=1280; N not a multiple of
+    the 8 rows per CTA at 392); M = 9 the tensor-core GEMM.  Both against the oracle, deterministic, and exact under
+    a power-of-two input scale without bias."""
+    x = ref.synth_activations(m, k, seed=40 + m)
+    w = ref.synth_weight(n, k, seed=41)
+    bb = ref.synth_bias(n, seed=42)
+    qw, sw, zw = ops.quantize_affine_w4_weight(torch.from_numpy(w).cuda(), 128, 256)
+    xt = bf16_dev(x)
+    out = ops.w4a8_affine_linear(xt, qw, sw, zw, bf16_dev(bb), group_size=128, convrot_groupsize=256)
+    _check_status()
+    qx, sx = ref.rotquant(x, 256, "int8")
+    qr, sr, zr = ref.weight_quant_affine(w, 256, 128)
+    assert_bf16_close(out, ref.linear_affine(qx, sx, qr, sr, zr, ref.bf16_bits_to_f32(bb), 128))
+    y1 = ops.w4a8_affine_linear(xt, qw, sw, zw, None, group_size=128, convrot_groupsize=256)
+    assert torch.equal(y1, ops.w4a8_affine_linear(xt, qw, sw, zw, None, group_size=128, convrot_groupsize=256))
+    assert torch.equal(ops.w4a8_affine_linear(xt * 2, qw, sw, zw, None, group_size=128, convrot_groupsize=256),
+                       y1 * 2)
+
+
 # n % 64 == 0: 64-column boxes shared by two epilogue warps; n = 96: 32-column boxes (one warp each)
 @pytest.mark.parametrize("m,n,k,col0,ldo", [(300, 256, 1024, 256, 768), (1000, 640, 3072, 0, 1280),
                                             (130, 96, 1024, 32, 256), (77, 128, 512, 40, 256)])
