@@ -9,7 +9,7 @@ tensor names, dtypes, shapes and ``_quantization_metadata`` JSON.  Each format a
     quantize(weight)       the B200 weight kernel, returning tensors in the order of ``tensors()``
 
 ``AffineW4A8`` is new here: the awq_w4a16 tensor layout (``W = (q - 8) * scale + zeros``, scale/zeros bf16
-[K/G, N]) executed with per-token int8 activations by the W4A8 affine kernel (3 and 5).
+[K/G, N]) executed with per-token int8 activations by the W4A8 affine kernel.
 """
 from __future__ import annotations
 
@@ -145,7 +145,7 @@ class AwqW4A16:
 
 @dataclass(frozen=True)
 class AffineW4A8:
-    """The BASELINE W4A8 format: awq_w4a16 tensors (group 128), optional ConvRot, int8 per-token activations."""
+    """The W4A8 format: awq_w4a16 tensors (group 128), optional ConvRot, int8 per-token activations."""
     group_size: int = 128
     convrot_groupsize: int = 0
     name = "affine_w4a8"

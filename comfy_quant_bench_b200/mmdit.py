@@ -44,7 +44,7 @@ class MMDiTConfig:
     txt_tokens: int = 256
     group_size: int = 128
     convrot_groupsize: int = 256
-    quantize_modulation: bool = True   # BASELINE: every linear W4A8; the reference excludes modulation layers
+    quantize_modulation: bool = True   # every linear W4A8; the reference's profiles leave modulation unquantized
     fused_glue: bool = True            # kernel path: layer norm + modulation inside the activation kernel of the
                                        # QKV and MLP-up linears, q/k RMSNorm + rotary + attention layout in one kernel
 

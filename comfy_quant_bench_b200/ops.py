@@ -9,7 +9,7 @@ Names, argument meaning and error behaviour follow the call sites in comfy-quant
 * ``quantize_convrot_w4a4_weight`` / ``quantize_int8_convrot_weight`` (``tools/_formats.py:72-76, 149-156``) and
   ``quantize_affine_w4_weight`` (the awq_w4a16 layout, ``tools/_formats.py:191-212``) - the converter kernels;
 * ``int4_linear`` (``g64_bench6.py:109``), ``convrot_w4a4_linear`` (``patches/comfy_kitchen_swiglu_w4a4_fused.patch:41-95``),
-  ``int8_linear`` (``tools/_native_probe.py:234-255``) and ``w4a8_affine_linear`` (the BASELINE W4A8 linear).
+  ``int8_linear`` (``tools/_native_probe.py:234-255``) and ``w4a8_affine_linear`` (W4A8 on awq-layout weights).
 
 Every op runs the CUDA kernels of libcq_b200.so on the input's device and the current torch stream.  Inputs
 on the CPU or on a non-sm_100 device are rejected: there is no eager fallback.
@@ -517,7 +517,7 @@ def gemm_affine_into(a: torch.Tensor, sa: torch.Tensor, gsplit: torch.Tensor, qw
 
 
 # ----------------------------------------------------------------------------------------------
-# ConvRot W4A4 linear with the SwiGLU output fused into the GEMM epilogue (epilogue variant)
+# ConvRot W4A4 linear with the SwiGLU output silu(y[:, :N/2]) * y[:, N/2:] fused into the GEMM epilogue
 # ----------------------------------------------------------------------------------------------
 
 def swiglu_output_rows(n: int, device=None) -> torch.Tensor:

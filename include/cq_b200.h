@@ -160,7 +160,7 @@ CQ_API int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const v
                           void* stream);
 
 /*
- * W4A8 affine linear, the BASELINE north-star GEMM:
+ * W4A8 affine linear, the headline GEMM:
  *   out[m, n] = bf16( sa[m] * sum_g ( s[g,n] * sum_{k in g} a[m,k]*(q[n,k]-8) + z[g,n] * gsum[g,m] ) + bias[n] )
  * with q the awq_w4a16 uint4 codes (packed [N, K/2]), s bf16 [K/group, N] and the zeros z passed as zt, the
  * operand cq_prepare_affine_zeros builds from z bf16 [K/group, N]
@@ -200,8 +200,8 @@ CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int ro
                    void* stream);
 
 /*
- * W4A4 row/col GEMM / ConvRot W4A4 linear with the SwiGLU output fused into the epilogue (the
- * epilogue variant: silu(y[:, :N/2]) * y[:, N/2:] of the N-column linear y):
+ * W4A4 row/col GEMM / ConvRot W4A4 linear with the SwiGLU output fused into the epilogue
+ * (silu(y[:, :N/2]) * y[:, N/2:] of the N-column linear y):
  *   out[m, j] = bf16( bf16(silu(y[m, j])) * y[m, N/2 + j] ),  y = bf16(linear output),  out bf16 [M, N/2]
  * (torch's silu and mul on the bf16 linear output).  The weight rows, scales and bias are passed interleaved in
  * groups of 32: row p of b_glu / sb / bias is original row (p / 32) * 16 + p % 32 for p % 32 < 16 (gate) and

@@ -24,8 +24,8 @@ It restates, in numpy float32/int64 arithmetic, the algorithm comfy-quant-bench 
   (``patches/comfyui_awq_w4a16_format.patch:79-80``).
 * Integer GEMM (int64 accumulation) and the fp epilogues of ``g64_bench6.py:50-68`` (row x row scales,
   per-group scales) plus the affine zero-point term.
-* Dequantize-and-matmul (``patches/tests/test_comfyui_fase4_dispatch.py:98``): the reference path the
-  north star checks bf16 outputs against.
+* Dequantize-and-matmul (``patches/tests/test_comfyui_fase4_dispatch.py:98``): the reference path that the
+  quantized linears' bf16 outputs are checked against.
 
 Float32 evaluation order is spelled out (every ``np.float32`` op rounds once, numpy never fuses a multiply
 and an add), so the CUDA kernels, which use explicitly rounded intrinsics in the same order, match this
@@ -383,7 +383,7 @@ def rel_l2(ref: np.ndarray, got: np.ndarray) -> float:
 
 
 # ----------------------------------------------------------------------------------------------
-# seeded synthetic inputs
+# seeded synthetic inputs (the benchmark shapes' value distributions)
 # ----------------------------------------------------------------------------------------------
 
 def synth_activations(m: int, k: int, seed: int = 0, outlier_frac: float = 0.01, outlier_gain: float = 20.0):

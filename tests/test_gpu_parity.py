@@ -1,9 +1,10 @@
 """GPU parity: the CUDA path (through the C ABI, via comfy_quant_bench_b200.ops) against the CPU oracle.
 
-Bars (the north star's): integer and byte outputs bit-exact (codes, packed nibbles, group sums, int32
-accumulators); scales bit-exact; bf16 outputs within rel-L2 <= 1e-3 of the oracle's float64 result rounded to
-bf16, with at most 1e-3 of the elements off by more than one bf16 rounding.  The SwiGLU prologue calls the
-device expf, so its codes may differ by 1 at rounding ties (<= 0.1 % of codes), the reference's own rule.
+Bars: integer and byte outputs bit-exact (codes, packed nibbles, group sums, int32 accumulators); scales
+bit-exact; bf16 outputs within rel-L2 <= 1e-3 of the oracle's float64 result rounded to bf16, with at most 1e-3 of
+the elements off by more than one bf16 rounding.  The SwiGLU prologue computes silu with the device's hardware
+exponential (and, per token, its fast division, as comfy-kitchen's fast-math build does), so its codes may differ
+by 1 at rounding ties (<= 0.1 % of codes), the reference's own rule (g64_quant_test.py:72-103).
 """
 import numpy as np
 import pytest
@@ -387,7 +388,7 @@ def test_int8_linear_vs_oracle(ops):
 
 
 # ----------------------------------------------------------------------------------------------
-# BASELINE full size: size-independent properties + a row slice against the oracle
+# full benchmark size (M=4096, K=3072, N=12288): size-independent properties + a row slice against the oracle
 # ----------------------------------------------------------------------------------------------
 
 def test_full_size_w4a8_properties(ops):
