@@ -1,10 +1,11 @@
 // Small-M W4A8 affine product: the W4A8 linear for M <= 8 tokens (adaLN modulation and other one-token products).
 //
 // The tensor-core GEMM runs whole 256-token tiles, so a one-token product pays for 256 tokens of MMA and drain; at
-// M <= 8 the product is bound by reading the packed weights once.  One warp per weight row: lane l reads the row's
-// 16-byte chunks l, l + 32, ... (32 K columns each, a quarter of a 128-wide group) and every token's 32 matching
-// int8 codes, in the K-permuted order the activation kernel stores (0,2,4,6,1,3,5,7 inside each 8-column block),
-// so a packed word's low nibbles meet one activation word and its high nibbles the next.
+// M <= 8 the product is bound by reading the packed weights once.  One warp per four weight rows: lane l reads the
+// rows' 16-byte chunks l, l + 32, ... (32 K columns each, a quarter of a 128-wide group) and every token's 32
+// matching int8 codes once for the four rows, in the K-permuted order the activation kernel stores (0,2,4,6,1,3,5,7
+// inside each 8-column block), so a packed word's low nibbles meet one activation word and its high nibbles the
+// next.
 //
 // Per token and group: P = sum x (q - 8) = dp4a(q, x) - 8 R with R = sum x (exact int32), then the group adds
 // s[g, n] P + z[g, n] R in fp32; the lane partials are summed by a fixed shuffle tree (deterministic), and the
@@ -15,7 +16,8 @@
 namespace cq {
 
 namespace gemv {
-constexpr int kWarps = 8;      // weight rows per CTA
+constexpr int kWarps = 8;
+constexpr int kRowsPerWarp = 4;  // rows share each chunk's activation loads and group sums
 constexpr int kMaxTokens = 8;
 }  // namespace gemv
 
@@ -39,75 +41,103 @@ struct GemvArgs {
 
 template <int MT>
 __global__ void __launch_bounds__(gemv::kWarps * 32) gemv_affine_kernel(const GemvArgs args) {
+  constexpr int R = gemv::kRowsPerWarp;
   const int lane = threadIdx.x & 31;
-  const int n = blockIdx.x * gemv::kWarps + (threadIdx.x >> 5);
-  if (n >= args.N) return;                                   // warp-uniform
+  const int n0 = (blockIdx.x * gemv::kWarps + (threadIdx.x >> 5)) * R;
+  if (n0 >= args.N) return;                                  // warp-uniform
   const int K = args.K, M = args.M;
   const int nchunks = K >> 5;                                // 32-column chunks (16 packed bytes)
-  const uint8_t* wrow = args.b + static_cast<int64_t>(n) * (K >> 1);
   const bool leader = (lane & 3) == 0;                       // one lane per group adds the group's terms
-  float part[MT];
+  bool row_ok[R];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) part[m] = 0.0f;
+  for (int r = 0; r < R; ++r) row_ok[r] = n0 + r < args.N;
+  float part[R][MT];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) part[r][m] = 0.0f;
 
   // every lane runs every iteration (the shuffles below name the whole warp); chunks past the row are skipped.
   // nchunks is a multiple of 4, so the four lanes of a group are all inside the row or all past it.
-#pragma unroll 2
+#pragma unroll 1
   for (int c0 = 0; c0 < nchunks; c0 += 32) {
     const int c = c0 + lane;
     const bool valid = c < nchunks;
-    uint4 wq = make_uint4(0, 0, 0, 0);
-    if (valid) wq = __ldg(reinterpret_cast<const uint4*>(wrow + 16 * static_cast<int64_t>(c)));
-    const uint32_t w[4] = {wq.x, wq.y, wq.z, wq.w};
-    int pm[MT], rm[MT];
+    uint4 wq[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      wq[r] = make_uint4(0, 0, 0, 0);
+      if (valid && row_ok[r])
+        wq[r] = __ldg(reinterpret_cast<const uint4*>(args.b + static_cast<int64_t>(n0 + r) * (K >> 1) +
+                                                     16 * static_cast<int64_t>(c)));
+    }
+    int pm[R][MT], rm[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-      pm[m] = 0;
       rm[m] = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) pm[r][m] = 0;
       if (valid && m < M) {
+        // this token's 32 codes of the chunk, shared by the warp's R rows
         const int8_t* xr = args.a + static_cast<int64_t>(m) * K + 32 * c;
         const uint4 x0 = __ldg(reinterpret_cast<const uint4*>(xr));
         const uint4 x1 = __ldg(reinterpret_cast<const uint4*>(xr + 16));
         const uint32_t x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        int p = 0, r = 0;
+        int rs = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          p = dp4a_us(w[k] & 0x0F0F0F0Fu, x[2 * k], p);           // even columns of the 8-column block
-          p = dp4a_us((w[k] >> 4) & 0x0F0F0F0Fu, x[2 * k + 1], p);  // odd columns
-          r = __dp4a(static_cast<int>(x[2 * k]), 0x01010101, r);
-          r = __dp4a(static_cast<int>(x[2 * k + 1]), 0x01010101, r);
+        for (int j = 0; j < 8; ++j) rs = __dp4a(static_cast<int>(x[j]), 0x01010101, rs);
+        rm[m] = rs;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint32_t w[4] = {wq[r].x, wq[r].y, wq[r].z, wq[r].w};
+          int p = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            p = dp4a_us(w[k] & 0x0F0F0F0Fu, x[2 * k], p);           // even columns of the 8-column block
+            p = dp4a_us((w[k] >> 4) & 0x0F0F0F0Fu, x[2 * k + 1], p);  // odd columns
+          }
+          pm[r][m] = p - 8 * rs;                             // sum x (q - 8) over the chunk
         }
-        pm[m] = p - 8 * r;                                   // sum x (q - 8) over the chunk
-        rm[m] = r;
       }
     }
     // the four lanes of a group (chunks 4g .. 4g + 3 sit in lanes 4j .. 4j + 3) sum their chunks
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-      pm[m] += __shfl_xor_sync(0xffffffffu, pm[m], 1);
-      pm[m] += __shfl_xor_sync(0xffffffffu, pm[m], 2);
       rm[m] += __shfl_xor_sync(0xffffffffu, rm[m], 1);
       rm[m] += __shfl_xor_sync(0xffffffffu, rm[m], 2);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        pm[r][m] += __shfl_xor_sync(0xffffffffu, pm[r][m], 1);
+        pm[r][m] += __shfl_xor_sync(0xffffffffu, pm[r][m], 2);
+      }
     }
     if (leader && valid) {
       const int g = c >> 2;
-      const float sg = __bfloat162float(args.s[static_cast<int64_t>(g) * args.N + n]);
-      const float zg = __bfloat162float(args.zt[static_cast<int64_t>(n) * args.zt_cols + g]);
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
-        part[m] = __fmaf_rn(zg, __int2float_rn(rm[m]), __fmaf_rn(sg, __int2float_rn(pm[m]), part[m]));
+      for (int r = 0; r < R; ++r) {
+        if (!row_ok[r]) continue;
+        const int n = n0 + r;
+        const float sg = __bfloat162float(args.s[static_cast<int64_t>(g) * args.N + n]);
+        const float zg = __bfloat162float(args.zt[static_cast<int64_t>(n) * args.zt_cols + g]);
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+          part[r][m] = __fmaf_rn(zg, __int2float_rn(rm[m]), __fmaf_rn(sg, __int2float_rn(pm[r][m]), part[r][m]));
+      }
     }
   }
-  // lane partials -> one sum per token (fixed tree: deterministic)
+  // lane partials -> one sum per row and token (fixed tree: deterministic); lane r * MT + m writes (n0 + r, m)
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
+  for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part[m] += __shfl_xor_sync(0xffffffffu, part[m], o);
-  const float bias = args.bias != nullptr ? __bfloat162float(args.bias[n]) : 0.0f;
+    for (int m = 0; m < MT; ++m) {
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
-    if (lane == m && m < M)
-      args.out[static_cast<int64_t>(m) * args.N + n] = __float2bfloat16_rn(__fmaf_rn(part[m], args.sa[m], bias));
+      for (int o = 16; o > 0; o >>= 1) part[r][m] += __shfl_xor_sync(0xffffffffu, part[r][m], o);
+      if (lane == (r * MT + m) % 32 && m < M && row_ok[r]) {
+        const int n = n0 + r;
+        const float bias = args.bias != nullptr ? __bfloat162float(args.bias[n]) : 0.0f;
+        args.out[static_cast<int64_t>(m) * args.N + n] = __float2bfloat16_rn(__fmaf_rn(part[r][m], args.sa[m], bias));
+      }
+    }
 }
 
 bool gemv_affine_fits(int M, int a_kperm) { return M >= 1 && M <= gemv::kMaxTokens && a_kperm != 0; }
@@ -117,7 +147,8 @@ cudaError_t launch_gemv_affine(const int8_t* a, const float* sa, const void* b, 
   const GemvArgs g{a, sa, static_cast<const uint8_t*>(b), static_cast<const __nv_bfloat16*>(s),
                    static_cast<const __nv_bfloat16*>(zt), static_cast<const __nv_bfloat16*>(bias),
                    static_cast<__nv_bfloat16*>(out), M, N, K, rsplit_cols(K)};
-  const dim3 grid(static_cast<unsigned>((N + gemv::kWarps - 1) / gemv::kWarps)), block(gemv::kWarps * 32);
+  constexpr int kRowsPerCta = gemv::kWarps * gemv::kRowsPerWarp;
+  const dim3 grid(static_cast<unsigned>((N + kRowsPerCta - 1) / kRowsPerCta)), block(gemv::kWarps * 32);
   if (M <= 1) gemv_affine_kernel<1><<<grid, block, 0, st>>>(g);
   else if (M <= 2) gemv_affine_kernel<2><<<grid, block, 0, st>>>(g);
   else if (M <= 4) gemv_affine_kernel<4><<<grid, block, 0, st>>>(g);
