@@ -207,7 +207,7 @@ def run_reference(args, world, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2.0 * rows * n * k / cb["value"] / 1e9,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "w4a8_affine_linear", "desc": desc, "M": m, "K": k, "N": n, "convrot_groupsize": rot,
+        "config": {"workload": "w4a8_linear", "desc": desc, "M": m, "K": k, "N": n, "convrot_groupsize": rot,
                    "group_size": 128, "cpu_rows_per_step": rows},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
