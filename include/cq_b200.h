@@ -171,6 +171,10 @@ CQ_API int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const v
  *   group   128
  * The zero-point term sum_g z[g,n] * gsum[g,m] runs on the tensor core (bf16 x bf16 -> fp32, exact products)
  * and seeds the fp32 accumulator that the per-group int32 partial sums are scaled into.
+ * M <= 8 with a_kperm = 1 runs a CUDA-core product instead (one warp per four weight rows, dp4a, the weights read
+ * once; gsplit unused).  Its fp32 summation order differs from the tensor-core path's, so for the same inputs
+ * the two agree to fp32 rounding (an output may differ by one bf16 step), not bit for bit.  This applies to every
+ * W4A8 affine entry point below except the column-parallel (_peers) forms, which always use the GEMM.
  */
 CQ_API int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                           const void* s_bf16, const void* zt_bf16, const void* bias, void* out, int64_t M, int64_t N,

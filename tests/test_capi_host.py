@@ -97,6 +97,20 @@ def test_swiglu_output_rows_are_a_permutation_of_whole_groups():
         ops.swiglu_output_rows(192)
 
 
+def test_prepare_swiglu_output_weight_permutes_rows_scales_and_bias_together():
+    import torch
+    from comfy_quant_bench_b200 import ops
+    n, kh = 256, 64
+    qw = torch.arange(n, dtype=torch.int8).reshape(n, 1).repeat(1, kh)   # row r holds r (mod 256) everywhere
+    ws = torch.arange(n, dtype=torch.float32)
+    bias = torch.arange(n, dtype=torch.float32).to(torch.bfloat16)
+    q2, s2, b2 = ops.prepare_swiglu_output_weight(qw, ws, bias)
+    idx = ops.swiglu_output_rows(n)
+    assert torch.equal(q2, qw[idx]) and torch.equal(s2, ws[idx]) and torch.equal(b2, bias[idx])
+    assert q2.is_contiguous() and s2.dtype == torch.float32 and b2.dtype == torch.bfloat16
+    assert ops.prepare_swiglu_output_weight(qw, ws, None)[2] is None
+
+
 def test_dit_glue_argument_checks_need_no_device(lib):
     from comfy_quant_bench_b200 import _lib
     vp = ctypes.c_void_p(16)
