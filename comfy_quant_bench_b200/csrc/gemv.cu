@@ -59,7 +59,9 @@ __global__ void __launch_bounds__(gemv::kWarps * 32) gemv_affine_kernel(const Ge
 
   // every lane runs every iteration (the shuffles below name the whole warp); chunks past the row are skipped.
   // nchunks is a multiple of 4, so the four lanes of a group are all inside the row or all past it.
-#pragma unroll 1
+  // one or two tokens: two iterations' weight loads in flight; more tokens need the registers
+  constexpr int kUnroll = MT <= 2 ? 2 : 1;
+#pragma unroll kUnroll
   for (int c0 = 0; c0 < nchunks; c0 += 32) {
     const int c = c0 + lane;
     const bool valid = c < nchunks;
