@@ -60,3 +60,22 @@ def test_rowcol_linear_equals_dequantized_product():
     got = ref.linear_rowcol(qa, sa, qw, sw)
     want = ref.dequant_matmul(qa * sa[:, None], qw * sw[:, None])
     assert ref.rel_l2(want, got) < 1e-12
+
+
+@pytest.mark.parametrize("rot", [256, 0])
+def test_cpu_baseline_step_computes_the_affine_linear(rot):
+    """The timed CPU baseline (torch CPU: oracle activation quantization, weight dequantization, fp32 F.linear)
+    computes the same linear as the oracle's integer form, to fp32 rounding."""
+    import torch
+    from oracle import cpu_path
+    m, n, k = 7, 48, 512
+    x = ref.synth_activations(m, k, seed=5)
+    w = ref.synth_weight(n, k, seed=6)
+    bias = ref.bf16_bits_to_f32(ref.synth_bias(n, seed=7))
+    q, s, z = ref.weight_quant_affine(w, rot, 128)
+    packed = torch.from_numpy(ref.pack_int4(q))
+    got = cpu_path.w4a8_affine_step(x, rot, packed, torch.from_numpy(s), torch.from_numpy(z),
+                                    torch.from_numpy(bias)).numpy()
+    qx, sx = ref.rotquant(x, rot, "int8")
+    want = ref.linear_affine(qx, sx, q, s, z, bias, 128)
+    assert ref.rel_l2(want, got) < 1e-5
