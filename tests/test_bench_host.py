@@ -23,3 +23,42 @@ def test_reference_arm_prints_one_contract_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and "16 of 4096 tokens" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_clock_sampler_reports_median_clock_and_throttle_reasons(monkeypatch):
+    """The timed region's clock record, from a fake NVML: median SM clock, the maximum, and every throttle reason
+    seen in any sample (the bench only reads clocks; it sets nothing)."""
+    import importlib
+    import time
+    import types
+    sys.path.insert(0, ROOT)
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=1,
+        nvmlClocksEventReasonSwPowerCap=0x4, nvmlClocksEventReasonHwSlowdown=0x8,
+        nvmlClocksEventReasonHwThermalSlowdown=0x40, nvmlClocksEventReasonSwThermalSlowdown=0x20,
+        nvmlClocksEventReasonHwPowerBrakeSlowdown=0x80)
+    clocks = iter([1965, 1800, 1700] + [1965] * 10_000)
+    reasons = iter([0x0, 0x4, 0x0] + [0x0] * 10_000)
+    fake.nvmlInit = lambda: None
+    fake.nvmlDeviceGetHandleByIndex = lambda i: ("gpu", i)
+    fake.nvmlDeviceGetMaxClockInfo = lambda h, kind: 1965
+    fake.nvmlDeviceGetClockInfo = lambda h, kind: next(clocks)
+    fake.nvmlDeviceGetCurrentClocksEventReasons = lambda h: next(reasons)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    bench = importlib.import_module("bench")
+    with bench.ClockSampler(0) as clk:
+        time.sleep(0.05)
+    s = clk.summary()
+    assert s["sm_max_mhz"] == 1965 and s["samples"] >= 3
+    assert s["reasons"] == ["sw_power_cap"]
+    assert s["sm_mhz"] in (1800, 1965)
+
+
+def test_clock_sampler_without_nvml_says_unavailable(monkeypatch):
+    import importlib
+    sys.path.insert(0, ROOT)
+    monkeypatch.setitem(sys.modules, "pynvml", None)          # import fails
+    bench = importlib.import_module("bench")
+    with bench.ClockSampler(0) as clk:
+        pass
+    assert clk.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
