@@ -62,3 +62,20 @@ def test_clock_sampler_without_nvml_says_unavailable(monkeypatch):
     with bench.ClockSampler(0) as clk:
         pass
     assert clk.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+
+
+def test_reference_arm_under_torchrun_prints_once_from_rank_0():
+    """Launched like the driver's N>1 runs (torchrun, two ranks): rank 0 alone runs and prints; both exit 0."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    res = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                          "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--impl", "reference",
+                          "--gpus", "2", "--steps", "1", "--warmup", "3", "--cpu-rows", "16"],
+                         cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["cpu_baseline"]["cores"] == (os.cpu_count() or 1)
