@@ -145,6 +145,21 @@ def test_groupwise_quant_matches_oracle_and_pads(ops, group, m, k):
     assert (q[m:] == 0).all() and (s[:, m:] == 0).all()
 
 
+@pytest.mark.parametrize("group", [64, 128])
+def test_groupwise_swiglu_quant_at_the_reference_test_shape(ops, group):
+    """g64_quant_test.py's SwiGLU case (M=517, K=12288, h = [gate | up] of 2K columns): codes within rounding ties
+    of the oracle, scales equal except at rare bf16 boundaries (the reference's rule), padding rows zero."""
+    m, k = 517, 12288
+    h = ref.synth_activations(m, 2 * k, seed=group)
+    q, s = ops.quant(bf16_dev(h), group, True, 128)
+    mp = (m + 127) // 128 * 128
+    assert q.shape == (mp, k // 2) and s.shape == (k // group, mp)
+    qr, sr = ref.rotquant(h, 256, "int4_group", swiglu=True, act_group=group)
+    codes_within_ties(ref.unpack_int4_signed(q[:m].cpu().numpy()), qr)
+    assert (s[:, :m].cpu().numpy() != sr).mean() <= 1e-3
+    assert (q[m:] == 0).all() and (s[:, m:] == 0).all()
+
+
 def test_groupwise_quant_matches_reference_golden(ops):
     """The reference's own quantizer reference (g64_quant_test.ref), with its acceptance rule."""
     import os
