@@ -329,6 +329,29 @@ def test_gemm_rowcol_random_scales(ops, m, n, k, bias, kperm):
     assert_bf16_close(out, want)
 
 
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (4096, 24576, 4096), (16384, 4096, 12288)])
+def test_gemm_rowcol_at_reference_bench_shapes(ops, m, n, k):
+    """g64_bench6.py's GEMM check (:50-79, 110-128, 154) at its shapes: random int4 codes in [-7, 7] on both sides,
+    scales U(0.005, 0.015); on the first and last 256 rows rel-L2 < 3e-3 and max |diff| < 4 % of the reference's
+    standard deviation; two runs bit-identical."""
+    rng = np.random.default_rng(n + k + m)
+    a = rng.integers(-7, 8, size=(m, k), dtype=np.int8)
+    b = rng.integers(-7, 8, size=(n, k), dtype=np.int8)
+    sa = rng.uniform(0.005, 0.015, m).astype(np.float32)
+    sb = rng.uniform(0.005, 0.015, n).astype(np.float32)
+    args = (torch.from_numpy(a).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(ref.pack_int4(b)).cuda(),
+            torch.from_numpy(sb).cuda(), None)
+    y1 = ops.gemm_rowcol(*args)
+    assert torch.equal(y1, ops.gemm_rowcol(*args)), "two runs differ"
+    _check_status()
+    bf = b.astype(np.float64)
+    for rows in (slice(0, 256), slice(m - 256, m)):
+        want = (a[rows].astype(np.float64) @ bf.T) * sa[rows, None].astype(np.float64) * sb[None, :].astype(np.float64)
+        d = f32_of(y1[rows]).astype(np.float64) - want
+        assert np.linalg.norm(d) / np.linalg.norm(want) < 3e-3
+        assert np.abs(d).max() / want.std() < 0.04
+
+
 def test_int4_linear_matches_reference_policy0_golden(ops):
     import os
     g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_golden.npz")))
