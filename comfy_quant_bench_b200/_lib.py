@@ -46,6 +46,7 @@ SIGNATURES = {
     "cq_version": (ctypes.c_char_p, []),
     "cq_status_string": (ctypes.c_char_p, [_int]),
     "cq_take_device_status": (_int, [ctypes.POINTER(_int), _vp]),
+    "cq_selftest_bounded_wait": (_int, [_vp]),
     "cq_rotquant": (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _i64, _int, _vp, _vp, _vp, _vp]),
     "cq_weight_rotquant": (_int, [_vp, _int, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp]),
     "cq_unpack_int4": (_int, [_vp, _i64, _i64, _vp, _vp]),

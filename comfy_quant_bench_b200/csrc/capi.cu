@@ -65,6 +65,11 @@ int cq_take_device_status(int* status, void* stream) {
   return CQ_OK;
 }
 
+int cq_selftest_bounded_wait(void* stream) {
+  if (int dv = check_device()) return dv;
+  return cuda_status(cq::launch_selftest_wait(static_cast<cudaStream_t>(stream)));
+}
+
 int64_t cq_group_sum_cols(int64_t K) { return K > 0 ? 64 * ((K / 128 + 31) / 32) : 0; }
 
 int cq_prepare_affine_zeros(const void* z_bf16, int64_t N, int64_t K, int group, void* zt_bf16, void* stream) {

@@ -70,6 +70,9 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st, void* const* outs = nullptr, int n_outs = 0, int col0 = 0, int64_t ldo = 0);
 cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t st);
+// failure-path self-test: two waits on mbarriers nothing arrives on; sites kSelftestSite and kSelftestSite + 1
+constexpr int kSelftestSite = 90;
+cudaError_t launch_selftest_wait(cudaStream_t st);
 // small-M W4A8 affine product (M <= 8, K-permuted activations): one warp per weight row, read once
 bool gemv_affine_fits(int M, int a_kperm);
 cudaError_t launch_gemv_affine(const int8_t* a, const float* sa, const void* b, const void* s, const void* zt,

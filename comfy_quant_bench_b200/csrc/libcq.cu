@@ -4,5 +4,6 @@
 #include "gemm_sm100.cu"
 #include "gemv.cu"
 #include "dit.cu"
+#include "selftest.cu"
 #include "capi.cu"
 #include "noalloc.cu"

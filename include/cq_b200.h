@@ -80,6 +80,12 @@ CQ_API const char* cq_status_string(int status);
  * Synchronizes `stream`.  Returns CQ_OK or CQ_ERR_CUDA. */
 CQ_API int cq_take_device_status(int* status, void* stream);
 
+/* Self-test of the failure path (no reference counterpart): enqueues one small kernel whose two waits, on
+ * mbarriers nothing arrives on, give up after the library's wait limit (2 s), record CQ_ERR_TIMEOUT with site 90 or
+ * 91 in the device status word and return.  The context stays usable; read the status with cq_take_device_status().
+ * Returns CQ_OK, CQ_ERR_CUDA, or CQ_ERR_UNSUPPORTED on a device that is not sm_100. */
+CQ_API int cq_selftest_bounded_wait(void* stream);
+
 /*
  * Activation rotation + dynamic quantization.
  * Replaces comfy-kitchen's quantize_int4_rowwise_convrot64(x, 256) (called at
