@@ -14,8 +14,10 @@
 //   * every call uses the same array and leaves the last call's data in it; nothing in it needs to start at
 //     zero (the activation kernel writes every byte the GEMM reads), and calls that overlap on the GPU (two
 //     streams, or two host threads) race on it - serialize them on one stream;
-//   * its device address is looked up with cudaGetSymbolAddress once per device, on the first call made with
-//     that device current; make that first call before any stream capture begins.
+//   * its device address is looked up with cudaGetSymbolAddress on the first call made with a device current,
+//     and again whenever that device's current context has changed since (after cudaDeviceReset the module is
+//     loaded anew, possibly at another address); make the first call on a device, and the first one after a
+//     reset, before any stream capture begins.
 #include <mutex>
 
 #include "kernels.cuh"
@@ -31,16 +33,41 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes]
 
 static std::mutex g_noalloc_mutex;
 static void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+static CUcontext g_noalloc_ctx[kNoallocMaxDevices] = {};
 
-// Device address of the scratch array on the current device (looked up once per device).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The driver's current context of the calling thread (the runtime makes the device's primary context current).
+static int current_context(CUcontext* ctx) {
+  static CtxGetCurrentFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr)
+      return CQ_ERR_CUDA;
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  *ctx = nullptr;
+  return fn(ctx) == CUDA_SUCCESS ? CQ_OK : CQ_ERR_CUDA;   // null when no context is current on this thread yet
+}
+
+// Device address of the scratch array on the current device, cached per device together with the context it was
+// looked up in: a different current context (the primary context was reset and re-created) looks it up again.
 static int noalloc_scratch_ptr(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) return CQ_ERR_CUDA;
+  CUcontext ctx = nullptr;
+  if (int e = current_context(&ctx)) return e;
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
+    // the lookup also makes the device's primary context current on this thread when none was
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return CQ_ERR_CUDA;
+    if (int e = current_context(&ctx)) return e;
+    if (ctx == nullptr) return CQ_ERR_CUDA;
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return CQ_OK;

@@ -118,6 +118,12 @@ class FusedColumnParallelW4A8:
         self.ptrs = [int(p) for p in self.hdl.buffer_ptrs]
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """The gathered [..., N] output.
+
+        The result is a view of the layer's persistent symmetric-memory buffer, valid until the next call of this
+        layer on ANY rank: that call's peer stores overwrite it on every rank.  A caller that keeps the output past
+        the next call (a residual, a cached activation) must ``clone()`` it.
+        """
         from . import ops
         x2 = x.reshape(-1, x.shape[-1])
         m = x2.shape[0]

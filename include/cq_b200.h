@@ -95,7 +95,8 @@ CQ_API int cq_selftest_bounded_wait(void* stream);
  * quantization inside w4a8_int8_linear / int8_linear (tools/_native_probe.py:201-255).
  *
  *   x          bf16 [M, K], or [M, 2K] = [gate | up] when swiglu != 0 (the product silu(gate)*up is quantized)
- *   rot_group  0 (no rotation), 16, 64 or 256; K % max(rot_group, 256 if swiglu) == 0 ... see DESIGN notes
+ *   rot_group  0 (no rotation), 16, 64 or 256; every group divides K, which the constraints below make a
+ *              multiple of 256 (with swiglu, x holds 2K columns and the rotation runs over the K product columns)
  *   mode       cq_act_mode
  *   act_group  64 or 128 for CQ_ACT_INT4_GROUP, else ignored
  *   M_pad      >= M; rows M..M_pad-1 of q (and of scale for CQ_ACT_INT4_GROUP) are written as 0
@@ -251,8 +252,9 @@ CQ_API int cq_linear_w4a8_affine_peers(const void* x, int64_t M, int64_t K, int6
  * held by every GPU that loads it until the process exits; problems needing more than that
  * (cq_linear_workspace_bytes(M, K) > 32 MiB, e.g. M = 8192 at K = 3072 fits, M = 16384 does not) return
  * CQ_ERR_CAPACITY.  All calls share the array: calls that overlap on the GPU race, so serialize them on one
- * stream.  The first call on each device looks up the array's device address; make it before any stream
- * capture.  It calls no cudaMalloc / cudaFree.
+ * stream.  The first call on each device looks up the array's device address, and so does the first call after
+ * the device's context was reset (cudaDeviceReset); make those calls before any stream capture.  It calls no
+ * cudaMalloc / cudaFree.
  */
 CQ_API int cq_linear_w4a8_affine_noalloc(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
                                          const void* qweight, const void* s_bf16, const void* zt_bf16, int group,

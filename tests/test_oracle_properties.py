@@ -62,10 +62,25 @@ def test_rowcol_linear_equals_dequantized_product():
     assert ref.rel_l2(want, got) < 1e-12
 
 
+@pytest.mark.parametrize("rot", [256, 64, 0])
+def test_cpu_baseline_activation_quant_matches_the_oracle(rot):
+    """The CPU baseline's torch activation quantizer (rotation in the reference's matrix form x @ H) gives the
+    oracle's codes up to +-1 at rounding ties on at most 0.1 % of them, and scales within a few fp32 ulp."""
+    import torch
+    from oracle import cpu_path
+    m, k = 64, 1024
+    x = ref.synth_activations(m, k, seed=9)
+    q, s = cpu_path.rotquant_int8_torch(torch.from_numpy(x.view(np.int16)).view(torch.bfloat16), rot)
+    qo, so = ref.rotquant(x, rot, "int8")
+    d = np.abs(q.numpy().astype(np.int32) - qo)
+    assert d.max() <= 1 and (d > 0).mean() <= 1e-3
+    np.testing.assert_allclose(s.numpy(), so, rtol=1e-6)
+
+
 @pytest.mark.parametrize("rot", [256, 0])
-def test_cpu_baseline_step_computes_the_affine_linear(rot):
-    """The timed CPU baseline (torch CPU: oracle activation quantization, weight dequantization, fp32 F.linear)
-    computes the same linear as the oracle's integer form, to fp32 rounding."""
+def test_cpu_baseline_call_computes_the_affine_linear(rot):
+    """The timed CPU baseline call (torch CPU: activation quantization, weight dequantization, fp32 F.linear)
+    computes the same linear as the oracle's integer form on the codes it quantized, to fp32 rounding."""
     import torch
     from oracle import cpu_path
     m, n, k = 7, 48, 512
@@ -74,8 +89,11 @@ def test_cpu_baseline_step_computes_the_affine_linear(rot):
     bias = ref.bf16_bits_to_f32(ref.synth_bias(n, seed=7))
     q, s, z = ref.weight_quant_affine(w, rot, 128)
     packed = torch.from_numpy(ref.pack_int4(q))
-    got = cpu_path.w4a8_affine_step(x, rot, packed, torch.from_numpy(s), torch.from_numpy(z),
-                                    torch.from_numpy(bias)).numpy()
-    qx, sx = ref.rotquant(x, rot, "int8")
-    want = ref.linear_affine(qx, sx, q, s, z, bias, 128)
+    xt = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16)
+    timings = []
+    got = cpu_path.w4a8_affine_call(xt, rot, packed, torch.from_numpy(s), torch.from_numpy(z),
+                                    torch.from_numpy(bias), timings=timings).numpy()
+    qx, sx = cpu_path.rotquant_int8_torch(xt, rot)
+    want = ref.linear_affine(qx.numpy().astype(np.int64), sx.numpy(), q, s, z, bias, 128)
     assert ref.rel_l2(want, got) < 1e-5
+    assert len(timings) == 1 and all(t >= 0 for t in timings[0])
