@@ -36,6 +36,10 @@ CQ_Q_KPERM = 2
 CQ_B_INT4_SIGNED = 0
 CQ_B_INT8 = 1
 
+CQ_GEMM_AUTO = 0
+CQ_GEMM_ONE_SM = 1
+CQ_GEMM_PAIR = 2
+
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _vp = ctypes.c_void_p
@@ -45,6 +49,7 @@ _f32 = ctypes.c_float
 SIGNATURES = {
     "cq_version": (ctypes.c_char_p, []),
     "cq_status_string": (ctypes.c_char_p, [_int]),
+    "cq_set_gemm_variant": (_int, [_int]),
     "cq_take_device_status": (_int, [ctypes.POINTER(_int), _vp]),
     "cq_selftest_bounded_wait": (_int, [_vp]),
     "cq_rotquant": (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _i64, _int, _vp, _vp, _vp, _vp]),
@@ -128,6 +133,11 @@ def call(name: str, *args) -> None:
 
 def exported_symbols() -> list[str]:
     return list(SIGNATURES)
+
+
+def set_gemm_variant(variant: int) -> None:
+    """Process-wide kernel form of the packed-int4-weight GEMMs (CQ_GEMM_AUTO, CQ_GEMM_ONE_SM, CQ_GEMM_PAIR)."""
+    call("cq_set_gemm_variant", int(variant))
 
 
 def take_device_status(stream=None) -> tuple[int, int]:

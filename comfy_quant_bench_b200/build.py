@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libcq_b200.so")
-SOURCES = ["libcq.cu", "rotquant.cu", "gemm_sm100.cu", "gemv.cu", "dit.cu", "selftest.cu", "capi.cu", "noalloc.cu", "kernels.cuh",
+SOURCES = ["libcq.cu", "rotquant.cu", "gemm_sm100.cu", "gemm_pair.cu", "gemv.cu", "dit.cu", "selftest.cu", "capi.cu", "noalloc.cu", "kernels.cuh",
            "cq_common.cuh"]
 HEADER = os.path.join(ROOT, "include", "cq_b200.h")
 

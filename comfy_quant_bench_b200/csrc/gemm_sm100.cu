@@ -858,50 +858,4 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
 
-int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int M, int N, int K, cudaStream_t st) {
-  GemmArgs g{};
-  g.sa = sa;
-  g.sb = sb;
-  g.bias = static_cast<const __nv_bfloat16*>(bias);
-  g.out = static_cast<__nv_bfloat16*>(out);
-  g.M = M; g.N = N; g.K = K;
-  if (b_format == CQ_B_INT8) return launch_gemm_t<EPI_ROWCOL, BF_S8, false>(a, b, nullptr, g, st);
-  if (a_kperm) return launch_gemm_t<EPI_ROWCOL, BF_S4, true>(a, b, nullptr, g, st);
-  return launch_gemm_t<EPI_ROWCOL, BF_S4, false>(a, b, nullptr, g, st);
-}
-
-// W4A4 row/col GEMM with the SwiGLU output: b holds the weight rows interleaved in groups of 32 (16 gate rows, then
-// their 16 up rows); out is bf16 [M, N / 2].
-int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
-                           void* out, int M, int N, int K, cudaStream_t st) {
-  GemmArgs g{};
-  g.sa = sa;
-  g.sb = sb;
-  g.bias = static_cast<const __nv_bfloat16*>(bias);
-  g.out = static_cast<__nv_bfloat16*>(out);
-  g.M = M; g.N = N; g.K = K;
-  return launch_gemm_t<EPI_ROWCOL, BF_S4, true, true>(a, b, nullptr, g, st);
-}
-
-int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
-                       const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
-                       cudaStream_t st, void* const* outs, int n_outs, int col0, int64_t ldo) {
-  // a few tokens (adaLN modulation): read the weights once with a warp per row instead of 256-token MMA tiles
-  if (outs == nullptr && gemv_affine_fits(M, a_kperm))
-    return launch_gemv_affine(a, sa, b, s, zt, bias, out, M, N, K, st) == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
-  GemmArgs g{};
-  g.sa = sa;
-  g.nz = rsplit_cols(K) / 64;
-  g.ws = static_cast<const __nv_bfloat16*>(s);
-  g.zt = static_cast<const __nv_bfloat16*>(zt);
-  g.bias = static_cast<const __nv_bfloat16*>(bias);
-  g.out = static_cast<__nv_bfloat16*>(out);
-  g.M = M; g.N = N; g.K = K;
-  const OutSpec spec{outs, n_outs, col0, ldo};
-  const OutSpec* sp = outs != nullptr ? &spec : nullptr;
-  if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st, sp);
-  return launch_gemm_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st, sp);
-}
-
 }  // namespace cq

@@ -2,6 +2,7 @@
 // same module (no relocatable device code needed).
 #include "rotquant.cu"
 #include "gemm_sm100.cu"
+#include "gemm_pair.cu"
 #include "gemv.cu"
 #include "dit.cu"
 #include "selftest.cu"

@@ -71,10 +71,25 @@ typedef enum {
   CQ_B_INT8 = 1          /* int8 [N, K] (int8_tensorwise, decoded W4A8)           */
 } cq_b_format;
 
+/* Kernel forms of the packed-int4-weight GEMMs (cq_gemm_affine, cq_gemm_rowcol with CQ_B_INT4_SIGNED, the fused
+ * linears and the SwiGLU-output GEMM). */
+typedef enum {
+  CQ_GEMM_AUTO = 0,    /* by shape: the CTA-pair kernel when M >= 1024 and there are at least 74 tiles of 256 x 256 */
+  CQ_GEMM_ONE_SM = 1,  /* one CTA per 128-weight-row x 256-token tile (tcgen05 cta_group::1)                        */
+  CQ_GEMM_PAIR = 2     /* a cluster of two CTAs per 256 x 256 tile (tcgen05 cta_group::2), half the activation
+                          operand's shared-memory traffic per SM and a deeper load ring                              */
+} cq_gemm_variant;
+
 /* Library version string, e.g. "cq_b200 0.1.0 sm_100a". */
 CQ_API const char* cq_version(void);
 /* Human-readable name of a cq_status code. */
 CQ_API const char* cq_status_string(int status);
+
+/* Select the GEMM kernel form for every later call in this process (cq_gemm_variant; the default is CQ_GEMM_AUTO).
+ * Both forms compute the same integer sums and the same epilogue, so results agree to the last bit.  A tuning and
+ * testing switch with no counterpart in the reference; it is process-wide and not synchronized with calls running
+ * on other host threads.  Returns CQ_OK or CQ_ERR_ARG. */
+CQ_API int cq_set_gemm_variant(int variant);
 
 /* Copy the device status word of the current device into status[0..1] (code, site) and clear it.
  * Synchronizes `stream`.  Returns CQ_OK or CQ_ERR_CUDA. */
