@@ -32,10 +32,11 @@ namespace pr {
 
 constexpr int kRowsCta = 128;          // weight rows per CTA (TMEM lanes); the pair covers 256
 constexpr int kRowsPair = 2 * kRowsCta;
-constexpr int kTok = 256;              // tokens per pair tile (MMA N; TMEM columns per accumulator buffer)
+constexpr int kTok = 256;              // tokens per pair tile (MMA N; TMEM columns per accumulator buffer); 128 (four
+                                       // buffers) also builds and passes, but measured 1.5x slower at the T shape
 constexpr int kTokCta = kTok / 2;      // tokens whose activation rows one CTA loads
 constexpr int kBK = 128;
-constexpr int kBufs = 2;
+constexpr int kBufs = 512 / kTok;     // accumulator buffers in the 512 TMEM columns
 constexpr int kWarpTok = kTok / 2;     // tokens per epilogue warp (two warps per TMEM lane quadrant)
 constexpr int kChunks = kWarpTok / 32;
 constexpr int kConvStages = 4;        // one converter warp per stage (warps 2..5)
@@ -50,7 +51,7 @@ constexpr unsigned long long kDrainNs = 50000000ull;   // per wait while unwindi
 
 template <int EPI>
 struct Plan {
-  static constexpr int kXStages = (EPI == EPI_AFFINE) ? 4 : 6;
+  static constexpr int kXStages = (EPI == EPI_AFFINE) ? (kTok == 256 ? 4 : 8) : (kTok == 256 ? 6 : 10);
   static constexpr int kX = 0;
   static constexpr int kW = kX + kXStages * kXBytes;
   static constexpr int kConv = kW + kWStages * kWpBytes;
@@ -403,21 +404,33 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
               acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
             }
           };
-          // software-pipelined drain: chunk c+1 in flight while chunk c is scaled; the buffer goes back to the
-          // leader as soon as the last chunk is in registers
-          tmem_ld_32x32b_x32(taddr, ra);
-          tmem_wait_ld_dep(ra);
-          tmem_ld_32x32b_x32(taddr + 32, rb);
-          scale_chunk(ra, 0);
-          tmem_wait_ld_dep(rb);
-          tmem_ld_32x32b_x32(taddr + 64, ra);
-          scale_chunk(rb, 1);
-          tmem_wait_ld_dep(ra);
-          tmem_ld_32x32b_x32(taddr + 96, rb);
-          scale_chunk(ra, 2);
-          tmem_wait_ld_dep(rb);
-          release(buf);
-          scale_chunk(rb, 3);
+          if constexpr (kChunks == 4) {
+            // software-pipelined drain: chunk c+1 in flight while chunk c is scaled; the buffer goes back to the
+            // leader as soon as the last chunk is in registers
+            tmem_ld_32x32b_x32(taddr, ra);
+            tmem_wait_ld_dep(ra);
+            tmem_ld_32x32b_x32(taddr + 32, rb);
+            scale_chunk(ra, 0);
+            tmem_wait_ld_dep(rb);
+            tmem_ld_32x32b_x32(taddr + 64, ra);
+            scale_chunk(rb, 1);
+            tmem_wait_ld_dep(ra);
+            tmem_ld_32x32b_x32(taddr + 96, rb);
+            scale_chunk(ra, 2);
+            tmem_wait_ld_dep(rb);
+            release(buf);
+            scale_chunk(rb, 3);
+          } else {
+            // both chunks in flight together; the buffer goes back to the leader one load latency after the group
+            // completed, before any of the math
+            tmem_ld_32x32b_x32(taddr, ra);
+            tmem_ld_32x32b_x32(taddr + 32, rb);
+            tmem_wait_ld_dep(ra);
+            tmem_wait_ld_dep(rb);
+            release(buf);
+            scale_chunk(ra, 0);
+            scale_chunk(rb, 1);
+          }
           if (++buf == kBufs) { buf = 0; buf_phase ^= 1u; }
         }
         if (!ok) break;

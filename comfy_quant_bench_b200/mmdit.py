@@ -185,44 +185,61 @@ class MMDiT:
         attention layout, GELU on bf16, gated residual as one fused multiply-add.  With ``fused_glue`` (kernel path
         only) the layer norm + modulation run inside the activation kernel of the QKV and MLP-up linears and the
         q/k RMSNorm + rotary + layout copies are one kernel; the reference path always runs the torch ops."""
+        temb_act = F.silu(temb.float()).to(torch.bfloat16)
+        for blk in self.blocks:
+            img, txt = self._block(blk, img, txt, temb_act, reference)
+        return img, txt
+
+    def block_errors(self, img: torch.Tensor, txt: torch.Tensor, temb: torch.Tensor) -> list[float]:
+        """Teacher-forced check: every block run by the kernel path and by the fp32-linear reference on the kernel
+        path's own input to that block; the rel-L2 of the two image-stream outputs (the larger stream) per block."""
+        temb_act = F.silu(temb.float()).to(torch.bfloat16)
+        errs = []
+        for blk in self.blocks:
+            ref_img, _ = self._block(blk, img, txt, temb_act, True)
+            img, txt = self._block(blk, img, txt, temb_act, False)
+            errs.append(rel_l2(img, ref_img))
+        return errs
+
+    def _block(self, blk, img: torch.Tensor, txt: torch.Tensor, temb_act: torch.Tensor, reference: bool):
+        """One dual-stream block on (img, txt); returns the new (img, txt)."""
         c = self.cfg
         h, nh, d = c.hidden, c.heads, c.head_dim
         fused = c.fused_glue and not reference
         st_txt, st_img = txt.shape[0], img.shape[0]
         s_all = st_txt + st_img
-        temb_act = F.silu(temb.float()).to(torch.bfloat16)
         q = torch.empty(1, nh, s_all, d, dtype=torch.bfloat16, device=img.device)
         k = torch.empty_like(q)
         v = torch.empty_like(q)
-        for si, st in self.blocks:
-            mi = self._mod(si, temb_act, reference).chunk(6, dim=-1)
-            mt = self._mod(st, temb_act, reference).chunk(6, dim=-1)
-            for x, s, m, rot, lo, hi in ((txt, st, mt, self.rope_txt, 0, st_txt),
-                                         (img, si, mi, self.rope_img, st_txt, s_all)):
-                if fused:
-                    y = s.qkv.lnmod(x, m[0], 1.0 + m[1])
-                    ops.qkv_rmsnorm_rope(y, s.q_norm, s.k_norm, rot, q, k, v, lo, eps=1e-6)
-                    continue
-                xn = torch.addcmul(m[0], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[1])
-                y = self._lin(s.qkv, xn, reference).view(x.shape[0], 3, nh, d)
-                q[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 0], (d,), s.q_norm, eps=1e-6), rot).transpose(0, 1)
-                k[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 1], (d,), s.k_norm, eps=1e-6), rot).transpose(0, 1)
-                v[0, :, lo:hi] = y[:, 2].transpose(0, 1)
+        si, st = blk
+        mi = self._mod(si, temb_act, reference).chunk(6, dim=-1)
+        mt = self._mod(st, temb_act, reference).chunk(6, dim=-1)
+        for x, s, m, rot, lo, hi in ((txt, st, mt, self.rope_txt, 0, st_txt),
+                                     (img, si, mi, self.rope_img, st_txt, s_all)):
             if fused:
-                a = torch.empty(s_all, h, dtype=torch.bfloat16, device=img.device)
-                ops.heads_to_rows(F.scaled_dot_product_attention(q, k, v), [a], 0, h)
+                y = s.qkv.lnmod(x, m[0], 1.0 + m[1])
+                ops.qkv_rmsnorm_rope(y, s.q_norm, s.k_norm, rot, q, k, v, lo, eps=1e-6)
+                continue
+            xn = torch.addcmul(m[0], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[1])
+            y = self._lin(s.qkv, xn, reference).view(x.shape[0], 3, nh, d)
+            q[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 0], (d,), s.q_norm, eps=1e-6), rot).transpose(0, 1)
+            k[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 1], (d,), s.k_norm, eps=1e-6), rot).transpose(0, 1)
+            v[0, :, lo:hi] = y[:, 2].transpose(0, 1)
+        if fused:
+            a = torch.empty(s_all, h, dtype=torch.bfloat16, device=img.device)
+            ops.heads_to_rows(F.scaled_dot_product_attention(q, k, v), [a], 0, h)
+        else:
+            a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
+        new = []
+        for x, s, m, att in ((txt, st, mt, a[:st_txt]), (img, si, mi, a[st_txt:])):
+            x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
+            if fused:
+                f = F.gelu(s.fc1.lnmod(x, m[3], 1.0 + m[4]), approximate="tanh")
             else:
-                a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
-            new = []
-            for x, s, m, att in ((txt, st, mt, a[:st_txt]), (img, si, mi, a[st_txt:])):
-                x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
-                if fused:
-                    f = F.gelu(s.fc1.lnmod(x, m[3], 1.0 + m[4]), approximate="tanh")
-                else:
-                    xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
-                    f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
-                new.append(torch.addcmul(x, m[5], self._lin(s.fc2, f, reference)))
-            txt, img = new
+                xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
+                f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
+            new.append(torch.addcmul(x, m[5], self._lin(s.fc2, f, reference)))
+        txt, img = new
         return img, txt
 
     def inputs(self, seed: int = 1):

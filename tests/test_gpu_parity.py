@@ -55,6 +55,15 @@ def codes_within_ties(got, want, frac=1e-3):
     assert (d > 0).mean() <= frac
 
 
+@pytest.fixture(params=["one_sm", "pair"])
+def gemm_variant(request, ops):
+    """Runs a test once per kernel form of the int4-weight GEMM (one CTA per tile, or a CTA pair per tile)."""
+    from comfy_quant_bench_b200 import _lib
+    _lib.set_gemm_variant(_lib.CQ_GEMM_ONE_SM if request.param == "one_sm" else _lib.CQ_GEMM_PAIR)
+    yield request.param
+    _lib.set_gemm_variant(_lib.CQ_GEMM_AUTO)
+
+
 def _check_status():
     from comfy_quant_bench_b200 import _lib
     torch.cuda.synchronize()
@@ -262,7 +271,7 @@ def _sparse_codes(rng, shape, density, lo, hi):
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 128, 128), (300, 200, 3072), (1000, 640, 1024)])
-def test_int32_accumulators_bit_exact_rowcol(ops, m, n, k):
+def test_int32_accumulators_bit_exact_rowcol(ops, gemm_variant, m, n, k):
     """Unit scales and sparse +-1 codes keep |acc| <= 256, exactly representable in bf16: out == acc."""
     rng = np.random.default_rng(m + n)
     a = _sparse_codes(rng, (m, k), 0.05, -1, 1).astype(np.int8)
@@ -279,7 +288,7 @@ def test_int32_accumulators_bit_exact_rowcol(ops, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 128, 128), (300, 200, 3072)])
-def test_int32_accumulators_bit_exact_affine(ops, m, n, k):
+def test_int32_accumulators_bit_exact_affine(ops, gemm_variant, m, n, k):
     """scale 1, zero 0: out == sum over groups of the exact int32 partials."""
     rng = np.random.default_rng(m * 3 + n)
     a = _sparse_codes(rng, (m, k), 0.05, -1, 1).astype(np.int8)
@@ -294,7 +303,7 @@ def test_int32_accumulators_bit_exact_affine(ops, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 128, 128), (300, 200, 3072), (64, 128, 4224)])
-def test_affine_zero_point_term_exact(ops, m, n, k):
+def test_affine_zero_point_term_exact(ops, gemm_variant, m, n, k):
     """scale 0, zero 1: out == sum_g R[g, m] (the tensor-core zero-point pass on the split group sums)."""
     rng = np.random.default_rng(m + k)
     a = _sparse_codes(rng, (m, k), 0.02, -1, 1).astype(np.int8)
@@ -311,7 +320,7 @@ def test_affine_zero_point_term_exact(ops, m, n, k):
 
 @pytest.mark.parametrize("m,n,k,bias", [(300, 200, 768, True), (512, 1024, 3072, True), (64, 384, 2048, False)])
 @pytest.mark.parametrize("kperm", [False, True])
-def test_gemm_rowcol_random_scales(ops, m, n, k, bias, kperm):
+def test_gemm_rowcol_random_scales(ops, gemm_variant, m, n, k, bias, kperm):
     rng = np.random.default_rng(k + m)
     a = rng.integers(-127, 128, size=(m, k)).astype(np.int8)
     b = rng.integers(-7, 8, size=(n, k)).astype(np.int8)
@@ -367,7 +376,7 @@ def test_int4_linear_matches_reference_policy0_golden(ops):
 # ----------------------------------------------------------------------------------------------
 
 @pytest.mark.parametrize("m,n,k,rot", [(300, 384, 1024, 256), (256, 3072, 3072, 0), (129, 256, 3072, 64)])
-def test_w4a8_affine_linear_vs_oracle(ops, m, n, k, rot):
+def test_w4a8_affine_linear_vs_oracle(ops, gemm_variant, m, n, k, rot):
     x = ref.synth_activations(m, k, seed=m)
     w = ref.synth_weight(n, k, seed=n)
     bb = ref.synth_bias(n, seed=3)
@@ -389,7 +398,7 @@ def test_w4a8_affine_linear_vs_oracle(ops, m, n, k, rot):
 
 @pytest.mark.parametrize("m,n,k,rot,dtype", [(300, 384, 1024, 256, "int4"), (64, 512, 3072, 64, "int8"),
                                              (200, 256, 768, 16, "int4")])
-def test_convrot_w4a4_linear_vs_oracle(ops, m, n, k, rot, dtype):
+def test_convrot_w4a4_linear_vs_oracle(ops, gemm_variant, m, n, k, rot, dtype):
     x = ref.synth_activations(m, k, seed=k)
     w = ref.synth_weight(n, k, seed=m)
     bb = ref.synth_bias(n, seed=5)
@@ -429,35 +438,57 @@ def test_int8_linear_vs_oracle(ops):
 # full benchmark size (M=4096, K=3072, N=12288): size-independent properties + a row slice against the oracle
 # ----------------------------------------------------------------------------------------------
 
-def test_full_size_w4a8_properties(ops):
-    m, n, k = 4096, 12288, 3072
-    x = ref.synth_activations(m, k, seed=0)
-    w = ref.synth_weight(n, k, seed=1)
-    xt = bf16_dev(x)
-    qw, sw, zw = ops.quantize_affine_w4_weight(torch.from_numpy(w).cuda(), 128, 256)
-    y1 = ops.w4a8_affine_linear(xt, qw, sw, zw, None, convrot_groupsize=256)
-    y2 = ops.w4a8_affine_linear(xt, qw, sw, zw, None, convrot_groupsize=256)
-    assert torch.equal(y1, y2), "two runs differ (shared-memory or TMEM race)"
-    y3 = ops.w4a8_affine_linear(xt * 2, qw, sw, zw, None, convrot_groupsize=256)
-    assert torch.equal(y3, y1 * 2), "output must scale exactly with a power-of-two input scale"
-    rows = np.r_[0:256, m - 256:m]
-    qx, sx = ref.rotquant(x[rows], 256, "int8")
-    qr, sr, zr = ref.weight_quant_affine(w, 256, 128)
-    assert np.array_equal(ref.unpack_uint4(qw.cpu().numpy()), qr)
-    want = ref.linear_affine(qx, sx, qr, sr, zr, None, 128)
-    got = y1[torch.from_numpy(rows).cuda()]
+def _full_size_affine_check(ops, m, n, k, rot, y, x, w, bias_bits):
+    """Row slices spread over all of M (eight slices of 64 rows, both ends included) against the oracle, with the
+    bias, plus the reference bench's own acceptance check per slice (g64_bench6.py:71-79, 154): rel-L2 < 3e-3 and
+    max |diff| < 4 % of the reference's standard deviation."""
+    starts = np.linspace(0, m - 64, 8).astype(int)
+    rows = np.concatenate([np.arange(s0, s0 + 64) for s0 in starts])
+    qx, sx = ref.rotquant(x[rows], rot, "int8")
+    qr, sr, zr = ref.weight_quant_affine(w, rot, 128)
+    want = ref.linear_affine(qx, sx, qr, sr, zr, ref.bf16_bits_to_f32(bias_bits), 128)
+    got = y[torch.from_numpy(rows).cuda()]
     assert_bf16_close(got, want)
-    # the reference's own acceptance check on the same two 256-row slices (g64_bench6.py:71-79, 154):
-    # rel-L2 < 3e-3 and max |diff| < 4 % of the reference's standard deviation, per slice
     g = f32_of(got).astype(np.float64)
-    for sl in (slice(0, 256), slice(256, 512)):
+    for i in range(len(starts)):
+        sl = slice(64 * i, 64 * i + 64)
         d = g[sl] - want[sl]
         assert np.linalg.norm(d) / np.linalg.norm(want[sl]) < 3e-3
         assert np.abs(d).max() / want[sl].std() < 0.04
+    return qr
+
+
+def test_full_size_w4a8_properties(ops, gemm_variant):
+    m, n, k = 4096, 12288, 3072
+    x = ref.synth_activations(m, k, seed=0)
+    w = ref.synth_weight(n, k, seed=1)
+    b = ref.synth_bias(n, seed=2)
+    xt, bt = bf16_dev(x), bf16_dev(b)
+    qw, sw, zw = ops.quantize_affine_w4_weight(torch.from_numpy(w).cuda(), 128, 256)
+    y1 = ops.w4a8_affine_linear(xt, qw, sw, zw, bt, convrot_groupsize=256)
+    y2 = ops.w4a8_affine_linear(xt, qw, sw, zw, bt, convrot_groupsize=256)
+    assert torch.equal(y1, y2), "two runs differ (shared-memory or TMEM race)"
+    y0 = ops.w4a8_affine_linear(xt, qw, sw, zw, None, convrot_groupsize=256)
+    y3 = ops.w4a8_affine_linear(xt * 2, qw, sw, zw, None, convrot_groupsize=256)
+    assert torch.equal(y3, y0 * 2), "output must scale exactly with a power-of-two input scale"
+    qr = _full_size_affine_check(ops, m, n, k, 256, y1, x, w, b)
+    assert np.array_equal(ref.unpack_uint4(qw.cpu().numpy()), qr)
     _check_status()
 
 
-def test_full_size_w4a4_properties(ops):
+def test_c1_at_its_own_shape_with_bias(ops, gemm_variant):
+    """BASELINE config 1 at its shape: W4A8 M=4096, N=K=3072, affine int4 g128, no rotation, bias."""
+    m, n, k = 4096, 3072, 3072
+    x = ref.synth_activations(m, k, seed=10)
+    w = ref.synth_weight(n, k, seed=11)
+    b = ref.synth_bias(n, seed=12)
+    qw, sw, zw = ops.quantize_affine_w4_weight(torch.from_numpy(w).cuda(), 128, 0)
+    y = ops.w4a8_affine_linear(bf16_dev(x), qw, sw, zw, bf16_dev(b), convrot_groupsize=0)
+    _full_size_affine_check(ops, m, n, k, 0, y, x, w, b)
+    _check_status()
+
+
+def test_full_size_w4a4_properties(ops, gemm_variant):
     m, n, k = 4096, 12288, 3072
     x = ref.synth_activations(m, k, seed=0)
     w = ref.synth_weight(n, k, seed=1)
@@ -515,7 +546,7 @@ def test_w4a8_affine_linear_few_tokens_vs_oracle(ops, m, n, k):
 # n % 64 == 0: 64-column boxes shared by two epilogue warps; n = 96: 32-column boxes (one warp each)
 @pytest.mark.parametrize("m,n,k,col0,ldo", [(300, 256, 1024, 256, 768), (1000, 640, 3072, 0, 1280),
                                             (130, 96, 1024, 32, 256), (77, 128, 512, 40, 256)])
-def test_affine_linear_into_several_buffers_at_an_offset(ops, m, n, k, col0, ldo):
+def test_affine_linear_into_several_buffers_at_an_offset(ops, gemm_variant, m, n, k, col0, ldo):
     """The column-parallel form writes this shard's columns into every output buffer at col0; the rest stays."""
     x = bf16_dev(ref.synth_activations(m, k, seed=11))
     w = torch.from_numpy(ref.synth_weight(n, k, seed=12)).cuda()
@@ -549,7 +580,7 @@ def test_affine_linear_into_rejects_bad_layouts(ops):
 
 @pytest.mark.parametrize("m,n,k,rot,dtype", [(300, 384, 1024, 256, "int4"), (4096, 12288, 3072, 64, "int4"),
                                              (77, 256, 512, 16, "int8")])
-def test_convrot_w4a4_swiglu_output_matches_torch_composite(ops, m, n, k, rot, dtype):
+def test_convrot_w4a4_swiglu_output_matches_torch_composite(ops, gemm_variant, m, n, k, rot, dtype):
     """The SwiGLU output fused into the W4A4 GEMM's epilogue equals torch's silu(y[:, :N/2]) * y[:, N/2:] on the
     bf16 output of the plain linear (same codes, same int32 sums, the same two bf16 roundings)."""
     import torch.nn.functional as F
