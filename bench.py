@@ -154,6 +154,50 @@ def allreduce_max(v: float, world: int) -> float:
     return float(t.item())
 
 
+def bind_to_gpu_numa_node(index: int):
+    """Pin this process's host threads to the CPUs of GPU `index`'s NUMA node, so that pinned host buffers allocated
+    and first touched afterwards live on the node whose PCIe root the GPU hangs off.  Returns the node, or None when
+    the topology cannot be read (the buffers then stay wherever the OS puts them)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        bus = pynvml.nvmlDeviceGetPciInfo(pynvml.nvmlDeviceGetHandleByIndex(index)).busId
+        bus = (bus.decode() if isinstance(bus, bytes) else bus).lower()
+        dom, rest = bus.split(":", 1)
+        path = f"/sys/bus/pci/devices/{dom[-4:]}:{rest}/numa_node"
+        node = int(open(path).read().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        os.sched_setaffinity(0, cpus)
+        return node
+    except Exception:  # noqa: BLE001 - reported as unknown
+        return None
+
+
+def copy_gbs(dst: torch.Tensor, src: torch.Tensor, stream, reps: int = 5) -> float:
+    """Achieved bandwidth of one host<->device copy of `src` into `dst` (median of reps, CUDA events)."""
+    ts = []
+    for _ in range(reps + 1):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dst.copy_(src, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return src.numel() * src.element_size() / (statistics.median(ts[1:]) / 1e3) / 1e9
+
+
+def gemm_kernel_name(workload: str, m: int, n: int) -> str:
+    """The GEMM kernel form the library's shape rule picks for this linear (cq_gemm_variant CQ_GEMM_AUTO)."""
+    pair = m >= 1024 and ((m + 255) // 256) * ((n + 255) // 256) >= 74
+    epi = "rowcol" if workload == "w4a4" else "affine"
+    return f"gemm_pair_kernel<{epi}> (CTA pair, tcgen05 cta_group::2)" if pair else f"gemm_kernel<{epi}> (one SM)"
+
+
 def make_problem(workload: str, seed: int, dev):
     from oracle import ref  # synthetic inputs only (seeded: N(0,1) activations with 1% outlier channels x20, N(0,0.02) weights)
     from comfy_quant_bench_b200 import ops
@@ -310,8 +354,13 @@ def run_ours(args, world, rank, local):
     # (copy stream), runs the op (compute stream; L2 flushed first), and copies its output back to pinned host memory
     # (a second copy stream).  Double buffers let step i's output copy overlap step i+1's input copy and op (the copy
     # engines run both directions at once); every step's copies are inside the timed region.
+    numa_node = bind_to_gpu_numa_node(local)
     x_host = x.cpu().pin_memory()
     y_hosts = [torch.empty(m, n, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for yh in y_hosts:
+        yh.zero_()   # first touch on the GPU's node
+    h2d_gbs = copy_gbs(torch.empty_like(x), x_host, stream)
+    d2h_gbs = copy_gbs(y_hosts[0], torch.empty(m, n, dtype=torch.bfloat16, device=dev), stream)
     x_devs = [torch.empty_like(x) for _ in range(2)]
     s_in, s_c, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     e2e_steps = max(3, min(args.steps, 50))
@@ -373,6 +422,24 @@ def run_ours(args, world, rank, local):
     except Exception as exc:  # noqa: BLE001
         lib_int8 = {"unavailable": str(exc).splitlines()[0][:200]}
 
+    # The multi-GPU designs, measured beside the replicas of the headline line: the fused column-parallel linear
+    # (strong scaling of the same linear over the ranks, gather inside the GEMM) at N > 1, and the 60-block MMDiT step
+    # as data-parallel replicas at every N.  Every rank takes part; rank 0 reports.
+    subrecords = {}
+    if args.workload == "w4a8" and args.mode == "dp" and not args.no_subrecords:
+        if world > 1:
+            import copy
+            a2 = copy.copy(args)
+            a2.mode, a2.steps, a2.warmup = "tp_fused", min(args.steps, 20), max(3, min(args.warmup, 5))
+            xs, _, ws, bs = make_problem("w4a8", seed=0, dev=dev)
+            tl = run_tp(a2, world, rank, local, xs, ws, bs, emit=False)
+            subrecords["tp_fused"] = {k: tl.get(k) for k in ("value", "unit", "ms_per_step", "per_gpu_tops",
+                                                             "gather_check", "nvlink_gbs_per_rank", "scaling")}
+            subrecords["tp_fused"]["parallelism"] = f"tp{world}"
+            del xs, ws, bs
+            torch.cuda.empty_cache()
+        subrecords["mmdit_step"] = mmdit_dp_subrecord(world, rank, local)
+
     if rank != 0:
         return
     peaks = _peaks()
@@ -398,10 +465,11 @@ def run_ours(args, world, rank, local):
         "breakdown_ms": {"rotquant": quant_ms, "gemm": gemm_ms},
         "step_ms_spread": {"median": statistics.median(per_step), "min": min(per_step), "max": max(per_step),
                            "of": "rank 0's device-timed steps (activation kernel + GEMM)"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<rowcol>" if args.workload == "w4a4" else "gemm_kernel<affine>",
+        "roofline": {"bound": "tensor", "kernel": gemm_kernel_name(args.workload, m, n),
                      "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
                      "peak_source": f"2 x {peaks['source']} dense bf16 ({peaks['bf16_tflops']} TFLOP/s; B200 int8 "
                                     "dense rate is twice bf16)",
+                     "frac_vs_library_int8": (achieved / lib_int8["tops"]) if "tops" in lib_int8 else None,
                      "traffic": traffic,
                      "algorithmic": f"2*M*N*K = {ops_per_step:.4g} int-ops per launch"},
         "rotquant_roofline": {"bound": "hbm", "achieved": act_bytes / (quant_ms / 1e3) / 1e9,
@@ -410,7 +478,9 @@ def run_ours(args, world, rank, local):
                               "algorithmic_bytes": act_bytes},
         "library_int8_gemm": lib_int8,
         "e2e": {"value": e2e_val, "unit": "TOPS", "ms_per_step": e2e_ms, "h2d_bytes_per_step": m * k * 2,
-                "d2h_bytes_per_step": m * n * 2,
+                "d2h_bytes_per_step": m * n * 2, "h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs,
+                "copy_bound_ms": max(m * k * 2 / h2d_gbs, m * n * 2 / d2h_gbs) / 1e6,
+                "pinned_host_numa_node": numa_node,
                 "path": ("ops.w4a8_affine_linear (C ABI cq_linear_w4a8_affine)" if args.workload != "w4a4" else
                          "ops.convrot_w4a4_linear (C ABI cq_linear_convrot_w4a4)") +
                         " with pinned host buffers; each step's input copy, op (after an L2 flush) and output copy run "
@@ -418,14 +488,16 @@ def run_ours(args, world, rank, local):
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
+    line.update(subrecords)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline("w4a8" if args.workload == "w4a4" else args.workload, args.cpu_rows,
                                             args.cpu_steps)
     print(json.dumps(line), flush=True)
 
 
-def run_tp(args, world, rank, local, x, weights, bias):
-    """Column-parallel linear: rotquant on every rank, the local N/P GEMM, NCCL all-gather of the bf16 output."""
+def run_tp(args, world, rank, local, x, weights, bias, emit=True):
+    """Column-parallel linear: rotquant on every rank, the local N/P GEMM, NCCL all-gather of the bf16 output.
+    Returns the JSON line (printed by rank 0 when ``emit``)."""
     import torch.distributed as dist
     from comfy_quant_bench_b200 import ops, _lib, dist as cqdist
     dev = torch.device("cuda", local)
@@ -514,8 +586,50 @@ def run_tp(args, world, rank, local, x, weights, bias):
     }
     if gather_check is not None:
         line["gather_check"] = gather_check
-    if rank == 0:
+    if fused is not None and world > 1:
+        # every rank sends its [M, N/P] block to the P - 1 other ranks over NVLink
+        sent = m * nl * 2 * (world - 1)
+        line["nvlink_gbs_per_rank"] = sent / (total_ms / args.steps / 1e3) / 1e9
+    if rank == 0 and emit:
         print(json.dumps(line), flush=True)
+    return line
+
+
+def mmdit_dp_subrecord(world, rank, local, steps: int = 5, warmup: int = 3) -> dict:
+    """The 60-block MMDiT step (fused glue, every linear W4A8) as data-parallel replicas, one CUDA graph per rank:
+    step latency = max over ranks of the mean replay time; throughput = ranks / step latency."""
+    from comfy_quant_bench_b200 import mmdit as mm
+    dev = torch.device("cuda", local)
+    model = mm.MMDiT(mm.MMDiTConfig(), device=dev, seed=0)
+    img, txt, temb = model.inputs(seed=1 + rank)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        model.step(img, txt, temb)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        model.step(img, txt, temb)
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        model.step(img, txt, temb)
+    graph.replay()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    for e0, e1 in evs:
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    step_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in evs), world) / steps
+    del graph, model
+    torch.cuda.empty_cache()
+    return {"workload": "mmdit_step (60 blocks, hidden 3072, 4096 + 256 tokens, every linear W4A8, fused glue)",
+            "parallelism": f"dp{world}", "step_ms": step_ms, "steps_per_s": world / (step_ms / 1e3),
+            "timing": f"{steps} graph replays per rank after {warmup} warm-up steps, max over ranks"}
 
 
 def run_mmdit(args, world, rank, local):
@@ -869,6 +983,8 @@ def main():
                     help="tokens per timed CPU call (default: the workload's M, the real call)")
     ap.add_argument("--cpu-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="skip the fused column-parallel and MMDiT-step measurements beside the headline line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
