@@ -58,6 +58,7 @@ SIGNATURES = {
     "cq_gemm_rowcol": (_int, [_vp, _int, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "cq_group_sum_cols": (_i64, [_i64]),
     "cq_prepare_affine_zeros": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
+    "cq_gemm_groupwise": (_int, [_vp, _int, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_gemm_affine": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_linear_workspace_bytes": (_i64, [_i64, _i64]),
     "cq_linear_convrot_w4a4": (_int, [_vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),

@@ -223,6 +223,22 @@ int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b,
                                 static_cast<int>(K), static_cast<cudaStream_t>(stream));
 }
 
+int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, int64_t sa_ld, const void* b_packed,
+                      const float* sb_g, const void* bias, void* out, int64_t M, int64_t N, int64_t K, int group,
+                      void* stream) {
+  if (group != 128) return CQ_ERR_ARG;
+  if (a_kperm != 0 && a_kperm != 1) return CQ_ERR_ARG;
+  if (int e = check_gemm(a, b_packed, out, M, N, K)) return e;
+  if (M == 0) return CQ_OK;
+  if (K > kMaxK) return CQ_ERR_SHAPE;
+  if (sa_ld < M || sa_ld % 4 != 0 || sa_ld > kMaxRows) return CQ_ERR_SHAPE;
+  if (sa_g == nullptr || sb_g == nullptr) return CQ_ERR_ARG;
+  if (!aligned(sa_g, 16) || !aligned(sb_g, 4)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  return cq::launch_gemm_group(a, a_kperm, sa_g, sa_ld, b_packed, sb_g, bias, out, static_cast<int>(M),
+                               static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
+}
+
 int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                    const void* s_bf16, const void* zt_bf16, const void* bias, void* out, int64_t M, int64_t N,
                    int64_t K, int group, void* stream) {

@@ -49,9 +49,15 @@ constexpr int kWuBytes = kRowsCta * kBK;        // 16 KB unpacked
 constexpr int kWStages = 6;
 constexpr unsigned long long kDrainNs = 50000000ull;   // per wait while unwinding (50 ms)
 
+// per-group drains (affine and group scales) keep the output staging of the TMA stores
+template <int EPI>
+constexpr bool kPerGroup = (EPI == EPI_AFFINE || EPI == EPI_GROUP);
+constexpr int kSgStages = 4;                   // group epilogue: ring of per-group token scales
+constexpr int kSgBytes = kTok * 4;             //   one stage: the tile's tokens' scales of one group (f32)
+
 template <int EPI>
 struct Plan {
-  static constexpr int kXStages = (EPI == EPI_AFFINE) ? (kTok == 256 ? 4 : 8) : (kTok == 256 ? 6 : 10);
+  static constexpr int kXStages = kPerGroup<EPI> ? (kTok == 256 ? 4 : 8) : (kTok == 256 ? 6 : 10);
   static constexpr int kX = 0;
   static constexpr int kW = kX + kXStages * kXBytes;
   static constexpr int kConv = kW + kWStages * kWpBytes;
@@ -61,8 +67,10 @@ struct Plan {
   static constexpr int kSaBytes = 8 * kWarpTok * 4;
   static constexpr int kOut = kSa + kSaBytes;
   static constexpr int kOutWarpBytes = 64 * 32 * 2;
-  static constexpr int kOutBytes = (EPI == EPI_AFFINE) ? 8 * kOutWarpBytes : 0;
-  static constexpr int kBytes = kOut + kOutBytes + 1024 /*align slack*/;
+  static constexpr int kOutBytes = kPerGroup<EPI> ? 8 * kOutWarpBytes : 0;
+  static constexpr int kSg = kOut + kOutBytes;
+  static constexpr int kSgRingBytes = (EPI == EPI_GROUP) ? kSgStages * kSgBytes : 0;
+  static constexpr int kBytes = kSg + kSgRingBytes + 1024 /*align slack*/;
 };
 
 // every ring stage of a ring of n stages that `issued` loads reached: wait (bounded) for the last load's phase
@@ -102,9 +110,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
   uint64_t* box_full = box_free + 4;              // [4]
   uint64_t* mma_done = box_full + 4;              // [1] the leader's last commit: every MMA of the pair completed
   uint64_t* exit_bar = mma_done + 1;              // [1] the peer CTA finished with the pair's memory
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(exit_bar + 1);
+  uint64_t* sg_full = exit_bar + 1;               // [4] group: a group's token scales landed (TMA)
+  uint64_t* sg_empty = sg_full + kSgStages;       // [4] group: the 8 epilogue warps used them
+  const float* sm_sg = reinterpret_cast<const float*>(smem + P::kSg);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sg_empty + kSgStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  static_assert((2 * kXS + 2 * kWStages + 3 * kConvStages + 2 * kBufs + 10) * 8 + 8 <= P::kBarBytes,
+  static_assert((2 * kXS + 2 * kWStages + 3 * kConvStages + 2 * kBufs + 10 + 2 * kSgStages) * 8 + 8 <= P::kBarBytes,
                 "barriers, the TMEM address and the abort flag fit their region");
 
   const int warp = threadIdx.x >> 5;
@@ -143,10 +154,15 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
     }
     mbar_init(mma_done, 1);
     mbar_init(exit_bar, 1);
+    for (int q = 0; q < kSgStages; ++q) {
+      mbar_init(&sg_full[q], 1);
+      mbar_init(&sg_empty[q], 8);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tm_x);
     prefetch_tensormap(&tm_w);
+    if (EPI == EPI_GROUP) prefetch_tensormap(&tm_r);
     if (EPI == EPI_AFFINE) {
       prefetch_tensormap(&tm_r);
       prefetch_tensormap(&tm_z);
@@ -169,8 +185,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
     if (warp == 0 && lane == 0) {
       // ------------------------------ TMA producer ------------------------------
-      int xs = 0, ws = 0;
-      uint32_t xph = 0, wph = 0, x_issued = 0, w_issued = 0;
+      int xs = 0, ws = 0, gs = 0;
+      uint32_t xph = 0, wph = 0, gph = 0, x_issued = 0, w_issued = 0, g_issued = 0;
       bool ok = true;
       for (int item = pair_id; item < num_tiles && ok; item += num_pairs) {
         int mt, nt;
@@ -196,11 +212,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
           tma_load_2d(sm_x + xs * kXBytes, &tm_x, &full_x[xs], kb * kBK, m0);
           ++x_issued;
           if (++xs == kXS) { xs = 0; xph ^= 1u; }
+          if (EPI == EPI_GROUP) {
+            // group kb's scales of the tile's 256 tokens (both CTAs' epilogues cover all of them)
+            if (!(ok = mbar_wait(&sg_empty[gs], gph ^ 1u, abort_flag, 43))) break;
+            mbar_arrive_expect_tx(&sg_full[gs], kSgBytes);
+            tma_load_2d(const_cast<float*>(sm_sg) + gs * kTok, &tm_r, &sg_full[gs], mt * kTok, kb);
+            ++g_issued;
+            if (++gs == kSgStages) { gs = 0; gph ^= 1u; }
+          }
         }
       }
       // every load issued has landed before this CTA's shared memory can be released (a no-op on a normal end)
       drain_ring(full_x, kXS, x_issued);
       drain_ring(full_w, kWStages, w_issued);
+      if (EPI == EPI_GROUP) drain_ring(sg_full, kSgStages, g_issued);
     } else if (warp == 1 && lane == 0 && rank == 0) {
       // ------------------------------ MMA issuer (leader) ------------------------------
       const uint32_t idesc = idesc_i8(kRowsPair, kTok);
@@ -240,8 +265,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
           if (++buf == kBufs) { buf = 0; bph ^= 1u; }
         }
         for (int kb = 0; kb < kblocks && ok; ++kb) {
-          // affine: every group has its own accumulator buffer; row/col: one buffer per tile
-          const bool new_buf = (EPI == EPI_AFFINE) || kb == 0;
+          // affine / group scales: every group has its own accumulator buffer; row/col: one buffer per tile
+          const bool new_buf = kPerGroup<EPI> || kb == 0;
           if (!(ok = (new_buf ? buffer_and_operands_ready(46) : operands_ready(47)))) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kTok);
@@ -249,13 +274,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
           const uint32_t b_base = smem_u32(sm_x + xs * kXBytes);
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
-            // affine: every 128-wide group starts its own int32 sum
-            const uint32_t acc = (EPI == EPI_AFFINE) ? (k > 0) : (kb > 0 || k > 0);
+            // per-group drains: every 128-wide group starts its own int32 sum
+            const uint32_t acc = kPerGroup<EPI> ? (k > 0) : (kb > 0 || k > 0);
             mma_i8_pair(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc, acc);
           }
           tc_commit_pair(&empty_x[xs]);
           tc_commit_pair(&empty_conv[cs]);
-          if (EPI == EPI_AFFINE) {
+          if (kPerGroup<EPI>) {
             tc_commit_pair(&tmem_full[buf]);
             if (++buf == kBufs) { buf = 0; bph ^= 1u; }
           }
@@ -341,6 +366,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
     uint32_t box_pass = 0;
     int buf = 0;
     uint32_t buf_phase = 0;
+    int sg_stage = 0;                     // group scales: position in the producer's ring of token-scale stages
+    uint32_t sg_phase = 0;
     bool ok = true;
     auto release = [&](int b) {
       tc_fence_before();
@@ -359,16 +386,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
       float sa_pre[kChunks];
 #pragma unroll
-      for (int c = 0; c < kChunks; ++c) sa_pre[c] = __ldg(args.sa + min(m0 + 32 * c + lane, M - 1));
+      for (int c = 0; c < kChunks; ++c)   // group scales carry the tokens' scales per group: the final factor is 1
+        sa_pre[c] = (EPI == EPI_GROUP) ? 1.0f : __ldg(args.sa + min(m0 + 32 * c + lane, M - 1));
       auto stage_sa = [&]() {
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) sa_stage[32 * c + lane] = sa_pre[c];
         __syncwarp();
       };
-      if constexpr (EPI == EPI_AFFINE) {
+      if constexpr (kPerGroup<EPI>) {
         float2 acc[kWarpTok / 2];
-        {
+        if constexpr (EPI == EPI_GROUP) {
+#pragma unroll
+          for (int j = 0; j < kWarpTok / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
+        } else {
           // starting value: the zero-point term sum_g z[g, n] * R[g, m], accumulated in fp32 by the tensor core
           if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 51))) break;
           tc_fence_after();
@@ -384,29 +415,44 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
           release(buf);
           if (++buf == kBufs) { buf = 0; buf_phase ^= 1u; }
         }
-        // the weight scale of the next group is loaded one group ahead as raw bf16 bits and converted at use
-        const unsigned short* ws_bits = reinterpret_cast<const unsigned short*>(args.ws) + n;
-        unsigned short s_bits_next = n_ok ? __ldg(ws_bits) : static_cast<unsigned short>(0);
+        // the weight scale of the next group is loaded one group ahead as raw bits and converted at use (affine:
+        // bf16 [K/128, N]; group scales: f32 [K/128, N])
+        auto load_wscale = [&](int gg) -> uint32_t {
+          if (!n_ok) return 0u;
+          if constexpr (EPI == EPI_GROUP) return __float_as_uint(__ldg(args.sbg + static_cast<int64_t>(gg) * N + n));
+          else return __ldg(reinterpret_cast<const unsigned short*>(args.ws) + static_cast<int64_t>(gg) * N + n);
+        };
+        uint32_t s_bits_next = load_wscale(0);
         for (int g = 0; g < kblocks; ++g) {
-          const unsigned short s_bits = s_bits_next;
-          if (g + 1 < kblocks && n_ok) s_bits_next = __ldg(ws_bits + static_cast<int64_t>(g + 1) * N);
+          const uint32_t s_bits = s_bits_next;
+          if (g + 1 < kblocks) s_bits_next = load_wscale(g + 1);
           if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 52))) break;
           tc_fence_after();
-          const float s = bf16_bits_to_f32(s_bits) * wscale_fold;
+          const float s = (EPI == EPI_GROUP ? __uint_as_float(s_bits) : bf16_bits_to_f32(s_bits)) * wscale_fold;
           const float2 s2 = make_float2(s, s);
           const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kTok + half * kWarpTok);
+          // group scales: this group's scales of the warp's 128 tokens, staged by the producer
+          const float* sg_tok = sm_sg + sg_stage * kTok + half * kWarpTok;
+          if (EPI == EPI_GROUP && !(ok = mbar_wait(&sg_full[sg_stage], sg_phase, abort_flag, 59))) break;
           uint32_t ra[32], rb[32];
           auto scale_chunk = [&](const uint32_t (&r)[32], int ch) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               // |P| < 2^22, so the int32 -> fp32 conversion is exact
               const float2 p = make_float2(__int2float_rn(static_cast<int>(r[2 * j])), __int2float_rn(static_cast<int>(r[2 * j + 1])));
-              acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
+              if constexpr (EPI == EPI_GROUP) {
+                // the reference's order: t = P * s_w rounded once, then acc += t * s_a[token] with one rounding
+                const float2 t = ffma2(s2, p, make_float2(0.0f, 0.0f));
+                const float2 a = *reinterpret_cast<const float2*>(sg_tok + 32 * ch + 2 * j);
+                acc[16 * ch + j] = ffma2(t, a, acc[16 * ch + j]);
+              } else {
+                acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
+              }
             }
           };
           if constexpr (kChunks == 4) {
             // software-pipelined drain: chunk c+1 in flight while chunk c is scaled; the buffer goes back to the
-            // leader as soon as the last chunk is in registers
+            // leader as soon as the last chunk is in registers (two rounds of two loads measured the same)
             tmem_ld_32x32b_x32(taddr, ra);
             tmem_wait_ld_dep(ra);
             tmem_ld_32x32b_x32(taddr + 32, rb);
@@ -432,6 +478,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
             scale_chunk(rb, 1);
           }
           if (++buf == kBufs) { buf = 0; buf_phase ^= 1u; }
+          if constexpr (EPI == EPI_GROUP) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sg_empty[sg_stage]);   // this warp is done with the group's token scales
+            if (++sg_stage == kSgStages) { sg_stage = 0; sg_phase ^= 1u; }
+          }
         }
         if (!ok) break;
         stage_sa();
@@ -577,7 +628,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
     }
   }
 
-  if (EPI == EPI_AFFINE && warp >= kEpiWarp0 && lane == 0) bulk_wait_group0();
+  if (kPerGroup<EPI> && warp >= kEpiWarp0 && lane == 0) bulk_wait_group0();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -635,6 +686,10 @@ static int launch_gemm_pair_t(const int8_t* a, const void* b, const void* rsplit
     if (!make_map_u8(&tm_r, rsplit, args.M, 2 * rsplit_cols(args.K), 128, pr::kTokCta, true)) return CQ_ERR_CUDA;
     if (!make_map_u8(&tm_z, args.zt, args.N, 128 * static_cast<int64_t>(args.nz), 128, pr::kRowsCta, true))
       return CQ_ERR_CUDA;
+  } else if (EPI == EPI_GROUP) {
+    // the tokens' per-group scales [K/128, sag_ld] f32: one box = one group's scales of a tile's 256 tokens
+    if (!make_map_f32(&tm_r, rsplit, args.K / 128, args.sag_ld, pr::kTok, 1)) return CQ_ERR_CUDA;
+    tm_z = tm_x;
   } else {
     tm_r = tm_x;
     tm_z = tm_x;
@@ -648,13 +703,13 @@ static int launch_gemm_pair_t(const int8_t* a, const void* b, const void* rsplit
   std::memset(&tm_out, 0, sizeof(tm_out));
   ga.out_w64 = (outs != nullptr && args.N % 64 == 0) ? 1 : 0;
   const int box_cols = ga.out_w64 ? 64 : 32;
-  if (EPI == EPI_AFFINE && outs != nullptr) {
+  if (pr::kPerGroup<EPI> && outs != nullptr) {
     for (int i = 0; i < outs->n; ++i)
       if (!make_map_bf16(&tm_out.m[i], outs->ptrs[i], args.M, outs->ldo, box_cols, 64)) return CQ_ERR_CUDA;
     ga.tma_out = 1;
     ga.n_out = outs->n;
     ga.out_col0 = outs->col0;
-  } else if (EPI == EPI_AFFINE && args.N % 8 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0) {
+  } else if (pr::kPerGroup<EPI> && args.N % 8 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0) {
     if (!make_map_bf16(&tm_out.m[0], args.out, args.M, args.N, box_cols, 64)) return CQ_ERR_CUDA;
     ga.tma_out = 1;
     ga.n_out = 1;
@@ -753,6 +808,20 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   }
   if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st, sp);
   return launch_gemm_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st, sp);
+}
+
+// Per-group scales on both sides (the reference's policy 4): int4 activation codes (int8-held) x packed signed int4
+// weights, acc += round(P_g * sbg[g, n]) * sag[g, m] in fp32 over the 128-wide groups g, then + bias -> bf16.
+int launch_gemm_group(const int8_t* a, int a_kperm, const float* sag, int64_t sag_ld, const void* b, const float* sbg,
+                      const void* bias, void* out, int M, int N, int K, cudaStream_t st) {
+  GemmArgs g{};
+  g.sbg = sbg;
+  g.sag_ld = sag_ld;
+  g.bias = static_cast<const __nv_bfloat16*>(bias);
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.M = M; g.N = N; g.K = K;
+  if (a_kperm) return launch_gemm_pair_t<EPI_GROUP, BF_S4, true>(a, b, sag, g, st);
+  return launch_gemm_pair_t<EPI_GROUP, BF_S4, false>(a, b, sag, g, st);
 }
 
 }  // namespace cq

@@ -53,7 +53,9 @@ constexpr int kWpBytes = kBW * kBK / 2;     //  8 KB (packed int4)
 constexpr int kProducerRegs = 40;    // warps 0-7 (producer, MMA, converters)
 constexpr int kEpilogueRegs = 216;   // warps 8-15; 256*40 + 256*216 = 128*512, the launch allocation
 
-enum : int { EPI_ROWCOL = 0, EPI_AFFINE = 1 };
+// ROWCOL: per-token x per-row scales once per tile (the reference's policy 0); AFFINE: per-group weight scale and
+// zero, per-token activation scale; GROUP: per-group scales on both sides (the reference's policy 4, CTA-pair kernel)
+enum : int { EPI_ROWCOL = 0, EPI_AFFINE = 1, EPI_GROUP = 2 };
 enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 
 // shared-memory plan per epilogue and weight format.  The affine kernel trades one TMA stage for the output
@@ -81,7 +83,9 @@ struct OutMaps {
 };
 
 struct GemmArgs {
-  const float* sa;       // [M] activation scale
+  const float* sa;       // [M] activation scale (rowcol, affine)
+  const float* sbg;      // [K/128, N] f32 per-group weight scale (group)
+  int64_t sag_ld;        // group: row stride (elements) of the tokens' per-group scales [K/128, sag_ld] f32
   const float* sb;       // [N] weight scale (rowcol)
   const __nv_bfloat16* ws;  // [K/128, N] bf16 (affine)
   const __nv_bfloat16* zt;  // [N, 64*nz] bf16 (affine): Zt[n, j] = z[j mod G, n] for j < 2G, else 0
@@ -767,6 +771,20 @@ static bool make_map_bf16(CUtensorMap* map, void* base, int64_t rows, int64_t co
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// 2-D f32 tensor map over [rows, cols] (row stride cols * 4 bytes, a multiple of 16), box box_cols x box_rows.
+static bool make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

@@ -70,6 +70,9 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st, void* const* outs = nullptr, int n_outs = 0, int col0 = 0, int64_t ldo = 0);
 cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t st);
+// per-group scales on both sides (policy 4): sag f32 [K/128, sag_ld], sbg f32 [K/128, N]; CTA-pair kernel
+int launch_gemm_group(const int8_t* a, int a_kperm, const float* sag, int64_t sag_ld, const void* b, const float* sbg,
+                      const void* bias, void* out, int M, int N, int K, cudaStream_t st);
 // process-wide kernel choice for the packed-int4-weight GEMMs (cq_gemm_variant values)
 int set_gemm_variant(int variant);
 // failure-path self-test: two waits on mbarriers nothing arrives on; sites kSelftestSite and kSelftestSite + 1

@@ -234,6 +234,70 @@ def int4_linear(qact: torch.Tensor, qweight: torch.Tensor, x_scale: torch.Tensor
     return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
 
 
+def gemm_groupwise(a: torch.Tensor, sa_g: torch.Tensor, b: torch.Tensor, sb_g: torch.Tensor, bias=None, *,
+                   m: int | None = None, a_kperm: bool = False) -> torch.Tensor:
+    """Per-group scales on both sides (the reference GEMM's policy 4, ``g64_gemm6.cu:5-7, 228-229``):
+    out = sum_g round(P_g * sb_g[g, n]) * sa_g[g, m] + bias -> bf16 [m, N], accumulated over the 128-wide groups
+    in order.  a int4 values as int8 codes [M_pad, K]; sa_g f32 [K/128, M_pad]; b packed int4 [N, K/2];
+    sb_g f32 [K/128, N]."""
+    dev = _require_cuda(a, sa_g, b, sb_g, bias)
+    mp, k = a.shape
+    m = mp if m is None else int(m)
+    n = b.shape[0]
+    if 2 * b.shape[1] != k:
+        raise ValueError(f"Input K={k} does not match weight K={2 * b.shape[1]}")
+    if sa_g.shape[0] != k // 128 or sb_g.shape != (k // 128, n):
+        raise ValueError("sa_g must be [K/128, M_pad] and sb_g [K/128, N]")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    sa_g = sa_g.float().contiguous()
+    _lib.call("cq_gemm_groupwise", _ptr(a), int(bool(a_kperm)), _ptr(sa_g), sa_g.shape[1], _ptr(b),
+              _ptr(sb_g.float().contiguous()), _ptr(_bias_bf16(bias)), _ptr(out), m, n, k, 128, _stream(dev))
+    return out
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, ca=None, cw=None, bias=None,
+         pol: int = 0, cfg=None) -> torch.Tensor:
+    """The reference GEMM's interface, ``g64_gemm6.gemm(a, b, sa, sb, ca, cw, bias, pol, cfg)``
+    (``experiments/qwen21-kernel/kernels/g64_gemm6.cu:383-411``), for the policies built here:
+
+    * pol 0: row x column, sa [M] f32, sb [N] f32;
+    * pol 4: g128 x g128, sa [K/128, M_pad] f32 (the per-group quantizer's layout), sb [K/128, N] f32.
+
+    a packed int4 [M_pad, K/2]; b packed int4 [N, K/2]; bias bf16 [N] or empty; returns bf16 [M_pad, N].  ``ca``,
+    ``cw`` (the integer-ratio policies' operands) and ``cfg`` (the reference's tile configuration) are accepted and
+    not used: the integer-ratio policies 5/7/15/17 are not built and raise."""
+    dev = _require_cuda(a, b, sa, sb)
+    if bias is not None and bias.numel() == 0:
+        bias = None
+    mp, kh = a.shape
+    a8 = torch.empty(mp, 2 * kh, dtype=torch.int8, device=dev)
+    _lib.call("cq_unpack_int4", _ptr(a.contiguous()), mp, 2 * kh, _ptr(a8), _stream(dev))
+    if pol == 0:
+        return gemm_rowcol(a8, sa.reshape(-1), b.contiguous(), sb.reshape(-1), bias)
+    if pol == 4:
+        return gemm_groupwise(a8, sa, b.contiguous(), sb, bias)
+    raise ValueError(f"policy {pol} is not built (0 and 4 are)")
+
+
+def w4a4_groupwise_linear(x: torch.Tensor, qweight: torch.Tensor, sb_g: torch.Tensor, bias=None,
+                          swiglu: bool = False) -> torch.Tensor:
+    """The reference node's forward with policy 4 (``experiments/qwen21-kernel/node/__init__.py:152-187``): the
+    per-group quantizer (ConvRot-256, int4 per token and 128-wide group, bf16-up scales) on x (or on silu(gate) * up
+    of x = [gate | up] with ``swiglu``), then the g128 x g128 GEMM.  The activation codes go to the GEMM as int8 in
+    the K order the int4 weights unpack into, so nothing is packed and unpacked in between.  x [..., K] (or 2K)."""
+    dev = _require_cuda(x, qweight, sb_g, bias)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    k = 2 * qweight.shape[1]
+    mp = (m + 127) // 128 * 128
+    q, sa_g, _ = rotquant(x2, 256, _lib.CQ_ACT_INT4_GROUP, swiglu=swiglu, act_group=128, m_pad=mp,
+                          int4_as_int8=True, kperm=True)
+    if q.shape[1] != k:
+        raise ValueError(f"Input K={q.shape[1]} does not match weight K={k}")
+    y = gemm_groupwise(q, sa_g, qweight, sb_g, bias, m=m, a_kperm=True)
+    return y.reshape(*x.shape[:-1], y.shape[-1])
+
+
 def _workspace(m: int, k: int, dev) -> torch.Tensor:
     nbytes = int(_lib.load().cq_linear_workspace_bytes(m, k))
     return torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)

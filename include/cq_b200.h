@@ -182,6 +182,24 @@ CQ_API int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const v
                           void* stream);
 
 /*
+ * Per-group scales on both sides, the reference GEMM's policy 4
+ * (experiments/qwen21-kernel/kernels/g64_gemm6.cu:5-7, 228-229, 383-411; called from
+ * experiments/qwen21-kernel/node/__init__.py:152-187 after the per-group quantizer quant(x, 128, swiglu, pad)):
+ *   out[m, n] = bf16( sum_g ( round(P_g[m,n] * sb_g[g,n]) * sa_g[g,m] ) + bias[n] ),  P_g = sum_{k in g} a[m,k]*b[n,k]
+ * accumulated in fp32 over g = 0..K/128-1 in order, each step one fused multiply-add, as the reference's epilogue
+ * acc = fma(fma(D, w, -M*w), a, acc) does.
+ *   a       int4 activation values held as int8 codes [M, K] (cq_rotquant CQ_ACT_INT4_GROUP with CQ_Q_INT8_CODES;
+ *           a_kperm as for cq_gemm_rowcol)
+ *   sa_g    f32 [K/128, sa_ld] (the per-group quantizer's scale layout), sa_ld >= M, sa_ld % 4 == 0
+ *   b       packed signed int4 [N, K/2] (cq_weight_rotquant CQ_W_INT4_GROUP_BF16UP);  sb_g f32 [K/128, N]
+ *   bias    bf16 [N] or NULL;  out bf16 [M, N];  group 128
+ * Runs the CTA-pair GEMM whatever cq_set_gemm_variant selected.
+ */
+CQ_API int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, int64_t sa_ld, const void* b_packed,
+                             const float* sb_g, const void* bias, void* out, int64_t M, int64_t N, int64_t K, int group,
+                             void* stream);
+
+/*
  * W4A8 affine linear, the headline GEMM:
  *   out[m, n] = bf16( sa[m] * sum_g ( s[g,n] * sum_{k in g} a[m,k]*(q[n,k]-8) + z[g,n] * gsum[g,m] ) + bias[n] )
  * with q the awq_w4a16 uint4 codes (packed [N, K/2]), s bf16 [K/group, N] and the zeros z passed as zt, the

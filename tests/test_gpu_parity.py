@@ -604,3 +604,66 @@ def test_swiglu_output_rows_interleave_tiles(ops):
     assert idx[:16].tolist() == list(range(16)) and idx[16:32].tolist() == list(range(128, 144))
     assert idx[32:48].tolist() == list(range(16, 32)) and idx[240:].tolist() == list(range(240, 256))
     assert sorted(idx.tolist()) == list(range(256))
+
+
+# ----------------------------------------------------------------------------------------------
+# per-group scales on both sides (the reference GEMM's policy 4)
+# ----------------------------------------------------------------------------------------------
+
+def test_groupwise_gemm_matches_reference_policy4_golden(ops):
+    """The reference's own policy-4 outputs (g64_bench6.ref on its seeded inputs, committed by make_golden.py)."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_golden.npz"))
+    a, b = g["gemm_a"], g["gemm_b"]
+    out = ops.gemm(torch.from_numpy(g["gemm_a_packed"]).cuda(), torch.from_numpy(ref.pack_int4(b)).cuda(),
+                   torch.from_numpy(g["gemm_p4_sa"]).cuda(), torch.from_numpy(g["gemm_p4_sb"]).cuda(),
+                   bias=bf16_dev(g["gemm_bias"]), pol=4)
+    assert out.shape == (a.shape[0], b.shape[0])
+    assert_bf16_close(out, g["gemm_p4_out"])
+    _check_status()
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (384, 512, 1024), (1000, 768, 3072)])
+def test_groupwise_gemm_vs_oracle_with_reference_acceptance(ops, m, n, k):
+    """Random int4 codes and per-group scales: the oracle's float64 policy-4 product, with the reference bench's
+    rule on the first and last 256 rows (g64_bench6.py:71-79: rel-L2 < 3e-3, max |diff| < 4 % of the std) and two
+    runs bit-identical."""
+    rng = np.random.default_rng(m + n + k)
+    a = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
+    b = rng.integers(-8, 8, size=(n, k)).astype(np.int8)
+    sa = rng.uniform(0.005, 0.015, size=(k // 128, m)).astype(np.float32)
+    sb = ref.bf16_round(rng.uniform(0.005, 0.015, size=(k // 128, n)).astype(np.float32))
+    bias = ref.synth_bias(n, seed=5)
+    args = (torch.from_numpy(a).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(ref.pack_int4(b)).cuda(),
+            torch.from_numpy(sb).cuda(), bf16_dev(bias))
+    y1 = ops.gemm_groupwise(*args)
+    y2 = ops.gemm_groupwise(*args)
+    assert torch.equal(y1, y2)
+    rows = np.r_[0:min(256, m), max(0, m - 256):m]
+    want = ref.linear_groupwise(a[rows], sa[:, rows], b, sb, ref.bf16_bits_to_f32(bias), 128)
+    got = y1[torch.from_numpy(rows).cuda()]
+    assert_bf16_close(got, want)
+    gv = f32_of(got).astype(np.float64)
+    half = len(rows) // 2
+    for sl in (slice(0, half), slice(half, len(rows))):
+        d = gv[sl] - want[sl]
+        assert np.linalg.norm(d) / np.linalg.norm(want[sl]) < 3e-3
+        assert np.abs(d).max() / want[sl].std() < 0.04
+    _check_status()
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_groupwise_linear_matches_the_node_path(ops, swiglu):
+    """The node's policy-4 forward: per-group quantizer (ConvRot-256, g128, bf16-up scales), then the GEMM, against
+    the oracle's quantizers and policy-4 product on the same inputs."""
+    m, n, k = 300, 384, 1024
+    x = ref.synth_activations(m, 2 * k if swiglu else k, seed=21)
+    w = ref.synth_weight(n, k, seed=22)
+    bias = ref.synth_bias(n, seed=23)
+    qw, sw = ops.quantize_int4_groupwise_weight(torch.from_numpy(w).cuda(), 128, 256)
+    y = ops.w4a4_groupwise_linear(bf16_dev(x), qw, sw, bf16_dev(bias), swiglu=swiglu)
+    qa, sa = ref.rotquant(x, 256, "int4_group", swiglu=swiglu, act_group=128)
+    qr, sr = ref.weight_quant_groupwise_bf16up(w, 256, 128)
+    want = ref.linear_groupwise(qa, sa, qr, sr, ref.bf16_bits_to_f32(bias), 128)
+    assert_bf16_close(y, want, rel=2e-3 if swiglu else REL_L2)
+    _check_status()
