@@ -41,6 +41,8 @@ constexpr int kWarpTok = kTok / 2;     // tokens per epilogue warp (two warps pe
 constexpr int kChunks = kWarpTok / 32;
 constexpr int kConvStages = 4;        // one converter warp per stage (warps 2..5)
 constexpr int kConvWarp0 = 2;
+constexpr int kTmemWarp = 6;           // allocates and releases the pair's TMEM (warps 6-7 have no other role)
+constexpr int kRoleWarps = 14;         // warps 0, 1, the 4 converters and the 8 epilogue warps
 constexpr int kThreads = 512;
 constexpr int kEpiWarp0 = 8;
 constexpr int kXBytes = kTokCta * kBK;          // 16 KB
@@ -112,10 +114,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
   uint64_t* exit_bar = mma_done + 1;              // [1] the peer CTA finished with the pair's memory
   uint64_t* sg_full = exit_bar + 1;               // [4] group: a group's token scales landed (TMA)
   uint64_t* sg_empty = sg_full + kSgStages;       // [4] group: the 8 epilogue warps used them
+  uint64_t* cta_done = sg_empty + kSgStages;      // [1] every role warp of this CTA finished (14 arrivals)
   const float* sm_sg = reinterpret_cast<const float*>(smem + P::kSg);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sg_empty + kSgStages);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(cta_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  static_assert((2 * kXS + 2 * kWStages + 3 * kConvStages + 2 * kBufs + 10 + 2 * kSgStages) * 8 + 8 <= P::kBarBytes,
+  static_assert((2 * kXS + 2 * kWStages + 3 * kConvStages + 2 * kBufs + 11 + 2 * kSgStages) * 8 + 8 <= P::kBarBytes,
                 "barriers, the TMEM address and the abort flag fit their region");
 
   const int warp = threadIdx.x >> 5;
@@ -154,6 +157,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
     }
     mbar_init(mma_done, 1);
     mbar_init(exit_bar, 1);
+    mbar_init(cta_done, kRoleWarps);
     for (int q = 0; q < kSgStages; ++q) {
       mbar_init(&sg_full[q], 1);
       mbar_init(&sg_empty[q], 8);
@@ -170,8 +174,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
         for (int i = 0; i < args.n_out; ++i) prefetch_tensormap(&tm_out.m[i]);
     }
   }
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_holder, 512);   // collective: warp 1 of each CTA of the pair
+  if (warp == kTmemWarp) {
+    tmem_alloc_pair(tmem_holder, 512);   // collective: this warp of each CTA of the pair
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -183,6 +187,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
 
   if (warp < kEpiWarp0) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    // Lanes with no role leave now (the CTA's closing barrier waits only for threads that have not exited): a warp
+    // whose lane 0 loops while its other lanes sit at that barrier measurably delayed the epilogue warps of its SM
+    // sub-partition.  Warp kTmemWarp stays whole for the collective TMEM release at the end.
+    if ((warp <= 1 && lane != 0) || (warp > kConvWarp0 + kConvStages - 1 && warp != kTmemWarp)) return;
     if (warp == 0 && lane == 0) {
       // ------------------------------ TMA producer ------------------------------
       int xs = 0, ws = 0, gs = 0;
@@ -630,9 +638,16 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
 
   if (kPerGroup<EPI> && warp >= kEpiWarp0 && lane == 0) bulk_wait_group0();
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
+  if (warp != kTmemWarp) {
+    // this warp's role is done (its TMEM reads ordered before by the fence above)
+    __syncwarp(__activemask());
+    if (lane == 0) mbar_arrive(cta_done);
+    return;
+  }
+  {
     if (lane == 0) {
+      // every role warp of this CTA has finished (bounded: an aborted CTA's roles still arrive)
+      mbar_wait_drain(cta_done, 0u, kWaitLimitNs);
       // the leader's last commit: every MMA of the pair has completed (bounded: an aborted leader still commits)
       mbar_wait_drain(mma_done, 0u, kDrainNs);
       // tell the other CTA that this one is done with the pair's memory, and wait until it is done too
