@@ -679,12 +679,13 @@ def run_wan(args, world, rank, local):
 
 def run_ltx(args, world, rank, local):
     """One LTX-like video DiT step (48 blocks, hidden 4096, 32,768 tokens, every linear W4A8), tensor-parallel over
-    the ranks (head-parallel attention, column-parallel projections / MLP with the gather inside the GEMM).  Eager
-    (the symmetric-memory barriers are not captured in a graph); device-timed, max over ranks."""
+    the ranks: head-parallel attention and column-parallel MLP-up, row-parallel output projections and MLP-down
+    with NCCL all-reduces (``--ltx-gather``: every linear column-parallel with the gather inside the GEMM).  Eager;
+    device-timed, max over ranks."""
     from comfy_quant_bench_b200 import ltx, _lib, mmdit as mm
     dev = torch.device("cuda", local)
     cfg = ltx.LTXConfig(blocks=args.ltx_blocks)
-    model = ltx.LTXDiT(cfg, device=dev, seed=0, rank=rank, world=world)
+    model = ltx.LTXDiT(cfg, device=dev, seed=0, rank=rank, world=world, row_parallel=not args.ltx_gather)
     x, ctx = model.inputs(seed=1)              # the same activation on every rank (one step, split by columns)
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -731,8 +732,12 @@ def run_ltx(args, world, rank, local):
                    "ctx_tokens": cfg.ctx_tokens, "batch": 1,
                    "linears": "every linear W4A8 affine g128, ConvRot g256",
                    "parallelism": f"tp{world}" if world > 1 else "1 GPU",
-                   "sharding": "head-parallel attention (QKV / cross Q, KV rows by head, heads_to_rows peer gather); "
-                               "column-parallel out projections and MLP (gather inside the GEMM)" if world > 1 else None,
+                   "sharding": ("head-parallel attention (QKV / cross Q, KV rows by head) and column-parallel MLP-up "
+                                "(GELU in its epilogue), all rank-local; row-parallel output projections and MLP-down "
+                                "(per-token maxima all-reduced (MAX) before quantization, bf16 partial products "
+                                "all-reduced (SUM) over NCCL)" if model.row_parallel else
+                                "head-parallel attention (heads_to_rows peer gather); column-parallel out projections "
+                                "and MLP (gather inside the GEMM)") if world > 1 else None,
                    "l2": "weights larger than L2", "graph": "none (eager)"},
         "step_latency_ms": step_ms,
         "linear_int_ops_per_step": lin_ops, "attention_flops_per_step": model.attention_flops(),
@@ -978,6 +983,9 @@ def main():
                     help="keep the adaLN modulation linears in bf16 (the reference's profiles exclude them)")
     ap.add_argument("--wan-blocks", type=int, default=30)
     ap.add_argument("--ltx-blocks", type=int, default=48)
+    ap.add_argument("--ltx-gather", action="store_true",
+                    help="LTX at N>1: every linear column-parallel with the gather inside the GEMM, instead of "
+                         "row-parallel output projections and MLP-down with all-reduces")
     ap.add_argument("--no-reference-check", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=4096,
                     help="tokens per timed CPU call (default: the workload's M, the real call)")

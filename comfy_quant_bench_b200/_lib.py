@@ -40,10 +40,23 @@ CQ_GEMM_AUTO = 0
 CQ_GEMM_ONE_SM = 1
 CQ_GEMM_PAIR = 2
 
+CQ_OUT_PLAIN = 0
+CQ_OUT_GELU_TANH = 1
+CQ_OUT_GATED_RESIDUAL = 2
+
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _vp = ctypes.c_void_p
 _f32 = ctypes.c_float
+
+
+class CQOutOp(ctypes.Structure):
+    """cq_out_op: the output operation of the W4A8 affine GEMM's epilogue."""
+    _fields_ = [("kind", ctypes.c_int), ("residual", ctypes.c_void_p), ("residual_ld", ctypes.c_int64),
+                ("gate", ctypes.c_void_p)]
+
+
+_opp = ctypes.POINTER(CQOutOp)
 
 # name -> (restype, argtypes), one line per declaration of include/cq_b200.h
 SIGNATURES = {
@@ -60,6 +73,7 @@ SIGNATURES = {
     "cq_prepare_affine_zeros": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
     "cq_gemm_groupwise": (_int, [_vp, _int, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_gemm_affine": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "cq_gemm_affine_op": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _opp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_linear_workspace_bytes": (_i64, [_i64, _i64]),
     "cq_linear_convrot_w4a4": (_int, [_vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "cq_linear_w4a8_affine": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64,
@@ -73,6 +87,10 @@ SIGNATURES = {
     "cq_rotquant_lnmod": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _f32, _i64, _int, _vp, _vp, _vp, _vp]),
     "cq_linear_w4a8_affine_lnmod": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _f32, _vp, _vp, _vp, _int, _vp,
                                            _vp, _vp, _i64, _vp]),
+    "cq_linear_w4a8_op": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _f32, _vp, _vp, _vp, _int, _vp, _opp, _vp,
+                                 _vp, _i64, _vp]),
+    "cq_rotquant_absmax": (_int, [_vp, _i64, _i64, _int, _i64, _vp, _vp]),
+    "cq_rotquant_scaled": (_int, [_vp, _i64, _i64, _int, _vp, _i64, _int, _vp, _vp, _vp, _vp]),
     "cq_qkv_rmsnorm_rope": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "cq_heads_to_rows": (_int, [_vp, _i64, _int, _int, _vp, _int, _i64, _i64, _vp]),
     "cq_gemm_rowcol_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),

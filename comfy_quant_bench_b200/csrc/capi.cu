@@ -125,6 +125,42 @@ int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const 
   return cuda_status(cq::launch_act_rotquant(rot_group, false, CQ_ACT_INT8_ROW, a, static_cast<cudaStream_t>(stream)));
 }
 
+// the two phases of per-token int8 activations for a row-parallel linear (K split over ranks)
+static int check_sharded_act(const void* x, int64_t M, int64_t K, int rot_group, int64_t M_pad) {
+  if (M < 0 || M_pad < M || M_pad > kMaxRows) return CQ_ERR_SHAPE;
+  if (K < 256 || K % 256 != 0 || K > kMaxLnModK) return CQ_ERR_SHAPE;
+  if (!valid_rot(rot_group)) return CQ_ERR_ARG;
+  if (M > 0 && x == nullptr) return CQ_ERR_ARG;
+  if (!aligned(x, 16)) return CQ_ERR_ALIGN;
+  return CQ_OK;
+}
+
+int cq_rotquant_absmax(const void* x, int64_t M, int64_t K, int rot_group, int64_t M_pad, float* amax, void* stream) {
+  if (int e = check_sharded_act(x, M, K, rot_group, M_pad)) return e;
+  if (M_pad == 0) return CQ_OK;
+  if (amax == nullptr) return CQ_ERR_ARG;
+  if (!aligned(amax, 4)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), 0, 0, 0, nullptr, nullptr, nullptr, nullptr,
+                     cq::rsplit_cols(static_cast<int>(K))};
+  a.amax_out = amax;
+  return cuda_status(cq::launch_act_rotquant(rot_group, false, CQ_ACT_INT8_ROW, a, static_cast<cudaStream_t>(stream)));
+}
+
+int cq_rotquant_scaled(const void* x, int64_t M, int64_t K, int rot_group, const float* amax, int64_t M_pad,
+                       int flags, void* q, float* scale, void* group_sums, void* stream) {
+  if (int e = check_sharded_act(x, M, K, rot_group, M_pad)) return e;
+  if (flags & ~CQ_Q_KPERM) return CQ_ERR_ARG;
+  if (M_pad == 0) return CQ_OK;
+  if (amax == nullptr || q == nullptr || scale == nullptr) return CQ_ERR_ARG;
+  if (!aligned(amax, 4) || !aligned(q, 16) || !aligned(scale, 4) || !aligned(group_sums, 16)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), 0, 0, (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
+                     static_cast<__nv_bfloat16*>(group_sums), cq::rsplit_cols(static_cast<int>(K))};
+  a.amax_in = amax;
+  return cuda_status(cq::launch_act_rotquant(rot_group, false, CQ_ACT_INT8_ROW, a, static_cast<cudaStream_t>(stream)));
+}
+
 int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm, float eps,
                         const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0, void* stream) {
   if (S < 0 || S > kMaxRows || H < 1 || H > 4096 || (D != 64 && D != 128)) return CQ_ERR_SHAPE;
@@ -211,8 +247,17 @@ static int check_gemm(const void* a, const void* b, const void* out, int64_t M, 
   return CQ_OK;
 }
 
+static int gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
+                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl);
+
 int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
                    const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+  return gemm_rowcol(a, a_kperm, sa, b, b_format, sb, bias, out, M, N, K, stream, false);
+}
+
+// pdl: the fused linears launch the GEMM as a programmatic dependent of their activation kernel
+static int gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
+                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl) {
   if (b_format != CQ_B_INT4_SIGNED && b_format != CQ_B_INT8) return CQ_ERR_ARG;
   if (a_kperm != 0 && (a_kperm != 1 || b_format == CQ_B_INT8)) return CQ_ERR_ARG;
   if (int e = check_gemm(a, b, out, M, N, K)) return e;
@@ -220,7 +265,7 @@ int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b,
   if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
   if (int dv = check_device()) return dv;
   return cq::launch_gemm_rowcol(a, a_kperm, sa, b, b_format, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
-                                static_cast<int>(K), static_cast<cudaStream_t>(stream));
+                                static_cast<int>(K), static_cast<cudaStream_t>(stream), pdl);
 }
 
 int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, int64_t sa_ld, const void* b_packed,
@@ -239,9 +284,45 @@ int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, int64_t s
                                static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
 }
 
+static int gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                       const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
+                       int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl);
+
 int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                    const void* s_bf16, const void* zt_bf16, const void* bias, void* out, int64_t M, int64_t N,
                    int64_t K, int group, void* stream) {
+  return gemm_affine(a, a_kperm, sa, gsplit, b_packed, s_bf16, zt_bf16, bias, nullptr, out, M, N, K, group, stream,
+                     false);
+}
+
+// the output operation of cq_gemm_affine_op: a known kind and, for the gated residual, a residual that is either
+// the output itself (same rows) or wholly apart from it
+static int check_out_op(const cq_out_op* op, const void* out, int64_t M, int64_t N) {
+  if (op == nullptr || op->kind == CQ_OUT_PLAIN) return CQ_OK;
+  if (op->kind != CQ_OUT_GELU_TANH && op->kind != CQ_OUT_GATED_RESIDUAL) return CQ_ERR_ARG;
+  // the operations run in the epilogue's staged (TMA-store) output path
+  if (N % 8 != 0) return CQ_ERR_SHAPE;
+  if (!aligned(out, 16)) return CQ_ERR_ALIGN;
+  if (op->kind == CQ_OUT_GELU_TANH) return CQ_OK;
+  if (op->residual == nullptr || op->gate == nullptr) return CQ_ERR_ARG;
+  if (op->residual_ld < N || op->residual_ld > (int64_t(1) << 31)) return CQ_ERR_SHAPE;
+  if (!aligned(op->residual, 2) || !aligned(op->gate, 2)) return CQ_ERR_ALIGN;
+  const uintptr_t r0 = reinterpret_cast<uintptr_t>(op->residual), o0 = reinterpret_cast<uintptr_t>(out);
+  if (r0 == o0) return op->residual_ld == N ? CQ_OK : CQ_ERR_ARG;
+  const uintptr_t r1 = r0 + static_cast<uintptr_t>(((M - 1) * op->residual_ld + N) * 2);
+  const uintptr_t o1 = o0 + static_cast<uintptr_t>(M * N * 2);
+  return (r1 <= o0 || o1 <= r0) ? CQ_OK : CQ_ERR_ARG;
+}
+
+int cq_gemm_affine_op(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                      const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
+                      int64_t M, int64_t N, int64_t K, int group, void* stream) {
+  return gemm_affine(a, a_kperm, sa, gsplit, b_packed, s_bf16, zt_bf16, bias, op, out, M, N, K, group, stream, false);
+}
+
+static int gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                       const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
+                       int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl) {
   if (group != 128) return CQ_ERR_ARG;
   if (a_kperm != 0 && a_kperm != 1) return CQ_ERR_ARG;
   if (int e = check_gemm(a, b_packed, out, M, N, K)) return e;
@@ -249,9 +330,13 @@ int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gs
   if (K > kMaxK) return CQ_ERR_SHAPE;
   if (sa == nullptr || gsplit == nullptr || s_bf16 == nullptr || zt_bf16 == nullptr) return CQ_ERR_ARG;
   if (!aligned(gsplit, 16) || !aligned(zt_bf16, 16)) return CQ_ERR_ALIGN;
+  if (int e = check_out_op(op, out, M, N)) return e;
   if (int dv = check_device()) return dv;
+  cq::OutOp o{};
+  if (op != nullptr) o = cq::OutOp{op->kind, op->residual, op->residual_ld, op->gate};
   return cq::launch_gemm_affine(a, a_kperm, sa, gsplit, b_packed, s_bf16, zt_bf16, bias, out, static_cast<int>(M),
-                                static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
+                                static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream), nullptr,
+                                0, 0, 0, &o, pdl);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -297,18 +382,26 @@ int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int r
   if (int e = cq_rotquant(x, M, K, rot_group, swiglu, mode, 0, w.mpad, CQ_Q_INT8_CODES | CQ_Q_KPERM, w.xq, w.sx,
                           nullptr, stream))
     return e;
-  return cq_gemm_rowcol(w.xq, 1, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream);
+  return gemm_rowcol(w.xq, 1, w.sx, qweight, CQ_B_INT4_SIGNED, wscale, bias, out, M, N, K, stream, true);
 }
+
+static int gemm_rowcol_swiglu(const int8_t* a, const float* sa, const void* b_glu, const float* sb, const void* bias,
+                              void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl);
 
 int cq_gemm_rowcol_swiglu(const int8_t* a, const float* sa, const void* b_glu, const float* sb, const void* bias,
                           void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+  return gemm_rowcol_swiglu(a, sa, b_glu, sb, bias, out, M, N, K, stream, false);
+}
+
+static int gemm_rowcol_swiglu(const int8_t* a, const float* sa, const void* b_glu, const float* sb, const void* bias,
+                              void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl) {
   if (N % 128 != 0) return CQ_ERR_SHAPE;            // whole 128-row weight tiles of 16-gate + 16-up row groups
   if (int e = check_gemm(a, b_glu, out, M, N, K)) return e;
   if (M == 0) return CQ_OK;
   if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
   if (int dv = check_device()) return dv;
   return cq::launch_gemm_rowcol_glu(a, sa, b_glu, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
-                                    static_cast<int>(K), static_cast<cudaStream_t>(stream));
+                                    static_cast<int>(K), static_cast<cudaStream_t>(stream), pdl);
 }
 
 int cq_linear_convrot_w4a4_swiglu(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int act_bits,
@@ -323,7 +416,7 @@ int cq_linear_convrot_w4a4_swiglu(const void* x, int64_t M, int64_t K, int64_t N
   if (int e = cq_rotquant(x, M, K, rot_group, 0, mode, 0, w.mpad, CQ_Q_INT8_CODES | CQ_Q_KPERM, w.xq, w.sx, nullptr,
                           stream))
     return e;
-  return cq_gemm_rowcol_swiglu(w.xq, w.sx, qweight_glu, wscale_glu, bias_glu, out, M, N, K, stream);
+  return gemm_rowcol_swiglu(w.xq, w.sx, qweight_glu, wscale_glu, bias_glu, out, M, N, K, stream, true);
 }
 
 int cq_gemm_affine_peers(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
@@ -373,7 +466,8 @@ int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int ro
   if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
                           stream))
     return e;
-  return cq_gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, out, M, N, K, group, stream);
+  return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, nullptr, out, M, N, K, group, stream,
+                     true);
 }
 
 int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
@@ -386,7 +480,25 @@ int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, 
   if (int e = cq_rotquant_lnmod(x, M, K, rot_group, shift, scale1p, eps, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
                                 stream))
     return e;
-  return cq_gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, out, M, N, K, group, stream);
+  return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, nullptr, out, M, N, K, group, stream,
+                     true);
+}
+
+int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
+                      const void* scale1p, float eps, const void* qweight, const void* s_bf16, const void* zt_bf16,
+                      int group, const void* bias, const cq_out_op* op, void* out, void* workspace,
+                      int64_t workspace_bytes, void* stream) {
+  if (M == 0) return CQ_OK;
+  if (int e = check_out_op(op, out, M, N)) return e;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  const int e = shift != nullptr
+                    ? cq_rotquant_lnmod(x, M, K, rot_group, shift, scale1p, eps, w.mpad, CQ_Q_KPERM, w.xq, w.sx,
+                                        w.gsplit, stream)
+                    : cq_rotquant(x, M, K, rot_group, 0, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
+                                  stream);
+  if (e) return e;
+  return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, op, out, M, N, K, group, stream, true);
 }
 
 int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,
@@ -397,7 +509,7 @@ int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
   if (int e = cq_rotquant(x, M, K, rot_group, swiglu, CQ_ACT_INT8_ROW, 0, w.mpad, 0, w.xq, w.sx, nullptr, stream))
     return e;
-  return cq_gemm_rowcol(w.xq, 0, w.sx, weight, CQ_B_INT8, wscale, bias, out, M, N, K, stream);
+  return gemm_rowcol(w.xq, 0, w.sx, weight, CQ_B_INT8, wscale, bias, out, M, N, K, stream, true);
 }
 
 }  // extern "C"

@@ -45,6 +45,16 @@ __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch.  grid_dep_launch: this CTA no longer holds back the launch of the next kernel in
+// the stream (when that kernel was launched with programmatic stream serialization, it may start once every CTA of
+// this grid has called this or exited).  grid_dep_wait: block until the previous kernel in the stream has completed
+// and its memory operations are visible (returns at once for a kernel launched without the attribute).
+// a cache-line prefetch into L2 (no register result, nothing waits on it)
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
 }

@@ -84,7 +84,7 @@ __device__ __forceinline__ void drain_ring(uint64_t* full, int n, uint32_t issue
   }
 }
 
-template <int EPI, int BFMT, bool KPERM, bool GLU>
+template <int EPI, int BFMT, bool KPERM, bool GLU, int OP>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                  const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_z,
@@ -92,6 +92,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
   using P = Plan<EPI>;
   static_assert(BFMT == BF_U4 || BFMT == BF_S4, "the pair kernel converts packed int4 weights");
   static_assert(!GLU || EPI == EPI_ROWCOL, "the SwiGLU output is a row/col epilogue");
+  static_assert(OP == OUT_PLAIN || EPI == EPI_AFFINE, "output operations are affine-epilogue variants");
   constexpr int kXS = P::kXStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -184,6 +185,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  grid_dep_wait();   // inputs written by the previous kernel (programmatic launch) are visible from here on
 
   if (warp < kEpiWarp0) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
@@ -392,6 +394,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
       const bool n_ok = n < N;
       const bool m_full = m0 + kWarpTok <= M;
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
+      if constexpr (OP == OUT_GATED) {
+        // the warp's residual box (its 128 tokens x 32 columns) into L2 now, a whole tile of group drains before
+        // the store passes read it
+        const int c0 = n - lane;
+        if (c0 < N)
+          for (int r = lane; r < kWarpTok && m0 + r < M; r += 32)
+            prefetch_l2(args.res + static_cast<int64_t>(m0 + r) * args.res_ld + c0);
+      }
       float sa_pre[kChunks];
 #pragma unroll
       for (int c = 0; c < kChunks; ++c)   // group scales carry the tokens' scales per group: the final factor is 1
@@ -497,8 +507,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
         if (args.tma_out) {
           // two passes of 64 tokens through a per-warp staging buffer and TMA tensor stores (see the one-SM kernel;
           // with out_w64 two warps share one 64-column box)
-          auto store_passes = [&](auto row_bytes_c) -> bool {
+          auto store_passes = [&](auto row_bytes_c, auto op_c) -> bool {
             constexpr uint32_t kRow = decltype(row_bytes_c)::value;
+            constexpr int kOp = decltype(op_c)::value;
             constexpr bool kPair = kRow == 128;
             const int owner = kPair ? (e & ~1) : e;
             unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOut + owner * P::kOutWarpBytes);
@@ -522,12 +533,42 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
               // written after them would wait for them and expose its whole latency on every step
               const float4* sa4 = reinterpret_cast<const float4*>(sa_stage + 64 * pass);
               float4 c0 = sa4[0], c1 = sa4[1];
+              // gated residual: this lane's column of the pass's 64 residual rows, in batches of kResBatch rows issued
+              // kResAhead batches ahead of their use
+              // (one pointer walked down the rows; lanes past N read column N - 1 and rows past M repeat the last
+              // row, neither of which is stored)
+              uint32_t rres[kOp == OUT_GATED ? 64 : 1];
+              // the column's gate, loaded here rather than with the bias so that no register holds it across the
+              // tile's group drains
+              const float gate = (kOp == OUT_GATED && n_ok) ? __bfloat162float(args.gate[n]) : 0.0f;
+              const unsigned short* rp = nullptr;
+              int rows_left = 0;
+              if constexpr (kOp == OUT_GATED) {
+                rows_left = M - (m0 + 64 * pass);
+                rp = reinterpret_cast<const unsigned short*>(args.res) + min(n, N - 1) +
+                     static_cast<int64_t>(m0 + 64 * pass) * args.res_ld;
+              }
+              auto load_res = [&](int b) {
+                if constexpr (kOp == OUT_GATED) {
+#pragma unroll
+                  for (int i = 0; i < kResBatch; ++i) {
+                    rres[kResBatch * b + i] = __ldg(rp);
+                    if (kResBatch * b + i + 1 < rows_left) rp += args.res_ld;
+                  }
+                }
+              };
+#pragma unroll
+              for (int b = 0; b < kResAhead; ++b) load_res(b);
 #pragma unroll
               for (int j4 = 0; j4 < 16; ++j4) {
+                if (j4 % (kResBatch / 4) == 0 && j4 / (kResBatch / 4) + kResAhead < 64 / kResBatch) load_res(j4 / (kResBatch / 4) + kResAhead);
                 const float4 c2 = sa4[j4 + 2 < 16 ? j4 + 2 : 15];
                 const int t = 64 * pass + 4 * j4;
-                const float v0 = __fmaf_rn(acc[t / 2].x, c0.x, bias), v1 = __fmaf_rn(acc[t / 2].y, c0.y, bias);
-                const float v2 = __fmaf_rn(acc[t / 2 + 1].x, c0.z, bias), v3 = __fmaf_rn(acc[t / 2 + 1].y, c0.w, bias);
+                const int r = kOp == OUT_GATED ? 4 * j4 : 0;
+                const float v0 = out_apply<kOp>(__fmaf_rn(acc[t / 2].x, c0.x, bias), gate, rres[r]);
+                const float v1 = out_apply<kOp>(__fmaf_rn(acc[t / 2].y, c0.y, bias), gate, rres[r + (kOp == OUT_GATED)]);
+                const float v2 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].x, c0.z, bias), gate, rres[r + 2 * (kOp == OUT_GATED)]);
+                const float v3 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].y, c0.w, bias), gate, rres[r + 3 * (kOp == OUT_GATED)]);
                 sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v0, v1);
                 sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v2, v3);
                 c0 = c1;
@@ -546,8 +587,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
             }
             return true;
           };
-          const bool stored = args.out_w64 ? store_passes(std::integral_constant<uint32_t, 128>{})
-                                           : store_passes(std::integral_constant<uint32_t, 64>{});
+          // the output operation is a template parameter: the plain kernel carries none of its code
+          using Op = std::integral_constant<int, OP>;
+          const bool stored = args.out_w64 ? store_passes(std::integral_constant<uint32_t, 128>{}, Op{})
+                                           : store_passes(std::integral_constant<uint32_t, 64>{}, Op{});
           if (!__all_sync(0xffffffffu, stored)) { ok = false; break; }
         } else if (n_ok) {
           __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
@@ -664,10 +707,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
 
 static int g_pair_clusters = 0;   // CTA pairs that fit on the device at once (cudaOccupancyMaxActiveClusters)
 
-template <int EPI, int BFMT, bool KPERM, bool GLU = false>
+template <int EPI, int BFMT, bool KPERM, bool GLU = false, int OP = OUT_PLAIN>
 static int launch_gemm_pair_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args,
                               cudaStream_t st, const OutSpec* outs = nullptr) {
-  auto kern = pr::gemm_pair_kernel<EPI, BFMT, KPERM, GLU>;
+  auto kern = pr::gemm_pair_kernel<EPI, BFMT, KPERM, GLU, OP>;
   constexpr int smem_bytes = pr::Plan<EPI>::kBytes;
   static bool configured = false;
   static bool regs_ok = false;
@@ -733,17 +776,19 @@ static int launch_gemm_pair_t(const int8_t* a, const void* b, const void* rsplit
   const int pairs = tiles < clusters ? tiles : clusters;
   if (pairs == 0) return CQ_OK;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(pr::kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = ga.pdl ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, tm_x, tm_w, tm_r, tm_z, tm_out, ga) != cudaSuccess) return CQ_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
@@ -771,8 +816,9 @@ static bool use_pair_kernel(int M, int N) {
 }
 
 int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int M, int N, int K, cudaStream_t st) {
+                       const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl) {
   GemmArgs g{};
+  g.pdl = pdl;
   g.sa = sa;
   g.sb = sb;
   g.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -790,8 +836,9 @@ int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void
 // W4A4 row/col GEMM with the SwiGLU output: b holds the weight rows interleaved in groups of 32 (16 gate rows, then
 // their 16 up rows); out is bf16 [M, N / 2].
 int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
-                           void* out, int M, int N, int K, cudaStream_t st) {
+                           void* out, int M, int N, int K, cudaStream_t st, bool pdl) {
   GemmArgs g{};
+  g.pdl = pdl;
   g.sa = sa;
   g.sb = sb;
   g.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -803,11 +850,21 @@ int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, cons
 
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
-                       cudaStream_t st, void* const* outs, int n_outs, int col0, int64_t ldo) {
+                       cudaStream_t st, void* const* outs, int n_outs, int col0, int64_t ldo, const OutOp* op,
+                       bool pdl) {
+  const bool plain = op == nullptr || op->kind == OUT_PLAIN;
   // a few tokens (adaLN modulation): read the weights once with a warp per row instead of 256-token MMA tiles
-  if (outs == nullptr && gemv_affine_fits(M, a_kperm))
+  // (plain outputs only: the output operations live in the GEMM's epilogue)
+  if (outs == nullptr && plain && gemv_affine_fits(M, a_kperm))
     return launch_gemv_affine(a, sa, b, s, zt, bias, out, M, N, K, st) == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
   GemmArgs g{};
+  g.pdl = pdl;
+  if (!plain) {
+    g.out_op = op->kind;
+    g.res = static_cast<const __nv_bfloat16*>(op->res);
+    g.res_ld = op->res_ld;
+    g.gate = static_cast<const __nv_bfloat16*>(op->gate);
+  }
   g.sa = sa;
   g.nz = rsplit_cols(K) / 64;
   g.ws = static_cast<const __nv_bfloat16*>(s);
@@ -817,12 +874,18 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   g.M = M; g.N = N; g.K = K;
   const OutSpec spec{outs, n_outs, col0, ldo};
   const OutSpec* sp = outs != nullptr ? &spec : nullptr;
-  if (use_pair_kernel(M, N)) {
-    if (a_kperm) return launch_gemm_pair_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st, sp);
-    return launch_gemm_pair_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st, sp);
-  }
-  if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true>(a, b, rsplit, g, st, sp);
-  return launch_gemm_t<EPI_AFFINE, BF_U4, false>(a, b, rsplit, g, st, sp);
+  auto launch = [&](auto op_c) {
+    constexpr int kOp = decltype(op_c)::value;
+    if (use_pair_kernel(M, N)) {
+      if (a_kperm) return launch_gemm_pair_t<EPI_AFFINE, BF_U4, true, false, kOp>(a, b, rsplit, g, st, sp);
+      return launch_gemm_pair_t<EPI_AFFINE, BF_U4, false, false, kOp>(a, b, rsplit, g, st, sp);
+    }
+    if (a_kperm) return launch_gemm_t<EPI_AFFINE, BF_U4, true, false, kOp>(a, b, rsplit, g, st, sp);
+    return launch_gemm_t<EPI_AFFINE, BF_U4, false, false, kOp>(a, b, rsplit, g, st, sp);
+  };
+  if (g.out_op == OUT_GELU) return launch(std::integral_constant<int, OUT_GELU>{});
+  if (g.out_op == OUT_GATED) return launch(std::integral_constant<int, OUT_GATED>{});
+  return launch(std::integral_constant<int, OUT_PLAIN>{});
 }
 
 // Per-group scales on both sides (the reference's policy 4): int4 activation codes (int8-held) x packed signed int4

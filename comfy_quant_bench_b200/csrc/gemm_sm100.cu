@@ -100,7 +100,48 @@ struct GemmArgs {
                          // tiles each (a partial last wave of at most half the CTAs finishes in half a tile's time)
   int out_w64;           // affine with tma_out: two epilogue warps (adjacent lane quadrants) share one 64-column
                          // box per pass (128-byte rows) instead of one 32-column box each (N % 64 == 0)
+  int out_op;            // affine: OUT_PLAIN / OUT_GELU / OUT_GATED, applied to the bf16 result before the store
+  int64_t res_ld;        // OUT_GATED: row stride (elements) of res
+  const __nv_bfloat16* res;   // OUT_GATED: residual [M, res_ld] (may be `out` itself)
+  const __nv_bfloat16* gate;  // OUT_GATED: per-column gate [N]
+  int pdl;               // host: launch with programmatic stream serialization (the kernel's prologue - barrier
+                         // set-up, TMEM allocation, descriptor prefetch - overlaps the tail of the previous kernel;
+                         // every thread waits for that kernel's completion before its first read of any input)
 };
+
+// Output operations of the affine epilogue (values of cq_out_kind)
+enum : int { OUT_PLAIN = 0, OUT_GELU = 1, OUT_GATED = 2 };
+constexpr int kResBatch = 8;   // gated residual: rows per batch of residual loads
+constexpr int kResAhead = 2;   //   batches in flight ahead of the one in use
+
+// gelu_tanh(y) = 0.5 y (1 + tanh(u)) with u = sqrt(2/pi) (y + 0.044715 y^3), written in its logistic form
+// y / (1 + 2^(-y (kA + kB y^2))), kA = 2 sqrt(2/pi) log2(e), kB = 0.044715 kA: no cancellation near 1 + tanh(u) = 0.
+// The hardware base-2 exponential and reciprocal (two special-function ops, eight instructions per element; for
+// large negative y the exponential overflows to inf and the reciprocal gives 0).  A variant that replaced the
+// reciprocal by Newton steps on the FMA pipe measured slower: the store pass is bound by instruction issue of the
+// epilogue warps, not by the special-function unit.
+__device__ __forceinline__ float gelu_tanh(float y) {
+  float e, r;
+  const float t = -y * __fmaf_rn(0.10294324f, y * y, 2.3022082f);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return y * r;
+}
+
+// One result through the output operation: v is the fp32 linear output (bias included) and y = bf16(v) the value
+// the plain epilogue stores; res_bits is the bf16 residual element (OUT_GATED).  The caller rounds the return
+// value to bf16.
+template <int OP>
+__device__ __forceinline__ float out_apply(float v, float gate, uint32_t res_bits) {
+  if constexpr (OP == OUT_PLAIN) {
+    return v;
+  } else {
+    const float y = bf16_round(v);
+    if constexpr (OP == OUT_GELU) return gelu_tanh(y);
+    else return __fmaf_rn(gate, y, bf16_bits_to_f32(res_bits));
+  }
+}
+
 
 __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
@@ -168,13 +209,14 @@ __device__ __forceinline__ uint4 unpack16(uint2 p) {
                     prmt(lo1, hi1, 0x7362u));
 }
 
-template <int EPI, int BFMT, bool KPERM, bool GLU = false>
+template <int EPI, int BFMT, bool KPERM, bool GLU = false, int OP = OUT_PLAIN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
             const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_z,
             const __grid_constant__ OutMaps tm_out, const GemmArgs args) {
   using P = SmemPlan<EPI, BFMT, GLU>;
   static_assert(!GLU || (EPI == EPI_ROWCOL && BFMT == BF_S4), "the SwiGLU output is a row/col W4A4 epilogue");
+  static_assert(OP == OUT_PLAIN || EPI == EPI_AFFINE, "output operations are affine-epilogue variants");
   constexpr int kTmaStages = P::kStages;
   constexpr bool kConv = BFMT != BF_S8;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -255,6 +297,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  grid_dep_wait();   // inputs written by the previous kernel (programmatic launch) are visible from here on
 
   if (warp < kEpiWarp0) {
     setmaxnreg_dec();
@@ -456,6 +499,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       const bool n_ok = n < N;
       const bool m_full = m0 + kWarpTok <= M;   // every token of the warp exists: no per-element checks
       const float bias = (args.bias != nullptr && n_ok) ? __bfloat162float(args.bias[n]) : 0.0f;
+      if constexpr (OP == OUT_GATED) {
+        // the warp's residual box (its 128 tokens x 32 columns) into L2 now, a whole tile of group drains before
+        // the store passes read it
+        const int c0 = n - lane;
+        if (c0 < N)
+          for (int r = lane; r < kWarpTok && m0 + r < M; r += 32)
+            prefetch_l2(args.res + static_cast<int64_t>(m0 + r) * args.res_ld + c0);
+      }
       // the tokens' activation scales, one per lane and 32-token chunk, loaded when the tile starts so that their
       // latency hides behind the tile's MMAs (indices past the last token clamp to it; those rows are not stored)
       float sa_pre[kChunks];
@@ -549,8 +600,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           // token half) fill the two halves of a 64-column box in their joint 8 KB buffer, synchronized by a named
           // barrier, and the even warp issues the stores: each box row is 128 contiguous bytes, which a remote
           // (NVLink) write moves more efficiently than 64-byte rows.
-          auto store_passes = [&](auto row_bytes_c) -> bool {
+          auto store_passes = [&](auto row_bytes_c, auto op_c) -> bool {
             constexpr uint32_t kRow = decltype(row_bytes_c)::value;
+            constexpr int kOp = decltype(op_c)::value;
             constexpr bool kPair = kRow == 128;
             const int owner = kPair ? (e & ~1) : e;
             unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOutStage + owner * P::kOutWarpBytes);
@@ -570,12 +622,42 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
               } else if (!mbar_wait(&box_free[pr], par, abort_flag, 17)) {
                 return false;
               }
+              // gated residual: this lane's column of the pass's 64 residual rows, in batches of kResBatch rows issued
+              // kResAhead batches ahead of their use
+              // (one pointer walked down the rows; lanes past N read column N - 1 and rows past M repeat the last
+              // row, neither of which is stored)
+              uint32_t rres[kOp == OUT_GATED ? 64 : 1];
+              // the column's gate, loaded here rather than with the bias so that no register holds it across the
+              // tile's group drains
+              const float gate = (kOp == OUT_GATED && n_ok) ? __bfloat162float(args.gate[n]) : 0.0f;
+              const unsigned short* rp = nullptr;
+              int rows_left = 0;
+              if constexpr (kOp == OUT_GATED) {
+                rows_left = M - (m0 + 64 * pass);
+                rp = reinterpret_cast<const unsigned short*>(args.res) + min(n, N - 1) +
+                     static_cast<int64_t>(m0 + 64 * pass) * args.res_ld;
+              }
+              auto load_res = [&](int b) {
+                if constexpr (kOp == OUT_GATED) {
+#pragma unroll
+                  for (int i = 0; i < kResBatch; ++i) {
+                    rres[kResBatch * b + i] = __ldg(rp);
+                    if (kResBatch * b + i + 1 < rows_left) rp += args.res_ld;
+                  }
+                }
+              };
+#pragma unroll
+              for (int b = 0; b < kResAhead; ++b) load_res(b);
 #pragma unroll
               for (int j4 = 0; j4 < 16; ++j4) {
+                if (j4 % (kResBatch / 4) == 0 && j4 / (kResBatch / 4) + kResAhead < 64 / kResBatch) load_res(j4 / (kResBatch / 4) + kResAhead);
                 const int t = 64 * pass + 4 * j4;
+                const int r = kOp == OUT_GATED ? 4 * j4 : 0;
                 const float4 c = *reinterpret_cast<const float4*>(sa_stage + t);
-                const float v0 = __fmaf_rn(acc[t / 2].x, c.x, bias), v1 = __fmaf_rn(acc[t / 2].y, c.y, bias);
-                const float v2 = __fmaf_rn(acc[t / 2 + 1].x, c.z, bias), v3 = __fmaf_rn(acc[t / 2 + 1].y, c.w, bias);
+                const float v0 = out_apply<kOp>(__fmaf_rn(acc[t / 2].x, c.x, bias), gate, rres[r]);
+                const float v1 = out_apply<kOp>(__fmaf_rn(acc[t / 2].y, c.y, bias), gate, rres[r + (kOp == OUT_GATED)]);
+                const float v2 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].x, c.z, bias), gate, rres[r + 2 * (kOp == OUT_GATED)]);
+                const float v3 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].y, c.w, bias), gate, rres[r + 3 * (kOp == OUT_GATED)]);
                 sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v0, v1);
                 sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v2, v3);
               }
@@ -593,8 +675,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             }
             return true;
           };
-          const bool stored = args.out_w64 ? store_passes(std::integral_constant<uint32_t, 128>{})
-                                           : store_passes(std::integral_constant<uint32_t, 64>{});
+          // the output operation is a template parameter: the plain kernel carries none of its code
+          using Op = std::integral_constant<int, OP>;
+          const bool stored = args.out_w64 ? store_passes(std::integral_constant<uint32_t, 128>{}, Op{})
+                                           : store_passes(std::integral_constant<uint32_t, 64>{}, Op{});
           if (!__all_sync(0xffffffffu, stored)) { ok = false; break; }
         } else if (n_ok) {
           // column n of the output for tokens m0..m0+127: one pointer walked down the rows
@@ -798,10 +882,10 @@ struct OutSpec {
   int64_t ldo;
 };
 
-template <int EPI, int BFMT, bool KPERM, bool GLU = false>
+template <int EPI, int BFMT, bool KPERM, bool GLU = false, int OP = OUT_PLAIN>
 static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, const GemmArgs& args, cudaStream_t st,
                          const OutSpec* outs = nullptr) {
-  auto kern = gemm_kernel<EPI, BFMT, KPERM, GLU>;
+  auto kern = gemm_kernel<EPI, BFMT, KPERM, GLU, OP>;
   constexpr int smem_bytes = SmemPlan<EPI, BFMT, GLU>::kBytes;
   static bool configured = false;
   static bool regs_ok = false;
@@ -872,7 +956,21 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
   const int items = tiles + split;
   const int grid = items < g_num_sms ? items : g_num_sms;
   if (grid == 0) return CQ_OK;
-  kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_out, ga);
+  if (ga.pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tm_x, tm_w, tm_r, tm_z, tm_out, ga) != cudaSuccess) return CQ_ERR_CUDA;
+  } else {
+    kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_out, ga);
+  }
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }
 

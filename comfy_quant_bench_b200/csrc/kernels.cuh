@@ -24,6 +24,13 @@ struct RotQuantArgs {
   const __nv_bfloat16* ln_shift;
   const __nv_bfloat16* ln_scale1p;
   float ln_eps;
+  // per-token int8 activations whose K columns are split over ranks (row-parallel linears).  amax_out set: the
+  // kernel only writes, per token t, the NaN-ignoring maximum of |rotated x| over its columns (amax_out[t]) and
+  // 1 if a NaN was among them, else 0 (amax_out[rows_pad + t]).  amax_in set (the same two rows, combined over the
+  // ranks by a maximum): the kernel quantizes with those instead of its own maximum, so every rank derives the
+  // scale the whole row would give.
+  float* amax_out;
+  const float* amax_in;
 };
 
 // columns of the split group-sum array for a K (the affine GEMM's zero-point operand)
@@ -58,17 +65,27 @@ cudaError_t launch_heads_to_rows(const HeadsToRowsArgs& a, cudaStream_t st);
 cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_weight_rotquant(int rot, bool w_bf16, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_unpack_int4(const void* src, int64_t n_bytes, void* dst, cudaStream_t st);
+// pdl: launch with programmatic stream serialization (the fused linears, whose previous kernel in the stream is
+// their own activation kernel): the GEMM's prologue overlaps that kernel's tail
 int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int M, int N, int K, cudaStream_t st);
+                       const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl = false);
 int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
-                           void* out, int M, int N, int K, cudaStream_t st);
+                           void* out, int M, int N, int K, cudaStream_t st, bool pdl = false);
 constexpr int kMaxOutBuffers = 8;   // output buffers of one column-parallel affine launch
 
 // outs != nullptr: write the result into n_outs (<= kMaxOutBuffers) buffers of [M, ldo] bf16 at columns [col0, col0 + N)
 // instead of `out` (column-parallel layers)
+// output operation of the affine epilogue (cq_out_op): kind 0 plain, 1 GELU-tanh, 2 gated residual
+struct OutOp {
+  int kind;
+  const void* res;
+  int64_t res_ld;
+  const void* gate;
+};
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
-                       cudaStream_t st, void* const* outs = nullptr, int n_outs = 0, int col0 = 0, int64_t ldo = 0);
+                       cudaStream_t st, void* const* outs = nullptr, int n_outs = 0, int col0 = 0, int64_t ldo = 0,
+                       const OutOp* op = nullptr, bool pdl = false);
 cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t st);
 // per-group scales on both sides (policy 4): sag f32 [K/128, sag_ld], sbg f32 [K/128, N]; CTA-pair kernel
 int launch_gemm_group(const int8_t* a, int a_kperm, const float* sag, int64_t sag_ld, const void* b, const float* sbg,

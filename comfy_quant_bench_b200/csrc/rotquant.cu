@@ -597,6 +597,9 @@ __device__ __forceinline__ float2 bf16x2_round(float2 v) {
 template <int ROT, int PASSES, bool LNMOD, int QMAX, bool SWIGLU>
 __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
   static_assert(!(LNMOD && SWIGLU), "one prologue at a time");
+  // the GEMM that consumes these codes may be scheduled as soon as every CTA of this grid runs (its prologue then
+  // overlaps this kernel's tail; it waits for this grid's completion before reading anything)
+  grid_dep_launch();
   extern __shared__ __align__(16) unsigned char act8_smem[];
   __shared__ float red[2][act8::kMaxTeamWarps];
   __shared__ float red_ln[2][2][act8::kMaxTeamWarps];   // layer-norm prologue: sums, then centered squares
@@ -722,32 +725,8 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
       if (warp + s * nwarps < nchunks) stages_cross_x2<ROT>(v[s], tile, lane);   // warp-uniform
   }
 
-  // per-token absolute maximum (NaN-propagating: a NaN or infinity anywhere makes it non-finite)
-  float pa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pb[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four chains per token
-#pragma unroll
-  for (int s = 0; s < PASSES; ++s)
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const int a = (i >> 1) & 3;
-      pa[a] = max3_nan(pa[a], fabsf(v[s][i].x), fabsf(v[s][i + 1].x));
-      pb[a] = max3_nan(pb[a], fabsf(v[s][i].y), fabsf(v[s][i + 1].y));
-    }
-  float ma = max_nan(max3_nan(pa[0], pa[1], pa[2]), pa[3]);
-  float mb = max_nan(max3_nan(pb[0], pb[1], pb[2]), pb[3]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    ma = max_nan(ma, __shfl_xor_sync(0xffffffffu, ma, o));
-    mb = max_nan(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-  }
-  if (nwarps > 1) {
-    if (lane == 0) { red[0][warp] = ma; red[1][warp] = mb; }
-    __syncthreads();
-    ma = red[0][0]; mb = red[1][0];
-    for (int w = 1; w < nwarps; ++w) { ma = max_nan(ma, red[0][w]); mb = max_nan(mb, red[1][w]); }
-  }
-  const bool finite = ma <= 3.402823466e38f && mb <= 3.402823466e38f;   // false for NaN and infinity
-  if (!finite) {
-    // the scalar kernel's maximum: fmaxf ignores NaN; an infinity gives scale inf and reciprocal 0
+  // the scalar kernel's maximum: fmaxf ignores NaN; an infinity gives scale inf and reciprocal 0
+  auto nan_ignoring_max = [&](float& ma, float& mb) {
     ma = 0.0f; mb = 0.0f;
 #pragma unroll
     for (int s = 0; s < PASSES; ++s)
@@ -759,12 +738,61 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
       mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
     }
     if (nwarps > 1) {
-      __syncthreads();                              // every warp has read red[] above
+      __syncthreads();                              // every warp has read red[] from an earlier use
       if (lane == 0) { red[0][warp] = ma; red[1][warp] = mb; }
       __syncthreads();
       ma = red[0][0]; mb = red[1][0];
       for (int w = 1; w < nwarps; ++w) { ma = fmaxf(ma, red[0][w]); mb = fmaxf(mb, red[1][w]); }
     }
+  };
+  float ma, mb;
+  bool finite;
+  if (args.amax_in != nullptr) {
+    // the row's maximum and NaN flag, combined over the ranks that hold its columns
+    ma = args.amax_in[rA];
+    mb = storeB ? args.amax_in[rA + 1] : 0.0f;
+    const bool nan_seen = args.amax_in[args.rows_pad + rA] != 0.0f || (storeB && args.amax_in[args.rows_pad + rA + 1] != 0.0f);
+    finite = !nan_seen && ma <= 3.402823466e38f && mb <= 3.402823466e38f;
+  } else {
+    // per-token absolute maximum (NaN-propagating: a NaN or infinity anywhere makes it non-finite)
+    float pa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pb[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four chains per token
+#pragma unroll
+    for (int s = 0; s < PASSES; ++s)
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const int a = (i >> 1) & 3;
+        pa[a] = max3_nan(pa[a], fabsf(v[s][i].x), fabsf(v[s][i + 1].x));
+        pb[a] = max3_nan(pb[a], fabsf(v[s][i].y), fabsf(v[s][i + 1].y));
+      }
+    ma = max_nan(max3_nan(pa[0], pa[1], pa[2]), pa[3]);
+    mb = max_nan(max3_nan(pb[0], pb[1], pb[2]), pb[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ma = max_nan(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+      mb = max_nan(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    }
+    if (nwarps > 1) {
+      if (lane == 0) { red[0][warp] = ma; red[1][warp] = mb; }
+      __syncthreads();
+      ma = red[0][0]; mb = red[1][0];
+      for (int w = 1; w < nwarps; ++w) { ma = max_nan(ma, red[0][w]); mb = max_nan(mb, red[1][w]); }
+    }
+    finite = ma <= 3.402823466e38f && mb <= 3.402823466e38f;   // false for NaN and infinity
+    if (args.amax_out != nullptr) {
+      // one rank's columns of the rows: the NaN-ignoring maximum and a NaN flag, for a maximum over the ranks
+      const bool nan_a = ma != ma, nan_b = mb != mb;
+      if (!finite) nan_ignoring_max(ma, mb);
+      if (threadIdx.x == 0) {
+        args.amax_out[rA] = liveA ? ma : 0.0f;
+        args.amax_out[args.rows_pad + rA] = (liveA && nan_a) ? 1.0f : 0.0f;
+        if (storeB) {
+          args.amax_out[rA + 1] = liveB ? mb : 0.0f;
+          args.amax_out[args.rows_pad + rA + 1] = (liveB && nan_b) ? 1.0f : 0.0f;
+        }
+      }
+      return;
+    }
+    if (!finite) nan_ignoring_max(ma, mb);
   }
   // per-token scale max(absmax / QMAX, 1e-10) (QMAX 127: int8 codes; 7: int4 values held in int8 codes)
   constexpr float kInvQ = 1.0f / static_cast<float>(QMAX);

@@ -12,6 +12,11 @@ Two schemes, both new relative to comfy-quant-bench (which runs on one GPU):
 ``FusedColumnParallelW4A8`` removes the separate gather: its GEMM stores each output tile into every rank's
 (symmetric-memory) output buffer over NVLink as the tile finishes.  Nothing in the library's kernels waits on a
 peer; the ranks synchronize with torch's symmetric-memory barrier around the launch.
+
+``RowParallelW4A8`` splits the weight by input columns instead: each rank quantizes its columns of the activation
+with the scale of the whole row (a small all-reduce MAX of per-token maxima), runs its K slice, and one all-reduce
+SUM of the bf16 partial products gives the output.  Paired with a column-parallel layer before it (an MLP-up, or a
+head-parallel attention), the activation between the two never leaves its rank.
 """
 from __future__ import annotations
 
@@ -134,6 +139,64 @@ class FusedColumnParallelW4A8:
                                     group_size=self.group_size, convrot_groupsize=self.convrot_groupsize)
         self.hdl.barrier(channel=0)
         return self.out[:m].reshape(*x.shape[:-1], self.n)
+
+
+def shard_affine_k(qweight, scale, zeros, rank: int, world: int, group_size: int = 128):
+    """Row-parallel (input-column) shard of an awq-layout weight: this rank's K/P input columns of the packed
+    weight (two codes per byte) and the matching groups (rows of the [K/G, N] scale / zeros)."""
+    k = qweight.shape[1] * 2
+    a, b = shard_bounds(k, rank, world)
+    if a % group_size or b % group_size:
+        raise ValueError(f"the {world} K slices must hold whole {group_size}-column groups")
+    return (qweight[:, a // 2:b // 2].contiguous(), scale[a // group_size:b // group_size].contiguous(),
+            zeros[a // group_size:b // group_size].contiguous())
+
+
+class RowParallelW4A8:
+    """y = x @ W^T + b with W split over ranks by INPUT columns and the partial outputs summed.
+
+    Rank r holds input columns ``[r*K/P, (r+1)*K/P)`` of the weight and receives the same columns of x (a
+    head-parallel attention's output, or a column-parallel MLP-up's activation, stays where it was computed).
+    The per-token int8 scale needs the whole row: each rank writes its columns' maximum and NaN flag
+    (``rotquant_absmax``), one all-reduce MAX of [2, M] floats combines them, and ``rotquant_scaled`` quantizes
+    with the combined values, so every rank's codes equal those of the unsplit row.  Each rank's GEMM over its K
+    slice gives a partial product (the bias on rank 0 only), and one all-reduce SUM of the bf16 partials over NCCL
+    yields the output on every rank.  The sum is taken in a different order than the one-GPU GEMM's fp32
+    accumulation over all groups, so the result agrees with the one-GPU linear to the bf16 rounding of the
+    partials, not bit for bit.
+    """
+
+    def __init__(self, qweight, scale, zeros, bias, rank: int, world: int, group=None, group_size: int = 128,
+                 convrot_groupsize: int = 0):
+        from . import ops
+        q, s, z = shard_affine_k(qweight, scale, zeros, rank, world, group_size)
+        if convrot_groupsize and (q.shape[1] * 2) % convrot_groupsize:
+            raise ValueError("the rotation groups must lie inside one rank's columns")
+        self.q, self.s = q, s
+        self.zt = ops.prepare_affine_zeros(z, group_size)
+        self.b = bias if rank == 0 else None
+        self.n = qweight.shape[0]
+        self.rank, self.world, self.group = rank, world, group
+        self.convrot_groupsize = convrot_groupsize
+
+    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
+        """x_local [..., K/P] (this rank's columns) -> the full [..., N] output on every rank."""
+        import torch.distributed as dist
+        from . import ops
+        x2 = x_local.reshape(-1, x_local.shape[-1])
+        m = x2.shape[0]
+        mp = (m + 15) // 16 * 16
+        rot = self.convrot_groupsize
+        if self.world > 1:
+            amax = ops.rotquant_absmax(x2, rot, m_pad=mp)
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+            q, sx, gs = ops.rotquant_scaled(x2, rot, amax, m_pad=mp, group_sums=True, kperm=True)
+        else:
+            q, sx, gs = ops.rotquant(x2, rot, 0, m_pad=mp, group_sums=True, kperm=True)
+        y = ops.gemm_affine(q[:m], sx[:m], gs, self.q, self.s, None, self.b, a_kperm=True, zeros_prepared=self.zt)
+        if self.world > 1:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y.reshape(*x_local.shape[:-1], self.n)
 
 
 def split_batch(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:

@@ -33,6 +33,7 @@ import torch.nn.functional as F
 
 from . import ops
 from . import _lib
+from .dist import RowParallelW4A8
 from .mmdit import rel_l2  # noqa: F401
 
 
@@ -82,6 +83,13 @@ class AffineLinear:
         return ops.w4a8_affine_linear_lnmod(x, shift, scale1p, self.qweight, self.scale, self.zt, self.bias,
                                             self.cfg.group_size, self.cfg.convrot_groupsize)
 
+    def op(self, x, out_op, *, residual=None, gate=None, shift=None, scale1p=None):
+        """This linear with GELU (``"gelu"``) or the gated residual (``"gated"``) in the GEMM epilogue, and with
+        shift/scale1p the modulated layer norm in the activation kernel (``ops.w4a8_affine_linear_op``)."""
+        return ops.w4a8_affine_linear_op(x, self.qweight, self.scale, self.zt, self.bias, out_op=out_op,
+                                         residual=residual, gate=gate, shift=shift, scale1p=scale1p,
+                                         group_size=self.cfg.group_size, convrot_groupsize=self.cfg.convrot_groupsize)
+
     def quantize(self, x, shift=None, scale1p=None):
         """The activation stage alone (codes, scales, split group sums), optionally of the modulated layer norm."""
         mp = (x.shape[0] + 15) // 16 * 16
@@ -118,19 +126,28 @@ def _rope3d(cfg: LTXConfig, device) -> torch.Tensor:
 
 
 class _Block:
-    def __init__(self, gen, device, cfg: LTXConfig, rank: int, world: int):
+    def __init__(self, gen, device, cfg: LTXConfig, rank: int, world: int, row_parallel: bool, group=None):
         h, f, d = cfg.hidden, cfg.ffn, cfg.head_dim
         hp = cfg.heads // world
         h0, h1 = rank * hp, (rank + 1) * hp
         cols = lambda n: list(range(rank * n // world, (rank + 1) * n // world)) if world > 1 else None  # noqa: E731
         heads = lambda parts, n: _head_rows(n, parts, h0, h1, d) if world > 1 else None  # noqa: E731
+        rp = row_parallel and world > 1
+
+        def row_par(lin: AffineLinear):
+            # the full weight, split by input columns (the same seeded draws as every other form)
+            return RowParallelW4A8(lin.qweight, lin.scale, lin.zeros, lin.bias, rank, world, group, cfg.group_size,
+                                   cfg.convrot_groupsize)
+
         self.qkv = AffineLinear(h, 3 * h, heads(3, h), gen, device, cfg)
-        self.out = AffineLinear(h, h, cols(h), gen, device, cfg)
+        self.out = AffineLinear(h, h, None if rp else cols(h), gen, device, cfg)
         self.cq = AffineLinear(h, h, heads(1, h), gen, device, cfg)
         self.ckv = AffineLinear(h, 2 * h, heads(2, h), gen, device, cfg)
-        self.co = AffineLinear(h, h, cols(h), gen, device, cfg)
+        self.co = AffineLinear(h, h, None if rp else cols(h), gen, device, cfg)
         self.ff1 = AffineLinear(h, f, cols(f), gen, device, cfg)
-        self.ff2 = AffineLinear(f, h, cols(h), gen, device, cfg)
+        self.ff2 = AffineLinear(f, h, None if rp else cols(h), gen, device, cfg)
+        if rp:
+            self.out, self.co, self.ff2 = row_par(self.out), row_par(self.co), row_par(self.ff2)
         self.mod = (torch.randn(6, h, generator=gen, device=device) * 0.1).to(torch.bfloat16)
         self.scale1p = (1.0 + self.mod[[1, 4]]).contiguous()
         self.norms = (1 + 0.1 * torch.randn(4, d, generator=gen, device=device)).to(torch.bfloat16)
@@ -140,22 +157,33 @@ class _Block:
     def linears(self):
         return [self.qkv, self.out, self.cq, self.ckv, self.co, self.ff1, self.ff2]
 
+    def weight_bytes(self) -> int:
+        tot = 0
+        for l in self.linears():
+            if isinstance(l, RowParallelW4A8):
+                tot += l.q.numel() + 2 * l.s.numel() * 2 + l.zt.numel() * 2
+            else:
+                tot += l.weight_bytes()
+        return tot
+
 
 class LTXDiT:
     """The LTX-like step on this rank: ``world`` > 1 runs the tensor-parallel form (call from every rank)."""
 
     def __init__(self, cfg: LTXConfig = LTXConfig(), device="cuda", seed: int = 0, rank: int = 0, world: int = 1,
-                 group=None):
+                 group=None, row_parallel: bool = True):
         if cfg.heads % world or cfg.hidden % world or cfg.ffn % world:
             raise ValueError(f"heads, hidden and ffn must divide by the {world} ranks")
         self.cfg, self.rank, self.world = cfg, rank, world
+        self.row_parallel = row_parallel and world > 1
+        self.group = group
         self.device = torch.device(device)
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed)
-        self.blocks = [_Block(gen, self.device, cfg, rank, world) for _ in range(cfg.blocks)]
+        self.blocks = [_Block(gen, self.device, cfg, rank, world, row_parallel, group) for _ in range(cfg.blocks)]
         self.rope = _rope3d(cfg, self.device)
         s, h, f = cfg.tokens, cfg.hidden, cfg.ffn
-        if world > 1:
+        if world > 1 and not self.row_parallel:
             import torch.distributed as dist
             import torch.distributed._symmetric_memory as symm_mem
             grp = group if group is not None else dist.group.WORLD
@@ -199,8 +227,68 @@ class LTXDiT:
         self._barrier()
         return self._bufs[name][0][: x.shape[0]]
 
+    def _heads_local(self, o: torch.Tensor) -> torch.Tensor:
+        """o [1, H/P, S, D] -> this rank's heads as [S, H/P * D] rows (the row-parallel projections' input)."""
+        _, hp, s, d = o.shape
+        a = torch.empty(s, hp * d, dtype=torch.bfloat16, device=o.device)
+        ops.heads_to_rows(o, [a], 0, hp * d)
+        return a
+
     # ---- the step ----
     def step(self, x: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return self._step_one_gpu(x, ctx)
+        if self.row_parallel:
+            return self._step_row_parallel(x, ctx)
+        return self._step_gather(x, ctx)
+
+    def _attn_inputs(self, s: int, device):
+        c = self.cfg
+        hp = c.heads // self.world
+        q = torch.empty(1, hp, s, c.head_dim, dtype=torch.bfloat16, device=device)
+        return q, torch.empty_like(q), torch.empty_like(q)
+
+    def _cross_attention(self, b, x, ctx, s: int):
+        c = self.cfg
+        d, hp = c.head_dim, c.heads // self.world
+        cq = F.rms_norm(b.cq.lnmod(x, b.zero_shift, b.one).view(s, hp, d), (d,), b.norms[2], eps=1e-6)
+        kv = b.ckv(ctx).view(-1, 2, hp, d)
+        ck = F.rms_norm(kv[:, 0], (d,), b.norms[3], eps=1e-6)
+        return F.scaled_dot_product_attention(cq.transpose(0, 1)[None], ck.transpose(0, 1)[None],
+                                              kv[:, 1].transpose(0, 1)[None])
+
+    def _step_one_gpu(self, x: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
+        """One GPU: the gated residuals and GELU in the GEMM epilogues, the norms in the activation kernels."""
+        s = x.shape[0]
+        q, k, v = self._attn_inputs(s, x.device)
+        for b in self.blocks:
+            m = b.mod
+            y = b.qkv.lnmod(x, m[0], b.scale1p[0])
+            ops.qkv_rmsnorm_rope(y, b.norms[0], b.norms[1], self.rope, q, k, v, 0, eps=1e-6)
+            x = b.out.op(self._heads_local(F.scaled_dot_product_attention(q, k, v)), "gated", residual=x, gate=m[2])
+            x = b.co.op(self._heads_local(self._cross_attention(b, x, ctx, s)), "gated", residual=x, gate=b.one)
+            g = b.ff1.op(x, "gelu", shift=m[3], scale1p=b.scale1p[1])
+            x = b.ff2.op(g, "gated", residual=x, gate=m[5])
+        return x
+
+    def _step_row_parallel(self, x: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
+        """P ranks, Megatron-style: attention heads and the MLP's hidden columns stay on their rank; the output
+        projections and MLP-down are row-parallel (an all-reduce of the partial products, NCCL), so the only
+        full-size exchanges per block are three all-reduces of [S, hidden] bf16."""
+        s = x.shape[0]
+        q, k, v = self._attn_inputs(s, x.device)
+        for b in self.blocks:
+            m = b.mod
+            y = b.qkv.lnmod(x, m[0], b.scale1p[0])
+            ops.qkv_rmsnorm_rope(y, b.norms[0], b.norms[1], self.rope, q, k, v, 0, eps=1e-6)
+            x = torch.addcmul(x, m[2], b.out(self._heads_local(F.scaled_dot_product_attention(q, k, v))))
+            x = x + b.co(self._heads_local(self._cross_attention(b, x, ctx, s)))
+            g = b.ff1.op(x, "gelu", shift=m[3], scale1p=b.scale1p[1])      # this rank's ffn/P hidden columns
+            x = torch.addcmul(x, m[5], b.ff2(g))
+        return x
+
+    def _step_gather(self, x: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
+        """P ranks, every linear column-parallel with the all-gather inside the GEMM (peer stores)."""
         c = self.cfg
         h, d = c.hidden, c.head_dim
         hp = c.heads // self.world
@@ -235,7 +323,7 @@ class LTXDiT:
         return [l for b in self.blocks for l in b.linears()]
 
     def weight_bytes(self) -> int:
-        return sum(l.weight_bytes() for l in self.linears())
+        return sum(b.weight_bytes() for b in self.blocks)
 
     def linear_int_ops(self) -> float:
         """2 * M * N * K of the whole model's linears for one step (all ranks together)."""

@@ -12,11 +12,12 @@ per-128-group scale/zero, tcgen05 GEMM).  The block follows the usual MMDiT layo
     x     = x + gate1 * Linear_out(attn)
     x     = x + gate2 * Linear_fc2(gelu_tanh(Linear_fc1(LayerNorm(x) * (1 + scale2) + shift2)))
 
-Attention, GELU and the gated residuals are torch ops.  The layer norm + modulation before the QKV and MLP-up
-linears run inside the library's activation kernel (``ops.w4a8_affine_linear_lnmod``) and the q/k RMSNorm + rotary
-embedding + joint attention layout run as one library kernel (``ops.qkv_rmsnorm_rope``), and the attention output
-goes to the [tokens, hidden] layout through ``ops.heads_to_rows``; ``fused_glue=False`` runs them as torch ops
-instead.  Weights are drawn N(0, 0.02) per linear from a
+Attention is a torch op (scaled_dot_product_attention).  On the kernel path the rest of the glue runs inside the
+library's kernels: the layer norm + modulation before the QKV and MLP-up linears in the activation kernel
+(``ops.w4a8_affine_linear_lnmod`` / ``ops.w4a8_affine_linear_op``), the GELU after MLP-up and the two gated residuals
+in the GEMM epilogues (``ops.w4a8_affine_linear_op``), the q/k RMSNorm + rotary embedding + joint attention layout as
+one kernel (``ops.qkv_rmsnorm_rope``), and the attention output to the [tokens, hidden] layout through
+``ops.heads_to_rows``; ``fused_glue=False`` runs them as torch ops instead.  Weights are drawn N(0, 0.02) per linear from a
 seeded generator, quantized on the device with the library's weight kernel, and only the packed form is kept.
 
 ``MMDiT.step(..., reference=True)`` runs the same step with every linear replaced by a torch fp32 product of the
@@ -47,6 +48,9 @@ class MMDiTConfig:
     quantize_modulation: bool = True   # every linear W4A8; the reference's profiles leave modulation unquantized
     fused_glue: bool = True            # kernel path: layer norm + modulation inside the activation kernel of the
                                        # QKV and MLP-up linears, q/k RMSNorm + rotary + attention layout in one kernel
+    epilogue_gated: bool = True        # with fused_glue: the gated residuals in the GEMM epilogues of the
+                                       # attention-output and MLP-down linears (False: torch addcmul)
+    epilogue_gelu: bool = True         # with fused_glue: GELU in the MLP-up GEMM's epilogue (False: torch gelu)
 
     @property
     def head_dim(self) -> int:
@@ -74,6 +78,14 @@ class QLinear:
         activation kernel."""
         return ops.w4a8_affine_linear_lnmod(x, shift, scale1p, self.qweight, self.scale, self.zt, self.bias,
                                             self.cfg.group_size, self.cfg.convrot_groupsize, eps=1e-6)
+
+    def op(self, x: torch.Tensor, out_op: str, *, residual=None, gate=None, shift=None, scale1p=None) -> torch.Tensor:
+        """This linear with the step after it in the GEMM's epilogue: ``gelu`` (tanh) or ``gated``
+        (residual + gate * y); with shift/scale1p the layer norm + modulation before it in the activation kernel."""
+        return ops.w4a8_affine_linear_op(x, self.qweight, self.scale, self.zt, self.bias, out_op=out_op,
+                                         residual=residual, gate=gate, shift=shift, scale1p=scale1p,
+                                         group_size=self.cfg.group_size, convrot_groupsize=self.cfg.convrot_groupsize,
+                                         eps=1e-6)
 
     def dequantized_weight(self) -> torch.Tensor:
         """W in the rotated basis, fp32 [N, K]: (q - 8) * scale + zeros per 128-wide group."""
@@ -232,12 +244,23 @@ class MMDiT:
             a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
         new = []
         for x, s, m, att in ((txt, st, mt, a[:st_txt]), (img, si, mi, a[st_txt:])):
-            x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
             if fused:
-                f = F.gelu(s.fc1.lnmod(x, m[3], 1.0 + m[4]), approximate="tanh")
-            else:
-                xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
-                f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
+                # layer norm + modulation in the activation kernels; GELU and the gated residuals in the GEMM
+                # epilogues, or as torch ops on the linears' outputs
+                if c.epilogue_gated:
+                    x = s.out.op(att, "gated", residual=x, gate=m[2])
+                else:
+                    x = torch.addcmul(x, m[2], s.out(att))
+                if c.epilogue_gelu:
+                    f = s.fc1.op(x, "gelu", shift=m[3], scale1p=1.0 + m[4])
+                else:
+                    f = F.gelu(s.fc1.lnmod(x, m[3], 1.0 + m[4]), approximate="tanh")
+                new.append(s.fc2.op(f, "gated", residual=x, gate=m[5]) if c.epilogue_gated
+                           else torch.addcmul(x, m[5], s.fc2(f)))
+                continue
+            x = torch.addcmul(x, m[2], self._lin(s.out, att, reference))
+            xn = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
+            f = F.gelu(self._lin(s.fc1, xn, reference), approximate="tanh")
             new.append(torch.addcmul(x, m[5], self._lin(s.fc2, f, reference)))
         txt, img = new
         return img, txt

@@ -101,6 +101,37 @@ def rotquant(x: torch.Tensor, rot_group: int, mode: int, *, swiglu: bool = False
     return q, scale, gs
 
 
+def rotquant_absmax(x: torch.Tensor, rot_group: int, *, m_pad: int | None = None) -> torch.Tensor:
+    """First phase of per-token int8 activations whose K columns are split over ranks: f32 [2, M_pad] holding each
+    token's NaN-ignoring max |rotated x| over these columns and a NaN flag.  Combine the ranks' arrays with an
+    all-reduce MAX, then call ``rotquant_scaled`` (cq_rotquant_absmax)."""
+    dev = _require_cuda(x)
+    x2 = _as2d(x)
+    m, k = x2.shape
+    mp = m if m_pad is None else int(m_pad)
+    amax = torch.empty(2, mp, dtype=torch.float32, device=dev)
+    _lib.call("cq_rotquant_absmax", _ptr(x2), m, k, _check_rot(rot_group), mp, _ptr(amax), _stream(dev))
+    return amax
+
+
+def rotquant_scaled(x: torch.Tensor, rot_group: int, amax: torch.Tensor, *, m_pad: int | None = None,
+                    group_sums: bool = False, kperm: bool = False):
+    """Second phase: per-token int8 codes of these columns with the scale of the whole row, from the combined
+    ``amax`` [2, M_pad].  Returns (q, scale, gsplit or None) as ``rotquant`` (cq_rotquant_scaled)."""
+    dev = _require_cuda(x, amax)
+    x2 = _as2d(x)
+    m, k = x2.shape
+    mp = m if m_pad is None else int(m_pad)
+    if amax.dtype != torch.float32 or tuple(amax.shape) != (2, mp) or not amax.is_contiguous():
+        raise ValueError(f"amax must be contiguous f32 [2, {mp}]")
+    q = torch.empty(mp, k, dtype=torch.int8, device=dev)
+    scale = torch.empty(mp, dtype=torch.float32, device=dev)
+    gs = torch.empty(mp, int(_lib.load().cq_group_sum_cols(k)), dtype=torch.bfloat16, device=dev) if group_sums else None
+    _lib.call("cq_rotquant_scaled", _ptr(x2), m, k, _check_rot(rot_group), _ptr(amax), mp,
+              _lib.CQ_Q_KPERM if kperm else 0, _ptr(q), _ptr(scale), _ptr(gs), _stream(dev))
+    return q, scale, gs
+
+
 def quantize_int4_rowwise_convrot64(x: torch.Tensor, convrot_groupsize: int = 256):
     """Rotate (block Hadamard) + per-token int4: (q [M, K/2] int8 packed, scale [M] f32)."""
     q, s, _ = rotquant(x, convrot_groupsize, _lib.CQ_ACT_INT4_ROW)
@@ -513,6 +544,61 @@ def w4a8_affine_linear_lnmod(x: torch.Tensor, shift: torch.Tensor, scale1p: torc
     _lib.call("cq_linear_w4a8_affine_lnmod", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc),
               float(eps), _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
               int(group_size), _ptr(_bias_bf16(bias)), _ptr(out), wp, wn, _stream(dev))
+    return out.reshape(*x.shape[:-1], n)
+
+
+def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, zeros_prepared: torch.Tensor,
+                          bias: torch.Tensor | None = None, *, out_op: str = "plain",
+                          residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                          shift: torch.Tensor | None = None, scale1p: torch.Tensor | None = None,
+                          group_size: int = 128, convrot_groupsize: int = 0, eps: float = 1e-6,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """A DiT-block linear with the elementwise step after it done in the GEMM's epilogue.
+
+    With y the bf16 output of ``w4a8_affine_linear`` (or of ``w4a8_affine_linear_lnmod`` when ``shift`` and
+    ``scale1p`` are given), returns
+      ``out_op="plain"``:  y
+      ``out_op="gelu"``:   ``F.gelu(y, approximate="tanh")``            (the MLP-up activation)
+      ``out_op="gated"``:  ``torch.addcmul(residual, gate, y)``         (the gated residual after the attention
+                           output and MLP-down linears; ``gate`` [N] or [1, N], ``residual`` [..., N] bf16)
+    ``out`` (bf16, contiguous, the output's shape) receives the result if given; it may be ``residual`` itself
+    (an in-place residual update)."""
+    if group_size != 128:
+        raise ValueError("the W4A8 affine kernel supports group_size 128")
+    kinds = {"plain": _lib.CQ_OUT_PLAIN, "gelu": _lib.CQ_OUT_GELU_TANH, "gated": _lib.CQ_OUT_GATED_RESIDUAL}
+    if out_op not in kinds:
+        raise ValueError(f"out_op must be one of {sorted(kinds)}")
+    if (shift is None) != (scale1p is None):
+        raise ValueError("shift and scale1p go together")
+    k = x.shape[-1]
+    if k != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
+    n = qweight.shape[0]
+    dev = _require_cuda(x, qweight, scale, zeros_prepared, bias, shift, scale1p, residual, gate, out)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    op = _lib.CQOutOp(kinds[out_op], None, 0, None)
+    if out_op == "gated":
+        if residual is None or gate is None:
+            raise ValueError("the gated residual needs residual and gate")
+        if residual.dtype != torch.bfloat16 or residual.shape[-1] != n or residual.numel() != m * n:
+            raise ValueError(f"residual must be bf16 with {m} rows of {n}")
+        r2 = residual.reshape(m, n)
+        if r2.stride(1) != 1:
+            raise ValueError("residual rows must be contiguous")
+        g = _vec_bf16(gate, n, "gate")
+        op.residual, op.residual_ld, op.gate = _ptr(r2), r2.stride(0), _ptr(g)
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    elif out.dtype != torch.bfloat16 or out.numel() != m * n or not out.is_contiguous():
+        raise ValueError(f"out must be contiguous bf16 with {m} x {n} elements")
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    sh = _vec_bf16(shift, k, "shift") if shift is not None else None
+    sc = _vec_bf16(scale1p, k, "scale1p") if scale1p is not None else None
+    _lib.call("cq_linear_w4a8_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc), float(eps),
+              _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
+              int(group_size), _ptr(_bias_bf16(bias)), ctypes.byref(op), _ptr(out), wp, wn, _stream(dev))
     return out.reshape(*x.shape[:-1], n)
 
 

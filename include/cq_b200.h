@@ -221,6 +221,38 @@ CQ_API int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const v
                           int64_t K, int group, void* stream);
 
 /*
+ * The elementwise step that follows a DiT block's linear, applied by the W4A8 affine GEMM to its bf16 result
+ * before the store.  y = the bf16 output cq_gemm_affine writes for the same inputs; then
+ *   CQ_OUT_PLAIN            out = y
+ *   CQ_OUT_GELU_TANH        out = bf16(gelu_tanh(y)),  gelu_tanh(y) = y / (1 + exp(-2 sqrt(2/pi) (y + 0.044715 y^3)))
+ *                           (torch F.gelu(y, approximate="tanh"), the MLP-up activation; the sigmoid form of
+ *                           0.5 y (1 + tanh(u)), within a few fp32 ulp of torch's value before the bf16 rounding)
+ *   CQ_OUT_GATED_RESIDUAL   out = bf16(residual + gate[n] * y)  (torch.addcmul(residual, gate, y), the gated residual
+ *                           after the attention-output and MLP-down linears; one fused multiply-add in fp32)
+ * residual: bf16 [M, residual_ld] (residual_ld >= N); it may be the output buffer itself (same pointer, same row
+ * stride: each element is read before it is overwritten) but must not overlap it otherwise.  gate: bf16 [N].
+ * The operations other than CQ_OUT_PLAIN need N % 8 == 0 and a 16-byte aligned output.
+ * No counterpart in the reference, whose model code runs these as torch ops on the linear's output.
+ */
+typedef enum {
+  CQ_OUT_PLAIN = 0,
+  CQ_OUT_GELU_TANH = 1,
+  CQ_OUT_GATED_RESIDUAL = 2
+} cq_out_kind;
+
+typedef struct {
+  int kind;                /* cq_out_kind */
+  const void* residual;    /* CQ_OUT_GATED_RESIDUAL: bf16 [M, residual_ld], 2-byte aligned */
+  int64_t residual_ld;     /*   row stride in elements */
+  const void* gate;        /*   bf16 [N] */
+} cq_out_op;
+
+/* cq_gemm_affine followed by the output operation `op` (NULL: CQ_OUT_PLAIN). */
+CQ_API int cq_gemm_affine_op(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
+                             const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
+                             int64_t M, int64_t N, int64_t K, int group, void* stream);
+
+/*
  * Fused linears (activation stage + GEMM) with caller-provided scratch.  `workspace` must hold at least
  * cq_linear_workspace_bytes(M, K) bytes of device memory (16-byte aligned).
  *
@@ -318,6 +350,34 @@ CQ_API int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int6
                                        const void* shift, const void* scale1p, float eps, const void* qweight,
                                        const void* s_bf16, const void* zt_bf16, int group, const void* bias,
                                        void* out, void* workspace, int64_t workspace_bytes, void* stream);
+/*
+ * cq_linear_w4a8_op: one DiT-block linear with the glue on both sides fused into its two kernels:
+ *   shift == NULL:  cq_linear_w4a8_affine of x (rotation rot_group, per-token int8)
+ *   shift != NULL:  cq_linear_w4a8_affine_lnmod of x (layer norm + modulation in the activation kernel, eps)
+ * followed by the output operation `op` in the GEMM's epilogue (cq_gemm_affine_op; NULL: CQ_OUT_PLAIN).
+ */
+CQ_API int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
+                             const void* scale1p, float eps, const void* qweight, const void* s_bf16,
+                             const void* zt_bf16, int group, const void* bias, const cq_out_op* op, void* out,
+                             void* workspace, int64_t workspace_bytes, void* stream);
+/*
+ * Per-token int8 activations of a row-parallel linear, whose K columns are split over ranks: each rank holds
+ * x bf16 [M, K] = its columns of the full rows, and the scale must be the one the whole row gives.
+ * cq_rotquant_absmax: per token t, amax[t] = the NaN-ignoring maximum of |rotated x| over this rank's columns and
+ *   amax[M_pad + t] = 1 if one of them is NaN, else 0 (f32 [2, M_pad]; padding tokens 0).
+ * cq_rotquant_scaled: after the ranks combine their amax arrays elementwise by a maximum (an all-reduce MAX), the
+ *   same outputs as cq_rotquant (CQ_ACT_INT8_ROW; flags: CQ_Q_KPERM only) with scale[t] =
+ *   max(amax[t] / 127, 1e-10); a token whose combined flag or maximum is not finite takes the non-finite rule of
+ *   cq_rotquant (NaN products give code 0).  The codes then equal, column for column, those cq_rotquant gives for
+ *   the unsplit rows, and each rank's GEMM over its K slice yields a partial sum of the linear.
+ * K % 256 == 0, K <= 24576, the rotation groups inside each rank's columns.  No counterpart in the reference (one
+ * GPU).
+ */
+CQ_API int cq_rotquant_absmax(const void* x, int64_t M, int64_t K, int rot_group, int64_t M_pad, float* amax,
+                              void* stream);
+CQ_API int cq_rotquant_scaled(const void* x, int64_t M, int64_t K, int rot_group, const float* amax, int64_t M_pad,
+                              int flags, void* q, float* scale, void* group_sums, void* stream);
+
 /*
  * cq_heads_to_rows: attention output o bf16 [Hp, S, D] (head-major, batch 1) -> outs[i][s, col0 + h*D + d] for
  * every buffer outs[i] (bf16 [S, ldo], 16-byte aligned, 1..8 buffers).  With one local buffer it is the transpose

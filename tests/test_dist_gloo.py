@@ -128,3 +128,75 @@ def test_head_parallel_rows_partition_the_fused_weight():
             for p in range(parts):
                 block = sh[p * hp * d:(p + 1) * hp * d]
                 assert block == list(range(p * hidden + r * hp * d, p * hidden + (r + 1) * hp * d))
+
+
+def _oracle_ops():
+    """CPU stand-ins for the three library calls RowParallelW4A8 makes, built on the oracle (test only): the rotated
+    slice's NaN-ignoring maxima and NaN flags, quantization with a given maximum, and the affine GEMM."""
+    import types
+    import numpy as np
+    from oracle import ref
+
+    def _rotated(x2, rot):
+        bits = x2.contiguous().view(torch.int16).numpy().view(np.uint16)
+        return ref.fwht_stages(ref.bf16_bits_to_f32(bits), rot)
+
+    def rotquant_absmax(x2, rot, m_pad=None):
+        v = _rotated(x2, rot)
+        mp = m_pad or v.shape[0]
+        out = np.zeros((2, mp), np.float32)
+        out[0, :v.shape[0]] = np.nan_to_num(np.abs(v), nan=0.0).max(axis=1)
+        out[1, :v.shape[0]] = np.isnan(v).any(axis=1)
+        return torch.from_numpy(out)
+
+    def rotquant_scaled(x2, rot, amax, m_pad=None, group_sums=False, kperm=False):
+        v = _rotated(x2, rot)
+        m = v.shape[0]
+        scale = np.maximum(amax[0, :m].numpy() * np.float32(1.0 / 127.0), np.float32(1e-10)).astype(np.float32)
+        inv = (np.float32(1.0) / scale).astype(np.float32)
+        q = np.clip(np.rint(v * inv[:, None]), -127, 127).astype(np.int16)
+        return torch.from_numpy(q), torch.from_numpy(scale), None
+
+    def gemm_affine(a, sa, gs, qweight, scale, zeros, bias, a_kperm=False, zeros_prepared=None):
+        y = ref.linear_affine(a.numpy(), sa.numpy(), ref.unpack_uint4(qweight.numpy()), scale.numpy(),
+                              zeros_prepared.numpy(), None if bias is None else bias.numpy())
+        return torch.from_numpy(y.astype(np.float32))
+
+    return types.SimpleNamespace(rotquant_absmax=rotquant_absmax, rotquant_scaled=rotquant_scaled,
+                                 gemm_affine=gemm_affine, prepare_affine_zeros=lambda z, g: z,
+                                 rotquant=None)
+
+
+def _row_parallel(rank, world):
+    import sys
+    import numpy as np
+    from comfy_quant_bench_b200 import dist as cqdist
+    from oracle import ref
+    stand_in = _oracle_ops()
+    sys.modules["comfy_quant_bench_b200.ops"] = stand_in          # the protocol under test, on CPU kernels
+    import comfy_quant_bench_b200
+    comfy_quant_bench_b200.ops = stand_in
+    m, n, k, rot = 6, 16, 1024, 256
+    x_bits = ref.synth_activations(m, k, seed=3)
+    w = ref.synth_weight(n, k, seed=4)
+    qw_u4, s, z = ref.weight_quant_affine(w, rot, 128)
+    bias = ref.synth_bias(n, seed=5).astype(np.float32)
+    packed = torch.from_numpy(ref.pack_int4(qw_u4.astype(np.int16)).view(np.uint8).view(np.int8))
+    layer = cqdist.RowParallelW4A8(packed, torch.from_numpy(s), torch.from_numpy(z), torch.from_numpy(bias), rank,
+                                   world, convrot_groupsize=rot)
+    x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16)
+    kl = k // world
+    y = layer(x[:, rank * kl:(rank + 1) * kl]).numpy().astype(np.float64)
+    qx, sx = ref.rotquant(x_bits, rot, "int8")
+    want = ref.linear_affine(qx, sx, qw_u4, s, z, bias)
+    return float(np.abs(y - want).max() / np.abs(want).max())
+
+
+def test_row_parallel_protocol_matches_the_full_linear():
+    """RowParallelW4A8 over 2 gloo ranks with oracle stand-ins for the kernels: the combined per-token maxima give
+    the full row's codes and scales, and the summed partials (bias once) equal the full linear to fp32 rounding."""
+    out = run_ranks(_row_parallel)
+    for rank in range(2):
+        st, val = out[rank]
+        assert st == "ok", val
+        assert val <= 1e-5, val

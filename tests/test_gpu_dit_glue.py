@@ -125,3 +125,119 @@ def test_dit_glue_rejects_bad_arguments(ops):
     w = torch.ones(96, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.CQShapeError):
         ops.qkv_rmsnorm_rope(y, w, w, torch.zeros(8, 48, 2, device="cuda"), q, q.clone(), q.clone(), 0)
+
+
+# ----------------------------------------------------------------------------------------------
+# output operations in the W4A8 affine GEMM's epilogue (GELU-tanh, gated residual)
+# ----------------------------------------------------------------------------------------------
+
+def _affine_layer(n, k, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn(n, k, device="cuda", generator=g) * 0.02
+    from comfy_quant_bench_b200 import ops as _ops
+    qw, sc, z = _ops.quantize_affine_w4_weight(w, 128, 256)
+    bias = (0.01 * torch.randn(n, device="cuda", generator=g)).to(torch.bfloat16)
+    return qw, sc, z, _ops.prepare_affine_zeros(z, 128), bias
+
+
+def _plain_via_gemm(ops, x, qw, sc, z, zt, bias):
+    """The plain linear's bf16 output through the tensor-core GEMM: inputs of eight tokens or fewer take the
+    few-token product, whose fp32 summation order differs, so they are padded to 16 rows and sliced."""
+    m = x.shape[0]
+    xp = torch.cat([x, torch.zeros(16 - m, x.shape[1], dtype=x.dtype, device=x.device)]) if m < 16 else x
+    return ops.w4a8_affine_linear(xp, qw, sc, z, bias, 128, 256, zeros_prepared=zt)[:m]
+
+
+@pytest.fixture(params=["one_sm", "pair"])
+def gemm_variant(request, ops):
+    """Runs a test once per kernel form of the int4-weight GEMM (one CTA per tile, or a CTA pair per tile)."""
+    from comfy_quant_bench_b200 import _lib
+    _lib.set_gemm_variant(_lib.CQ_GEMM_ONE_SM if request.param == "one_sm" else _lib.CQ_GEMM_PAIR)
+    yield request.param
+    _lib.set_gemm_variant(_lib.CQ_GEMM_AUTO)
+
+
+# (M, N, K): the MMDiT image-stream MLP-up shape, a text-stream shape, ragged M with N a multiple of 64 / of 32 only,
+# a few tokens (the GEMM, not the few-token product, applies the operation), N a multiple of 8 only
+_OP_SHAPES = [(4096, 12288, 3072), (256, 3072, 3072), (300, 384, 1024), (77, 416, 1024), (5, 256, 1024), (33, 264, 512)]
+
+
+@pytest.mark.parametrize("m,n,k", _OP_SHAPES)
+def test_gelu_output_matches_torch_gelu_of_the_linear(ops, gemm_variant, m, n, k):
+    """out = bf16(gelu_tanh(y)) on y, the plain linear's bf16 output: torch's F.gelu(y, approximate="tanh") up to
+    a few fp32 ulp before the bf16 rounding (the logistic form of tanh), so at most one bf16 rounding apart."""
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    qw, sc, z, zt, bias = _affine_layer(n, k, seed=n)
+    y = _plain_via_gemm(ops, x, qw, sc, z, zt, bias)
+    got = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gelu", convrot_groupsize=256)
+    _status_clear()
+    _within_one_rounding(got, F.gelu(y, approximate="tanh"))
+    assert float((got != F.gelu(y, approximate="tanh")).float().mean()) <= 2e-3
+
+
+@pytest.mark.parametrize("m,n,k", _OP_SHAPES)
+def test_gated_residual_output_matches_addcmul(ops, gemm_variant, m, n, k):
+    """out = bf16(residual + gate * y): torch.addcmul(residual, gate, y) on the plain linear's bf16 output, the
+    same fp32 fused multiply-add, so bit for bit; also in place (out is the residual) and with a residual whose rows
+    are strided (a column slice of a wider tensor)."""
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    qw, sc, z, zt, bias = _affine_layer(n, k, seed=n + 1)
+    res = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    gate = torch.randn(1, n, device="cuda", generator=g).to(torch.bfloat16)
+    y = _plain_via_gemm(ops, x, qw, sc, z, zt, bias)
+    want = torch.addcmul(res, gate, y)
+    got = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gated", residual=res, gate=gate, convrot_groupsize=256)
+    wide = torch.randn(m, n + 64, device="cuda", generator=g).to(torch.bfloat16)
+    wide[:, 16:16 + n] = res
+    got_strided = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gated", residual=wide[:, 16:16 + n],
+                                            gate=gate, convrot_groupsize=256)
+    inplace = res.clone()
+    ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gated", residual=inplace, gate=gate, out=inplace,
+                              convrot_groupsize=256)
+    _status_clear()
+    assert torch.equal(got, want)
+    assert torch.equal(got_strided, want)
+    assert torch.equal(inplace, want)
+
+
+def test_lnmod_gelu_output_matches_composite(ops, gemm_variant):
+    """The MLP-up linear of a DiT block in one call: layer norm + modulation in the activation kernel, GELU in the
+    GEMM epilogue, against F.gelu of w4a8_affine_linear_lnmod."""
+    m, k, n = 1024, 3072, 12288
+    x, shift, scale1p = _lnmod_inputs(m, k, seed=9)
+    qw, sc, z, zt, bias = _affine_layer(n, k, seed=10)
+    want = F.gelu(ops.w4a8_affine_linear_lnmod(x, shift, scale1p, qw, sc, zt, bias, 128, 256), approximate="tanh")
+    got = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gelu", shift=shift, scale1p=scale1p,
+                                    convrot_groupsize=256)
+    _status_clear()
+    _within_one_rounding(got, want)
+    assert float((got != want).float().mean()) <= 2e-3
+
+
+def test_output_op_rejects_bad_arguments(ops):
+    from comfy_quant_bench_b200 import _lib
+    m, n, k = 64, 256, 512
+    x = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
+    qw, sc, z, zt, bias = _affine_layer(n, k, seed=11)
+    res = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+    gate = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):            # gated without a residual
+        ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gated", gate=gate)
+    with pytest.raises(ValueError):            # unknown operation
+        ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="relu")
+    out = torch.zeros(m + 1, n, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.CQShapeError):     # residual overlaps the output without being it
+        ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gated", residual=out[1:], gate=gate, out=out[:m])
+    x196 = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
+    qw2, sc2, z2, zt2, b2 = _affine_layer(196, k, seed=12)
+    with pytest.raises(_lib.CQShapeError):     # N not a multiple of 8: the operations need the staged stores
+        ops.w4a8_affine_linear_op(x196, qw2, sc2, zt2, b2, out_op="gelu")
+    op = _lib.CQOutOp(7, None, 0, None)         # kind out of range, through the C ABI
+    ws = torch.empty(_lib.load().cq_linear_workspace_bytes(m, k), dtype=torch.uint8, device="cuda")
+    st = _lib.load().cq_linear_w4a8_op(x.data_ptr(), m, k, n, 256, None, None, 1e-6, qw.data_ptr(), sc.data_ptr(),
+                                        zt.data_ptr(), 128, bias.data_ptr(), _lib.ctypes.byref(op), res.data_ptr(),
+                                        ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert st == _lib.CQ_ERR_ARG
+    _status_clear()
