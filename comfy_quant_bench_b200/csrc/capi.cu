@@ -105,8 +105,19 @@ int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, 
   return cuda_status(cq::launch_act_rotquant(rot_group, swiglu != 0, mode, a, static_cast<cudaStream_t>(stream)));
 }
 
+static int rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
+                          float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream,
+                          bool scale_plus_one);
+
 int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
                       float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream) {
+  return rotquant_lnmod(x, M, K, rot_group, shift, scale1p, eps, M_pad, flags, q, scale, group_sums, stream, false);
+}
+
+// scale_plus_one: `scale1p` holds the modulation scale; the kernel forms bf16(1 + scale) itself
+static int rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
+                          float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream,
+                          bool scale_plus_one) {
   if (M < 0 || M_pad < M || M_pad > kMaxRows) return CQ_ERR_SHAPE;
   if (K < 256 || K % 256 != 0 || K > kMaxLnModK) return CQ_ERR_SHAPE;
   if (!valid_rot(rot_group)) return CQ_ERR_ARG;
@@ -121,7 +132,8 @@ int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const 
   if (int dv = check_device()) return dv;
   cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), 0, 0, (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
                      static_cast<__nv_bfloat16*>(group_sums), cq::rsplit_cols(static_cast<int>(K)),
-                     static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale1p), eps};
+                     static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale1p), eps,
+                     scale_plus_one ? 1 : 0};
   return cuda_status(cq::launch_act_rotquant(rot_group, false, CQ_ACT_INT8_ROW, a, static_cast<cudaStream_t>(stream)));
 }
 
@@ -485,7 +497,7 @@ int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, 
 }
 
 int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
-                      const void* scale1p, float eps, const void* qweight, const void* s_bf16, const void* zt_bf16,
+                      const void* mod_scale, float eps, const void* qweight, const void* s_bf16, const void* zt_bf16,
                       int group, const void* bias, const cq_out_op* op, void* out, void* workspace,
                       int64_t workspace_bytes, void* stream) {
   if (M == 0) return CQ_OK;
@@ -493,8 +505,8 @@ int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_gr
   Workspace w;
   if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
   const int e = shift != nullptr
-                    ? cq_rotquant_lnmod(x, M, K, rot_group, shift, scale1p, eps, w.mpad, CQ_Q_KPERM, w.xq, w.sx,
-                                        w.gsplit, stream)
+                    ? rotquant_lnmod(x, M, K, rot_group, shift, mod_scale, eps, w.mpad, CQ_Q_KPERM, w.xq, w.sx,
+                                     w.gsplit, stream, true)
                     : cq_rotquant(x, M, K, rot_group, 0, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
                                   stream);
   if (e) return e;

@@ -24,6 +24,7 @@ struct RotQuantArgs {
   const __nv_bfloat16* ln_shift;
   const __nv_bfloat16* ln_scale1p;
   float ln_eps;
+  int ln_scale_plus_one;  // ln_scale1p holds the modulation scale itself; the kernel forms bf16(1 + scale)
   // per-token int8 activations whose K columns are split over ranks (row-parallel linears).  amax_out set: the
   // kernel only writes, per token t, the NaN-ignoring maximum of |rotated x| over its columns (amax_out[t]) and
   // 1 if a NaN was among them, else 0 (amax_out[rows_pad + t]).  amax_in set (the same two rows, combined over the

@@ -703,7 +703,9 @@ __global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const Ro
         for (int i2 = 0; i2 < 8; ++i2) {
           const int i = 8 * k + i2;
           const uint32_t shb = (i2 & 1) ? (shw[i2 >> 1] & 0xFFFF0000u) : (shw[i2 >> 1] << 16);
-          const uint32_t scb = (i2 & 1) ? (scw[i2 >> 1] & 0xFFFF0000u) : (scw[i2 >> 1] << 16);
+          uint32_t scb = (i2 & 1) ? (scw[i2 >> 1] & 0xFFFF0000u) : (scw[i2 >> 1] << 16);
+          if (args.ln_scale_plus_one)   // bf16(1 + scale): torch's `1 + scale` on a bf16 tensor
+            scb = __float_as_uint(bf16_round(__fadd_rn(1.0f, __uint_as_float(scb))));
           const float2 ln = bf16x2_round(f2_mul(v[s][i], rstd));
           float2 xn = bf16x2_round(f2_fma(ln, make_float2(__uint_as_float(scb), __uint_as_float(scb)),
                                           make_float2(__uint_as_float(shb), __uint_as_float(shb))));

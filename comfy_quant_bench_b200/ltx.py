@@ -83,11 +83,12 @@ class AffineLinear:
         return ops.w4a8_affine_linear_lnmod(x, shift, scale1p, self.qweight, self.scale, self.zt, self.bias,
                                             self.cfg.group_size, self.cfg.convrot_groupsize)
 
-    def op(self, x, out_op, *, residual=None, gate=None, shift=None, scale1p=None):
+    def op(self, x, out_op, *, residual=None, gate=None, shift=None, scale=None):
         """This linear with GELU (``"gelu"``) or the gated residual (``"gated"``) in the GEMM epilogue, and with
-        shift/scale1p the modulated layer norm in the activation kernel (``ops.w4a8_affine_linear_op``)."""
+        shift / the modulation scale the modulated layer norm (by the bf16 1 + scale) in the activation kernel
+        (``ops.w4a8_affine_linear_op``)."""
         return ops.w4a8_affine_linear_op(x, self.qweight, self.scale, self.zt, self.bias, out_op=out_op,
-                                         residual=residual, gate=gate, shift=shift, scale1p=scale1p,
+                                         residual=residual, gate=gate, shift=shift, scale=scale,
                                          group_size=self.cfg.group_size, convrot_groupsize=self.cfg.convrot_groupsize)
 
     def quantize(self, x, shift=None, scale1p=None):
@@ -267,7 +268,7 @@ class LTXDiT:
             ops.qkv_rmsnorm_rope(y, b.norms[0], b.norms[1], self.rope, q, k, v, 0, eps=1e-6)
             x = b.out.op(self._heads_local(F.scaled_dot_product_attention(q, k, v)), "gated", residual=x, gate=m[2])
             x = b.co.op(self._heads_local(self._cross_attention(b, x, ctx, s)), "gated", residual=x, gate=b.one)
-            g = b.ff1.op(x, "gelu", shift=m[3], scale1p=b.scale1p[1])
+            g = b.ff1.op(x, "gelu", shift=m[3], scale=m[4])
             x = b.ff2.op(g, "gated", residual=x, gate=m[5])
         return x
 
@@ -283,7 +284,7 @@ class LTXDiT:
             ops.qkv_rmsnorm_rope(y, b.norms[0], b.norms[1], self.rope, q, k, v, 0, eps=1e-6)
             x = torch.addcmul(x, m[2], b.out(self._heads_local(F.scaled_dot_product_attention(q, k, v))))
             x = x + b.co(self._heads_local(self._cross_attention(b, x, ctx, s)))
-            g = b.ff1.op(x, "gelu", shift=m[3], scale1p=b.scale1p[1])      # this rank's ffn/P hidden columns
+            g = b.ff1.op(x, "gelu", shift=m[3], scale=m[4])      # this rank's ffn/P hidden columns
             x = torch.addcmul(x, m[5], b.ff2(g))
         return x
 

@@ -79,11 +79,12 @@ class QLinear:
         return ops.w4a8_affine_linear_lnmod(x, shift, scale1p, self.qweight, self.scale, self.zt, self.bias,
                                             self.cfg.group_size, self.cfg.convrot_groupsize, eps=1e-6)
 
-    def op(self, x: torch.Tensor, out_op: str, *, residual=None, gate=None, shift=None, scale1p=None) -> torch.Tensor:
-        """This linear with the step after it in the GEMM's epilogue: ``gelu`` (tanh) or ``gated``
-        (residual + gate * y); with shift/scale1p the layer norm + modulation before it in the activation kernel."""
+    def op(self, x: torch.Tensor, out_op: str, *, residual=None, gate=None, shift=None, scale=None) -> torch.Tensor:
+        """This linear with the step after it in the GEMM's epilogue: ``plain``, ``gelu`` (tanh) or ``gated``
+        (residual + gate * y); with shift / the modulation scale, the layer norm + modulation (by the bf16 1 + scale)
+        before it in the activation kernel."""
         return ops.w4a8_affine_linear_op(x, self.qweight, self.scale, self.zt, self.bias, out_op=out_op,
-                                         residual=residual, gate=gate, shift=shift, scale1p=scale1p,
+                                         residual=residual, gate=gate, shift=shift, scale=scale,
                                          group_size=self.cfg.group_size, convrot_groupsize=self.cfg.convrot_groupsize,
                                          eps=1e-6)
 
@@ -229,7 +230,7 @@ class MMDiT:
         for x, s, m, rot, lo, hi in ((txt, st, mt, self.rope_txt, 0, st_txt),
                                      (img, si, mi, self.rope_img, st_txt, s_all)):
             if fused:
-                y = s.qkv.lnmod(x, m[0], 1.0 + m[1])
+                y = s.qkv.op(x, "plain", shift=m[0], scale=m[1])
                 ops.qkv_rmsnorm_rope(y, s.q_norm, s.k_norm, rot, q, k, v, lo, eps=1e-6)
                 continue
             xn = torch.addcmul(m[0], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[1])
@@ -252,7 +253,7 @@ class MMDiT:
                 else:
                     x = torch.addcmul(x, m[2], s.out(att))
                 if c.epilogue_gelu:
-                    f = s.fc1.op(x, "gelu", shift=m[3], scale1p=1.0 + m[4])
+                    f = s.fc1.op(x, "gelu", shift=m[3], scale=m[4])
                 else:
                     f = F.gelu(s.fc1.lnmod(x, m[3], 1.0 + m[4]), approximate="tanh")
                 new.append(s.fc2.op(f, "gated", residual=x, gate=m[5]) if c.epilogue_gated

@@ -547,16 +547,17 @@ def w4a8_affine_linear_lnmod(x: torch.Tensor, shift: torch.Tensor, scale1p: torc
     return out.reshape(*x.shape[:-1], n)
 
 
-def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, zeros_prepared: torch.Tensor,
+def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.Tensor, zeros_prepared: torch.Tensor,
                           bias: torch.Tensor | None = None, *, out_op: str = "plain",
                           residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
-                          shift: torch.Tensor | None = None, scale1p: torch.Tensor | None = None,
+                          shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
                           group_size: int = 128, convrot_groupsize: int = 0, eps: float = 1e-6,
                           out: torch.Tensor | None = None) -> torch.Tensor:
     """A DiT-block linear with the elementwise step after it done in the GEMM's epilogue.
 
-    With y the bf16 output of ``w4a8_affine_linear`` (or of ``w4a8_affine_linear_lnmod`` when ``shift`` and
-    ``scale1p`` are given), returns
+    With y the bf16 output of ``w4a8_affine_linear`` (or, when ``shift`` and the modulation ``scale`` are given, of
+    ``w4a8_affine_linear_lnmod(x, shift, 1 + scale, ...)`` with the bf16 ``1 + scale`` formed in the activation
+    kernel), returns
       ``out_op="plain"``:  y
       ``out_op="gelu"``:   ``F.gelu(y, approximate="tanh")``            (the MLP-up activation)
       ``out_op="gated"``:  ``torch.addcmul(residual, gate, y)``         (the gated residual after the attention
@@ -568,13 +569,13 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, scale: torch.T
     kinds = {"plain": _lib.CQ_OUT_PLAIN, "gelu": _lib.CQ_OUT_GELU_TANH, "gated": _lib.CQ_OUT_GATED_RESIDUAL}
     if out_op not in kinds:
         raise ValueError(f"out_op must be one of {sorted(kinds)}")
-    if (shift is None) != (scale1p is None):
-        raise ValueError("shift and scale1p go together")
+    if (shift is None) != (scale is None):
+        raise ValueError("shift and scale go together")
     k = x.shape[-1]
     if k != qweight.shape[-1] * 2:
         raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
     n = qweight.shape[0]
-    dev = _require_cuda(x, qweight, scale, zeros_prepared, bias, shift, scale1p, residual, gate, out)
+    dev = _require_cuda(x, qweight, wscale, zeros_prepared, bias, shift, scale, residual, gate, out)
     x2 = _as2d(x)
     m = x2.shape[0]
     op = _lib.CQOutOp(kinds[out_op], None, 0, None)
@@ -595,9 +596,9 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, scale: torch.T
     ws = _workspace(m, k, dev)
     wp, wn = _ws_ptr(ws)
     sh = _vec_bf16(shift, k, "shift") if shift is not None else None
-    sc = _vec_bf16(scale1p, k, "scale1p") if scale1p is not None else None
+    sc = _vec_bf16(scale, k, "scale") if scale is not None else None
     _lib.call("cq_linear_w4a8_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc), float(eps),
-              _ptr(qweight.contiguous()), _ptr(scale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
+              _ptr(qweight.contiguous()), _ptr(wscale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
               int(group_size), _ptr(_bias_bf16(bias)), ctypes.byref(op), _ptr(out), wp, wn, _stream(dev))
     return out.reshape(*x.shape[:-1], n)
 

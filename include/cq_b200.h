@@ -353,11 +353,13 @@ CQ_API int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int6
 /*
  * cq_linear_w4a8_op: one DiT-block linear with the glue on both sides fused into its two kernels:
  *   shift == NULL:  cq_linear_w4a8_affine of x (rotation rot_group, per-token int8)
- *   shift != NULL:  cq_linear_w4a8_affine_lnmod of x (layer norm + modulation in the activation kernel, eps)
+ *   shift != NULL:  cq_linear_w4a8_affine_lnmod of x with scale1p = bf16(1 + mod_scale) formed inside the
+ *                   activation kernel (mod_scale bf16 [K], the adaLN scale as the modulation linear produced it;
+ *                   torch's `1 + scale` on a bf16 tensor), eps
  * followed by the output operation `op` in the GEMM's epilogue (cq_gemm_affine_op; NULL: CQ_OUT_PLAIN).
  */
 CQ_API int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
-                             const void* scale1p, float eps, const void* qweight, const void* s_bf16,
+                             const void* mod_scale, float eps, const void* qweight, const void* s_bf16,
                              const void* zt_bf16, int group, const void* bias, const cq_out_op* op, void* out,
                              void* workspace, int64_t workspace_bytes, void* stream);
 /*

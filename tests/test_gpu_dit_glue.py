@@ -203,14 +203,18 @@ def test_gated_residual_output_matches_addcmul(ops, gemm_variant, m, n, k):
 
 
 def test_lnmod_gelu_output_matches_composite(ops, gemm_variant):
-    """The MLP-up linear of a DiT block in one call: layer norm + modulation in the activation kernel, GELU in the
-    GEMM epilogue, against F.gelu of w4a8_affine_linear_lnmod."""
+    """The MLP-up linear of a DiT block in one call: layer norm + modulation (with the bf16 1 + scale formed in the
+    activation kernel) and GELU in the GEMM epilogue, against F.gelu of w4a8_affine_linear_lnmod with torch's
+    1 + scale."""
     m, k, n = 1024, 3072, 12288
-    x, shift, scale1p = _lnmod_inputs(m, k, seed=9)
+    x, shift, _ = _lnmod_inputs(m, k, seed=9)
+    scale = (0.3 * torch.randn(k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(8))).to(torch.bfloat16)
     qw, sc, z, zt, bias = _affine_layer(n, k, seed=10)
-    want = F.gelu(ops.w4a8_affine_linear_lnmod(x, shift, scale1p, qw, sc, zt, bias, 128, 256), approximate="tanh")
-    got = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gelu", shift=shift, scale1p=scale1p,
+    want = F.gelu(ops.w4a8_affine_linear_lnmod(x, shift, 1.0 + scale, qw, sc, zt, bias, 128, 256), approximate="tanh")
+    got = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gelu", shift=shift, scale=scale,
                                     convrot_groupsize=256)
+    plain = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, shift=shift, scale=scale, convrot_groupsize=256)
+    assert torch.equal(plain, ops.w4a8_affine_linear_lnmod(x, shift, 1.0 + scale, qw, sc, zt, bias, 128, 256))
     _status_clear()
     _within_one_rounding(got, want)
     assert float((got != want).float().mean()) <= 2e-3
