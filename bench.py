@@ -486,6 +486,9 @@ def run_ours(args, world, rank, local):
                                     "dense rate is twice bf16)",
                      "frac_vs_library_int8": (achieved / lib_int8["tops"]) if "tops" in lib_int8 else None,
                      "traffic": traffic,
+                     "traffic_source": (f"profiles/gemm_{args.workload}_traffic.json: dram__bytes_read.sum + "
+                                        "dram__bytes_write.sum of one ncu capture of this kernel, not of this run")
+                                       if traffic is not None else None,
                      "algorithmic": f"2*M*N*K = {ops_per_step:.4g} int-ops per launch"},
         "rotquant_roofline": {"bound": "hbm", "achieved": act_bytes / (quant_ms / 1e3) / 1e9,
                               "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -981,6 +984,52 @@ def run_sweep(args, world, rank, local):
     ms = timed(lambda: ops.convrot_w4a4_linear(h, qd, sd, None, convrot_groupsize=256, input_act="swiglu"), args.steps)
     emit({"case": "convrot_w4a4_linear_swiglu_prologue", "M": m, "N": nd, "K": kd, "rot": 256, "ms": ms,
           "tops": 2.0 * m * nd * kd / (ms / 1e3) / 1e12})
+    # --- per-group scales on both sides (the reference GEMM's policy 4): the node's forward at T, and the GEMM
+    #     alone at the reference bench's 4096^3 ---
+    for m, n, k in ((4096, 12288, 3072), (4096, 4096, 4096)):
+        w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+        qg, sg = ops.quantize_int4_groupwise_weight(w, 128, 256)
+        x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+        ms = timed(lambda: ops.w4a4_groupwise_linear(x, qg, sg), args.steps)
+        emit({"case": "w4a4_groupwise_linear_policy4", "M": m, "N": n, "K": k, "ms": ms,
+              "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12, "frac_of_int8_peak": 2.0 * m * n * k / (ms / 1e3) / 1e12 / int8_peak,
+              "note": "per-group activation quantizer + g128 x g128 GEMM (policy 4)"})
+        qa, sa = ops.quant(x, 128)
+        ms = timed(lambda: ops.gemm(qa, qg, sa, sg, pol=4), args.steps)
+        emit({"case": "gemm_policy4", "M": m, "N": n, "K": k, "ms": ms,
+              "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12, "frac_of_int8_peak": 2.0 * m * n * k / (ms / 1e3) / 1e12 / int8_peak})
+        del w, x
+    # --- output operations in the affine epilogue (a DiT block's MLP-up with GELU, output projections with the
+    #     gated residual), against the plain linear followed by the torch op ---
+    for m, n, k, op in ((4096, 12288, 3072, "gelu"), (4096, 3072, 3072, "gated"), (4096, 3072, 12288, "gated")):
+        w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+        qw, sc, z = ops.quantize_affine_w4_weight(w, 128, 256)
+        zt = ops.prepare_affine_zeros(z, 128)
+        x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+        res = torch.randn(m, n, generator=gen, device=dev).to(torch.bfloat16)
+        gate = torch.randn(n, generator=gen, device=dev).to(torch.bfloat16)
+        kw = {"residual": res, "gate": gate} if op == "gated" else {}
+        ms = timed(lambda: ops.w4a8_affine_linear_op(x, qw, sc, zt, None, out_op=op, convrot_groupsize=256, **kw),
+                   args.steps)
+
+        def then_torch():
+            y = ops.w4a8_affine_linear(x, qw, sc, z, None, 128, 256, zeros_prepared=zt)
+            return torch.nn.functional.gelu(y, approximate="tanh") if op == "gelu" else torch.addcmul(res, gate, y)
+
+        ms_t = timed(then_torch, args.steps)
+        emit({"case": f"w4a8_affine_linear_epilogue_{op}", "M": m, "N": n, "K": k, "ms": ms,
+              "ms_linear_then_torch_op": ms_t})
+        del w, x, res
+    # --- row-parallel activation stage (LTX MLP-down slice on one of 8 ranks: K = 16384 / 8), both phases ---
+    m, k = 32768, 2048
+    x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+    amax = ops.rotquant_absmax(x, 256)
+    ms1 = timed(lambda: ops.rotquant_absmax(x, 256), args.steps)
+    ms2 = timed(lambda: ops.rotquant_scaled(x, 256, amax, group_sums=True, kperm=True), args.steps)
+    ms0 = timed(lambda: ops.rotquant(x, 256, _lib.CQ_ACT_INT8_ROW, group_sums=True, kperm=True), args.steps)
+    emit({"case": "rotquant_row_parallel_phases", "M": m, "K": k, "ms_absmax": ms1, "ms_scaled": ms2,
+          "ms_single_pass": ms0, "note": "the all-reduce MAX of the [2, M] maxima runs between the two phases"})
+    del x
     if _lib.take_device_status() != (0, 0):
         raise RuntimeError("device status set")
 
