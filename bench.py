@@ -436,8 +436,9 @@ def run_ours(args, world, rank, local):
         lib_int8 = {"unavailable": str(exc).splitlines()[0][:200]}
 
     # The multi-GPU designs, measured beside the replicas of the headline line: the fused column-parallel linear
-    # (strong scaling of the same linear over the ranks, gather inside the GEMM) at N > 1, and the 60-block MMDiT step
-    # as data-parallel replicas at every N.  Every rank takes part; rank 0 reports.
+    # (strong scaling of the same linear over the ranks, gather inside the GEMM) at N > 1, the 60-block MMDiT step
+    # as data-parallel replicas at every N, and 8 blocks of the LTX step split over the ranks (strong scaling,
+    # row-parallel projections) at every N.  Every rank takes part; rank 0 reports.
     subrecords = {}
     if args.workload == "w4a8" and args.mode == "dp" and not args.no_subrecords:
         if world > 1:
@@ -452,6 +453,7 @@ def run_ours(args, world, rank, local):
             del xs, ws, bs
             torch.cuda.empty_cache()
         subrecords["mmdit_step"] = mmdit_dp_subrecord(world, rank, local)
+        subrecords["ltx_step"] = ltx_tp_subrecord(world, rank, local)
 
     if rank != 0:
         return
@@ -648,6 +650,40 @@ def mmdit_dp_subrecord(world, rank, local, steps: int = 5, warmup: int = 3) -> d
     return {"workload": "mmdit_step (60 blocks, hidden 3072, 4096 + 256 tokens, every linear W4A8, fused glue)",
             "parallelism": f"dp{world}", "step_ms": step_ms, "steps_per_s": world / (step_ms / 1e3),
             "timing": f"{steps} graph replays per rank after {warmup} warm-up steps, max over ranks"}
+
+
+def ltx_tp_subrecord(world, rank, local, blocks: int = 8, steps: int = 3, warmup: int = 2) -> dict:
+    """An LTX-like video DiT step (hidden 4096, 32,768 tokens, every linear W4A8), ``blocks`` of its 48 blocks, split
+    over the ranks (strong scaling): one GPU runs it whole; at N > 1 attention is head-parallel, the MLP-up
+    column-parallel, the output projections and MLP-down row-parallel with NCCL all-reduces.  Eager; step latency =
+    max over ranks of the mean device-timed step."""
+    from comfy_quant_bench_b200 import ltx
+    dev = torch.device("cuda", local)
+    cfg = ltx.LTXConfig(blocks=blocks)
+    model = ltx.LTXDiT(cfg, device=dev, seed=0, rank=rank, world=world)
+    x, ctx = model.inputs(seed=1)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        model.step(x, ctx)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    for e0, e1 in evs:
+        e0.record(stream)
+        model.step(x, ctx)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    step_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in evs), world) / steps
+    del model
+    torch.cuda.empty_cache()
+    return {"workload": f"ltx_step ({blocks} of 48 blocks, hidden 4096, 32768 tokens, every linear W4A8)",
+            "parallelism": f"tp{world}" if world > 1 else "1 GPU", "step_ms": step_ms, "ms_per_block": step_ms / blocks,
+            "scaling": "strong",
+            "sharding": "head-parallel attention, column-parallel MLP-up, row-parallel output projections and "
+                        "MLP-down (NCCL all-reduces)" if world > 1 else None,
+            "timing": f"{steps} eager steps per rank after {warmup} warm-up steps, max over ranks"}
 
 
 def run_mmdit(args, world, rank, local):
