@@ -1035,6 +1035,24 @@ def run_sweep(args, world, rank, local):
         emit({"case": "gemm_policy4", "M": m, "N": n, "K": k, "ms": ms,
               "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12, "frac_of_int8_peak": 2.0 * m * n * k / (ms / 1e3) / 1e12 / int8_peak})
         del w, x
+    # --- integer weight ratios (policies 5 / 7 / 17) at the reference bench's 4096^3: int4 codes, ratios in [1, 255] ---
+    m = n = k = 4096
+    a4 = torch.randint(-7, 8, (m, k), generator=gen, device=dev, dtype=torch.int8)
+    b4 = torch.randint(-7, 8, (n, k), generator=gen, device=dev, dtype=torch.int8)
+    ap = ((a4[:, 0::2].to(torch.int16) & 0xF) | ((a4[:, 1::2].to(torch.int16) & 0xF) << 4)).to(torch.uint8).view(torch.int8)
+    bp = ((b4[:, 0::2].to(torch.int16) & 0xF) | ((b4[:, 1::2].to(torch.int16) & 0xF) << 4)).to(torch.uint8).view(torch.int8)
+    sa_r = torch.rand(m, generator=gen, device=dev) * 0.01 + 0.005
+    sb_r = (torch.rand(n, generator=gen, device=dev) * 0.01 + 0.005) / 255
+    for pol in (5, 7, 17):
+        grp = 64 if pol % 10 == 5 else 128
+        cw = torch.randint(1, 256, (k // grp, n), generator=gen, device=dev, dtype=torch.int32)
+        if pol >= 10:
+            cw = cw.to(torch.uint8)
+        ms = timed(lambda: ops.gemm(ap, bp, sa_r, sb_r, None, cw, None, pol=pol), args.steps)
+        emit({"case": f"gemm_policy{pol}", "M": m, "N": n, "K": k, "ms": ms,
+              "tops": 2.0 * m * n * k / (ms / 1e3) / 1e12, "frac_of_int8_peak": 2.0 * m * n * k / (ms / 1e3) / 1e12 / int8_peak,
+              "note": "includes the activations' int4 unpack (the reference interface takes packed codes)"})
+    del a4, b4, ap, bp
     # --- output operations in the affine epilogue (a DiT block's MLP-up with GELU, output projections with the
     #     gated residual), against the plain linear followed by the torch op ---
     for m, n, k, op in ((4096, 12288, 3072, "gelu"), (4096, 3072, 3072, "gated"), (4096, 3072, 12288, "gated")):

@@ -72,6 +72,7 @@ SIGNATURES = {
     "cq_group_sum_cols": (_i64, [_i64]),
     "cq_prepare_affine_zeros": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
     "cq_gemm_groupwise": (_int, [_vp, _int, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "cq_gemm_intratio": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     "cq_gemm_affine": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_gemm_affine_op": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _opp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_linear_workspace_bytes": (_i64, [_i64, _i64]),

@@ -296,6 +296,22 @@ int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, int64_t s
                                static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
 }
 
+int cq_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const void* b_packed, const float* sb,
+                     const void* cw, int cw_u8, int cw_group, const void* bias, void* out, int64_t M, int64_t N,
+                     int64_t K, void* stream) {
+  if (a_kperm != 0 && a_kperm != 1) return CQ_ERR_ARG;
+  if (cw_group != 64 && cw_group != 128) return CQ_ERR_ARG;
+  if (cw_u8 != 0 && cw_u8 != 1) return CQ_ERR_ARG;
+  if (int e = check_gemm(a, b_packed, out, M, N, K)) return e;
+  if (M == 0) return CQ_OK;
+  if (K >= 171840) return CQ_ERR_SHAPE;          // the reference's int32 accumulator bound
+  if (sa == nullptr || sb == nullptr || cw == nullptr) return CQ_ERR_ARG;
+  if (!aligned(cw, cw_u8 ? 1 : 4)) return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  return cq::launch_gemm_intratio(a, a_kperm, sa, b_packed, sb, cw, cw_u8, cw_group, bias, out, static_cast<int>(M),
+                                  static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
+}
+
 static int gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                        const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
                        int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl);

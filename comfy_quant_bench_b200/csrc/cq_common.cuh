@@ -154,6 +154,17 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
+// Every stage of a ring of n stages that `issued` loads reached: wait (bounded, limit_ns each) for the phase of the
+// last load issued into it.  Used before a CTA releases its shared memory, so that no copy still in flight can
+// land in it (on a normal end every load was consumed long before, and each wait returns at once).
+__device__ __forceinline__ void drain_ring(uint64_t* full, int n, uint32_t issued, unsigned long long limit_ns) {
+  for (int s = 0; s < n; ++s) {
+    if (issued <= static_cast<uint32_t>(s)) break;
+    const uint32_t last = issued - 1 - ((issued - 1 - s) % n);   // index of the last load into stage s
+    mbar_wait_drain(&full[s], (last / n) & 1u, limit_ns);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // thread-block clusters (CTA pairs of the 2-SM GEMM).  Remote mbarrier arrivals only; no multicast loads.
 // ---------------------------------------------------------------------------------------------

@@ -54,6 +54,9 @@ constexpr unsigned long long kDrainNs = 50000000ull;   // per wait while unwindi
 // per-group drains (affine and group scales) keep the output staging of the TMA stores
 template <int EPI>
 constexpr bool kPerGroup = (EPI == EPI_AFFINE || EPI == EPI_GROUP);
+// every group's partial sum in its own accumulator buffer (the integer-ratio epilogue too)
+template <int EPI>
+constexpr bool kDrainPerGroup = kPerGroup<EPI> || EPI == EPI_INTRATIO;
 constexpr int kSgStages = 4;                   // group epilogue: ring of per-group token scales
 constexpr int kSgBytes = kTok * 4;             //   one stage: the tile's tokens' scales of one group (f32)
 
@@ -75,14 +78,6 @@ struct Plan {
   static constexpr int kBytes = kSg + kSgRingBytes + 1024 /*align slack*/;
 };
 
-// every ring stage of a ring of n stages that `issued` loads reached: wait (bounded) for the last load's phase
-__device__ __forceinline__ void drain_ring(uint64_t* full, int n, uint32_t issued) {
-  for (int s = 0; s < n; ++s) {
-    if (issued <= static_cast<uint32_t>(s)) break;
-    const uint32_t last = issued - 1 - ((issued - 1 - s) % n);   // index of the last load into stage s
-    mbar_wait_drain(&full[s], (last / n) & 1u, kDrainNs);
-  }
-}
 
 template <int EPI, int BFMT, bool KPERM, bool GLU, int OP>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -233,9 +228,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
         }
       }
       // every load issued has landed before this CTA's shared memory can be released (a no-op on a normal end)
-      drain_ring(full_x, kXS, x_issued);
-      drain_ring(full_w, kWStages, w_issued);
-      if (EPI == EPI_GROUP) drain_ring(sg_full, kSgStages, g_issued);
+      drain_ring(full_x, kXS, x_issued, kDrainNs);
+      drain_ring(full_w, kWStages, w_issued, kDrainNs);
+      if (EPI == EPI_GROUP) drain_ring(sg_full, kSgStages, g_issued, kDrainNs);
     } else if (warp == 1 && lane == 0 && rank == 0) {
       // ------------------------------ MMA issuer (leader) ------------------------------
       const uint32_t idesc = idesc_i8(kRowsPair, kTok);
@@ -275,22 +270,40 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
           if (++buf == kBufs) { buf = 0; bph ^= 1u; }
         }
         for (int kb = 0; kb < kblocks && ok; ++kb) {
-          // affine / group scales: every group has its own accumulator buffer; row/col: one buffer per tile
-          const bool new_buf = kPerGroup<EPI> || kb == 0;
+          // affine / group scales / integer ratios: every group has its own accumulator buffer; row/col: one
+          // buffer per tile
+          const bool new_buf = kDrainPerGroup<EPI> || kb == 0;
           if (!(ok = (new_buf ? buffer_and_operands_ready(46) : operands_ready(47)))) break;
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kTok);
           const uint32_t a_base = smem_u32(sm_conv + cs * kWuBytes);
           const uint32_t b_base = smem_u32(sm_x + xs * kXBytes);
+          if (EPI == EPI_INTRATIO && args.cw_group == 64) {
+            // two 64-wide ratio groups per K block, each summed in its own buffer
 #pragma unroll
-          for (int k = 0; k < kBK / 32; ++k) {
-            // per-group drains: every 128-wide group starts its own int32 sum
-            const uint32_t acc = kPerGroup<EPI> ? (k > 0) : (kb > 0 || k > 0);
-            mma_i8_pair(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc, acc);
+            for (int k = 0; k < kBK / 32; ++k) {
+              if (k == 2) {
+                tc_commit_pair(&tmem_full[buf]);
+                if (++buf == kBufs) { buf = 0; bph ^= 1u; }
+                if (!(ok = mbar_wait(&tmem_empty[buf], bph, abort_flag, 49))) break;
+                tc_fence_after();
+              }
+              const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kTok);
+              mma_i8_pair(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc,
+                          (k & 1) ? 1u : 0u);
+            }
+            if (!ok) break;
+          } else {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kTok);
+#pragma unroll
+            for (int k = 0; k < kBK / 32; ++k) {
+              // per-group drains: every 128-wide group starts its own int32 sum
+              const uint32_t acc = kDrainPerGroup<EPI> ? (k > 0) : (kb > 0 || k > 0);
+              mma_i8_pair(d_tmem, smem_desc_k_sw128(a_base + 32 * k), smem_desc_k_sw128(b_base + 32 * k), idesc, acc);
+            }
           }
           tc_commit_pair(&empty_x[xs]);
           tc_commit_pair(&empty_conv[cs]);
-          if (kPerGroup<EPI>) {
+          if (kDrainPerGroup<EPI>) {
             tc_commit_pair(&tmem_full[buf]);
             if (++buf == kBufs) { buf = 0; bph ^= 1u; }
           }
@@ -613,6 +626,74 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
             orow += 4 * static_cast<int64_t>(N);
           }
         }
+      } else if constexpr (EPI == EPI_INTRATIO) {
+        // integer ratios (the reference's policies 5/7/15/17): acc = sum_g P_g * cw[g, n] in int32, exactly as the
+        // reference sums it, then bf16(float(acc) * sa[m] * sb[n] + bias) in its order.  The int4 unpack stores
+        // 16 * v, so the TMEM sums are 16 P_g: summed as they are while 16 |acc| stays inside int32 (K <= 8192: at
+        // most 64 groups of 128, or 128 of 64, of |16 P cw| <= 2^25) and divided by 16 at the end (float(16 acc) / 16
+        // = float(acc), a power-of-two scaling), else shifted back to P_g first.
+        int acc[kWarpTok];
+#pragma unroll
+        for (int j = 0; j < kWarpTok; ++j) acc[j] = 0;
+        const int ngroups = K / args.cw_group;
+        const bool pre_shift = K > 8192;
+        auto load_cw = [&](int gg) -> int {
+          if (!n_ok) return 0;
+          const int64_t i = static_cast<int64_t>(gg) * N + n;
+          return args.cw_u8 ? static_cast<int>(__ldg(static_cast<const uint8_t*>(args.cw) + i))
+                            : __ldg(static_cast<const int*>(args.cw) + i);
+        };
+        int cw_next = load_cw(0);
+        for (int g = 0; g < ngroups; ++g) {
+          const int cwg = cw_next;
+          if (g + 1 < ngroups) cw_next = load_cw(g + 1);
+          if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 60))) break;
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + lane_addr + static_cast<uint32_t>(buf * kTok + half * kWarpTok);
+          uint32_t ra[32], rb[32];
+          auto add_chunk = [&](const uint32_t (&r)[32], int ch) {
+            if (pre_shift) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[32 * ch + j] += (static_cast<int>(r[j]) >> 4) * cwg;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[32 * ch + j] += static_cast<int>(r[j]) * cwg;
+            }
+          };
+          tmem_ld_32x32b_x32(taddr, ra);
+          tmem_wait_ld_dep(ra);
+          tmem_ld_32x32b_x32(taddr + 32, rb);
+          add_chunk(ra, 0);
+          tmem_wait_ld_dep(rb);
+          tmem_ld_32x32b_x32(taddr + 64, ra);
+          add_chunk(rb, 1);
+          tmem_wait_ld_dep(ra);
+          tmem_ld_32x32b_x32(taddr + 96, rb);
+          add_chunk(ra, 2);
+          tmem_wait_ld_dep(rb);
+          release(buf);
+          add_chunk(rb, 3);
+          if (++buf == kBufs) { buf = 0; buf_phase ^= 1u; }
+        }
+        if (!ok) break;
+        stage_sa();
+        if (n_ok) {
+          const float sbn = args.sb[n];
+          const float unscale = pre_shift ? 1.0f : 0.0625f;
+          __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
+#pragma unroll
+          for (int j2 = 0; j2 < kWarpTok / 2; ++j2) {
+            const int mm = 2 * j2;
+            const float v0 = __fmaf_rn(__fmul_rn(__int2float_rn(acc[mm]) * unscale, sa_stage[mm]), sbn, bias);
+            const float v1 = __fmaf_rn(__fmul_rn(__int2float_rn(acc[mm + 1]) * unscale, sa_stage[mm + 1]), sbn, bias);
+            if (m_full || m0 + mm + 1 < M) {
+              st_bf16_pair_ordered(orow, orow + N, v0, v1);
+            } else if (m0 + mm < M) {
+              *orow = __float2bfloat16_rn(v0);
+            }
+            orow += 2 * static_cast<int64_t>(N);
+          }
+        }
       } else {
         if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 55))) break;
         tc_fence_after();
@@ -856,7 +937,7 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   // a few tokens (adaLN modulation): read the weights once with a warp per row instead of 256-token MMA tiles
   // (plain outputs only: the output operations live in the GEMM's epilogue)
   if (outs == nullptr && plain && gemv_affine_fits(M, a_kperm))
-    return launch_gemv_affine(a, sa, b, s, zt, bias, out, M, N, K, st) == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
+    return launch_gemv_affine(a, sa, b, s, zt, bias, out, M, N, K, st, pdl) == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
   GemmArgs g{};
   g.pdl = pdl;
   if (!plain) {
@@ -886,6 +967,24 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   if (g.out_op == OUT_GELU) return launch(std::integral_constant<int, OUT_GELU>{});
   if (g.out_op == OUT_GATED) return launch(std::integral_constant<int, OUT_GATED>{});
   return launch(std::integral_constant<int, OUT_PLAIN>{});
+}
+
+// Integer weight ratios per group (the reference's policies 5/7/15/17): int4 activation codes (int8-held) x packed
+// signed int4 weights, acc = sum_g P_g * cw[g, n] in int32 over groups of cw_group (64 or 128) K columns, then
+// bf16(float(acc) * sa[m] * sb[n] + bias).  cw is int32 or (cw_u8) uint8 [K/cw_group, N].
+int launch_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const void* b, const float* sb, const void* cw,
+                         int cw_u8, int cw_group, const void* bias, void* out, int M, int N, int K, cudaStream_t st) {
+  GemmArgs g{};
+  g.sa = sa;
+  g.sb = sb;
+  g.cw = cw;
+  g.cw_u8 = cw_u8;
+  g.cw_group = cw_group;
+  g.bias = static_cast<const __nv_bfloat16*>(bias);
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.M = M; g.N = N; g.K = K;
+  if (a_kperm) return launch_gemm_pair_t<EPI_INTRATIO, BF_S4, true>(a, b, nullptr, g, st);
+  return launch_gemm_pair_t<EPI_INTRATIO, BF_S4, false>(a, b, nullptr, g, st);
 }
 
 // Per-group scales on both sides (the reference's policy 4): int4 activation codes (int8-held) x packed signed int4

@@ -54,8 +54,10 @@ constexpr int kProducerRegs = 40;    // warps 0-7 (producer, MMA, converters)
 constexpr int kEpilogueRegs = 216;   // warps 8-15; 256*40 + 256*216 = 128*512, the launch allocation
 
 // ROWCOL: per-token x per-row scales once per tile (the reference's policy 0); AFFINE: per-group weight scale and
-// zero, per-token activation scale; GROUP: per-group scales on both sides (the reference's policy 4, CTA-pair kernel)
-enum : int { EPI_ROWCOL = 0, EPI_AFFINE = 1, EPI_GROUP = 2 };
+// zero, per-token activation scale; GROUP: per-group scales on both sides (the reference's policy 4, CTA-pair kernel);
+// INTRATIO: integer weight ratios per 64- or 128-wide group summed in int32, then per-token x per-row scales (the
+// reference's policies 5/7/15/17, CTA-pair kernel)
+enum : int { EPI_ROWCOL = 0, EPI_AFFINE = 1, EPI_GROUP = 2, EPI_INTRATIO = 3 };
 enum : int { BF_S4 = 0, BF_U4 = 1, BF_S8 = 2 };
 
 // shared-memory plan per epilogue and weight format.  The affine kernel trades one TMA stage for the output
@@ -104,6 +106,9 @@ struct GemmArgs {
   int64_t res_ld;        // OUT_GATED: row stride (elements) of res
   const __nv_bfloat16* res;   // OUT_GATED: residual [M, res_ld] (may be `out` itself)
   const __nv_bfloat16* gate;  // OUT_GATED: per-column gate [N]
+  const void* cw;        // intratio: integer weight ratios [K/cw_group, N], int32 or uint8
+  int cw_u8;             // intratio: cw holds uint8 (policies 15/17) instead of int32 (5/7)
+  int cw_group;          // intratio: 64 or 128 K columns per ratio
   int pdl;               // host: launch with programmatic stream serialization (the kernel's prologue - barrier
                          // set-up, TMEM allocation, descriptor prefetch - overlaps the tail of the previous kernel;
                          // every thread waits for that kernel's completion before its first read of any input)
@@ -234,8 +239,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   uint64_t* zt_full = tmem_empty + kNumBufs;   // affine: per converter pair, the TMA load of its zero-point operand
   uint64_t* box_free = zt_full + kConvStages;   // affine, 64-column boxes: per epilogue warp pair, staging free
   uint64_t* box_full = box_free + 4;            //   and both halves of the box written
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(box_full + 4);
-  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 8) * 8 + 8 <= P::kSaStage - P::kData,
+  uint64_t* mma_done = box_full + 4;            // every MMA this CTA issued has completed (before the TMEM release)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  static_assert((2 * kTmaStages + 3 * kConvStages + 2 * kNumBufs + 9) * 8 + 8 <= P::kSaStage - P::kData,
                 "the barriers, the TMEM address and the abort flag fit the region before the scale staging");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -280,6 +286,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       mbar_init(&box_free[p], 1);
       mbar_init(&box_full[p], 2);
     }
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tm_x);
@@ -304,7 +311,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     if (warp == 0 && lane == 0) {
       // ------------------------------ TMA producer ------------------------------
       int stage = 0;
-      uint32_t phase = 0;
+      uint32_t phase = 0, issued = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
         int mt, nt, t0, width;
         coords(item, mt, nt, t0, width);
@@ -317,6 +324,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             uint8_t* st = sm_tma + stage * P::kTmaStageBytes;
             mbar_arrive_expect_tx(&full_tma[stage], kXBytes);
             tma_load_2d(st, &tm_r, &full_tma[stage], p * 128, m0);
+            ++issued;
             if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
           }
         }
@@ -327,9 +335,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           tma_load_2d(st, &tm_x, &full_tma[stage], kb * kBK, m0);
           if (BFMT == BF_S8) tma_load_2d(st + kXBytes, &tm_w, &full_tma[stage], kb * kBK, n0);
           else tma_load_2d(st + kXBytes, &tm_w, &full_tma[stage], kb * (kBK / 2), n0);
+          ++issued;
           if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
         }
       }
+      // every load issued has landed before the CTA's shared memory can be released (at once on a normal end)
+      drain_ring(full_tma, kTmaStages, issued, 50000000ull);
     } else if (warp == 1 && lane == 0) {
       // ------------------------------ MMA issuer ------------------------------
       int stage = 0, cstage = 0;
@@ -407,6 +418,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
       }
+      // completes when every MMA issued above has completed; the TMEM release waits for it
+      tc_commit(mma_done);
     } else if (warp >= 2 && kConv) {
       // ------------------------------ int4 -> int8 converters ------------------------------
       // Three pairs of warps take this CTA's operand blocks round-robin: pair c converts blocks c, c + 3, c + 6, ...
@@ -787,6 +800,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   if (warp == 1) {
+    // no MMA still in flight writes the accumulators (on an abort the issuer may have left some behind)
+    mbar_wait_drain(mma_done, 0, 50000000ull);
+    tc_fence_after();
     __syncwarp();
     tmem_dealloc(tmem_base, 512);
   }

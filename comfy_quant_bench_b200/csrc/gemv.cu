@@ -61,17 +61,53 @@ __global__ void __launch_bounds__(gemv::kWarps * 32) gemv_affine_kernel(const Ge
   // nchunks is a multiple of 4, so the four lanes of a group are all inside the row or all past it.
   // one or two tokens: two iterations' weight loads in flight; more tokens need the registers
   constexpr int kUnroll = MT <= 2 ? 2 : 1;
+  // the group leaders' weight scales and zeros (raw bf16 bits) are loaded one iteration ahead, so no iteration
+  // waits for a dependent load after its shuffles
+  unsigned short s_next[R], z_next[R];
+  auto load_sz = [&](int c0, unsigned short (&sv)[R], unsigned short (&zv)[R]) {
+    const int c = c0 + lane;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      sv[r] = 0;
+      zv[r] = 0;
+      if (leader && c < nchunks && row_ok[r]) {
+        const int g = c >> 2, n = n0 + r;
+        sv[r] = __ldg(reinterpret_cast<const unsigned short*>(args.s) + static_cast<int64_t>(g) * args.N + n);
+        zv[r] = __ldg(reinterpret_cast<const unsigned short*>(args.zt) + static_cast<int64_t>(n) * args.zt_cols + g);
+      }
+    }
+  };
+  // the packed weights are loaded one iteration ahead as well
+  uint4 w_next[R];
+  auto load_w = [&](int c0, uint4 (&wv)[R]) {
+    const int c = c0 + lane;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      wv[r] = make_uint4(0, 0, 0, 0);
+      if (c < nchunks && row_ok[r])
+        wv[r] = __ldg(reinterpret_cast<const uint4*>(args.b + static_cast<int64_t>(n0 + r) * (K >> 1) +
+                                                     16 * static_cast<int64_t>(c)));
+    }
+  };
+  // Weights, scales and zeros are not written by the activation kernel this product follows: their first loads are
+  // issued before waiting for it (a programmatic launch of the fused linear), the activation codes only after.
+  load_w(0, w_next);
+  load_sz(0, s_next, z_next);
+  grid_dep_wait();
 #pragma unroll kUnroll
   for (int c0 = 0; c0 < nchunks; c0 += 32) {
     const int c = c0 + lane;
     const bool valid = c < nchunks;
+    unsigned short s_cur[R], z_cur[R];
     uint4 wq[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      wq[r] = make_uint4(0, 0, 0, 0);
-      if (valid && row_ok[r])
-        wq[r] = __ldg(reinterpret_cast<const uint4*>(args.b + static_cast<int64_t>(n0 + r) * (K >> 1) +
-                                                     16 * static_cast<int64_t>(c)));
+    for (int r = 0; r < R; ++r) { s_cur[r] = s_next[r]; z_cur[r] = z_next[r]; wq[r] = w_next[r]; }
+    // one or two tokens: the next iteration's weights in flight during this one (measured faster); more tokens
+    // need the registers, so their next weights are loaded after this iteration's products
+    constexpr bool kAhead = MT <= 2;
+    if (c0 + 32 < nchunks) {
+      if (kAhead) load_w(c0 + 32, w_next);
+      load_sz(c0 + 32, s_next, z_next);
     }
     int pm[R][MT], rm[MT];
 #pragma unroll
@@ -102,6 +138,7 @@ __global__ void __launch_bounds__(gemv::kWarps * 32) gemv_affine_kernel(const Ge
         }
       }
     }
+    if (!kAhead && c0 + 32 < nchunks) load_w(c0 + 32, w_next);
     // the four lanes of a group (chunks 4g .. 4g + 3 sit in lanes 4j .. 4j + 3) sum their chunks
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
@@ -114,13 +151,11 @@ __global__ void __launch_bounds__(gemv::kWarps * 32) gemv_affine_kernel(const Ge
       }
     }
     if (leader && valid) {
-      const int g = c >> 2;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         if (!row_ok[r]) continue;
-        const int n = n0 + r;
-        const float sg = __bfloat162float(args.s[static_cast<int64_t>(g) * args.N + n]);
-        const float zg = __bfloat162float(args.zt[static_cast<int64_t>(n) * args.zt_cols + g]);
+        const float sg = bf16_bits_to_f32(s_cur[r]);
+        const float zg = bf16_bits_to_f32(z_cur[r]);
 #pragma unroll
         for (int m = 0; m < MT; ++m)
           part[r][m] = __fmaf_rn(zg, __int2float_rn(rm[m]), __fmaf_rn(sg, __int2float_rn(pm[r][m]), part[r][m]));
@@ -144,17 +179,26 @@ __global__ void __launch_bounds__(gemv::kWarps * 32) gemv_affine_kernel(const Ge
 
 bool gemv_affine_fits(int M, int a_kperm) { return M >= 1 && M <= gemv::kMaxTokens && a_kperm != 0; }
 
+// pdl: launch as a programmatic dependent of the previous kernel in the stream (the fused linears, whose previous
+// kernel is their own activation kernel): the weight stream starts under that kernel's tail
 cudaError_t launch_gemv_affine(const int8_t* a, const float* sa, const void* b, const void* s, const void* zt,
-                               const void* bias, void* out, int M, int N, int K, cudaStream_t st) {
+                               const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl) {
   const GemvArgs g{a, sa, static_cast<const uint8_t*>(b), static_cast<const __nv_bfloat16*>(s),
                    static_cast<const __nv_bfloat16*>(zt), static_cast<const __nv_bfloat16*>(bias),
                    static_cast<__nv_bfloat16*>(out), M, N, K, rsplit_cols(K)};
   constexpr int kRowsPerCta = gemv::kWarps * gemv::kRowsPerWarp;
-  const dim3 grid(static_cast<unsigned>((N + kRowsPerCta - 1) / kRowsPerCta)), block(gemv::kWarps * 32);
-  if (M <= 1) gemv_affine_kernel<1><<<grid, block, 0, st>>>(g);
-  else if (M <= 2) gemv_affine_kernel<2><<<grid, block, 0, st>>>(g);
-  else if (M <= 4) gemv_affine_kernel<4><<<grid, block, 0, st>>>(g);
-  else gemv_affine_kernel<8><<<grid, block, 0, st>>>(g);
+  auto kern = M <= 1 ? gemv_affine_kernel<1> : M <= 2 ? gemv_affine_kernel<2> : M <= 4 ? gemv_affine_kernel<4>
+                                                                                          : gemv_affine_kernel<8>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>((N + kRowsPerCta - 1) / kRowsPerCta));
+  cfg.blockDim = dim3(gemv::kWarps * 32);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, kern, g) != cudaSuccess) return cudaErrorLaunchFailure;
   return cudaGetLastError();
 }
 

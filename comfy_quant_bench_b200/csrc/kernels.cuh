@@ -91,6 +91,9 @@ cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t s
 // per-group scales on both sides (policy 4): sag f32 [K/128, sag_ld], sbg f32 [K/128, N]; CTA-pair kernel
 int launch_gemm_group(const int8_t* a, int a_kperm, const float* sag, int64_t sag_ld, const void* b, const float* sbg,
                       const void* bias, void* out, int M, int N, int K, cudaStream_t st);
+// integer weight ratios per 64- or 128-wide group (policies 5/7/15/17): cw int32 or uint8 [K/cw_group, N]; CTA pair
+int launch_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const void* b, const float* sb, const void* cw,
+                         int cw_u8, int cw_group, const void* bias, void* out, int M, int N, int K, cudaStream_t st);
 // process-wide kernel choice for the packed-int4-weight GEMMs (cq_gemm_variant values)
 int set_gemm_variant(int variant);
 // failure-path self-test: two waits on mbarriers nothing arrives on; sites kSelftestSite and kSelftestSite + 1
@@ -99,6 +102,6 @@ cudaError_t launch_selftest_wait(cudaStream_t st);
 // small-M W4A8 affine product (M <= 8, K-permuted activations): one warp per weight row, read once
 bool gemv_affine_fits(int M, int a_kperm);
 cudaError_t launch_gemv_affine(const int8_t* a, const float* sa, const void* b, const void* s, const void* zt,
-                               const void* bias, void* out, int M, int N, int K, cudaStream_t st);
+                               const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl = false);
 
 }  // namespace cq

@@ -292,11 +292,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, c
     (``experiments/qwen21-kernel/kernels/g64_gemm6.cu:383-411``), for the policies built here:
 
     * pol 0: row x column, sa [M] f32, sb [N] f32;
-    * pol 4: g128 x g128, sa [K/128, M_pad] f32 (the per-group quantizer's layout), sb [K/128, N] f32.
+    * pol 4: g128 x g128, sa [K/128, M_pad] f32 (the per-group quantizer's layout), sb [K/128, N] f32;
+    * pol 5 / 7: integer weight ratios cw int32 [K/64, N] / [K/128, N] summed in int32, sa [M], sb [N] f32;
+    * pol 15 / 17: the same with cw uint8.
 
-    a packed int4 [M_pad, K/2]; b packed int4 [N, K/2]; bias bf16 [N] or empty; returns bf16 [M_pad, N].  ``ca``,
-    ``cw`` (the integer-ratio policies' operands) and ``cfg`` (the reference's tile configuration) are accepted and
-    not used: the integer-ratio policies 5/7/15/17 are not built and raise."""
+    a packed int4 [M_pad, K/2]; b packed int4 [N, K/2]; bias bf16 [N] or empty; returns bf16 [M_pad, N].  ``ca``
+    and ``cfg`` (the reference's tile configuration) are accepted and not used."""
     dev = _require_cuda(a, b, sa, sb)
     if bias is not None and bias.numel() == 0:
         bias = None
@@ -307,7 +308,27 @@ def gemm(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, c
         return gemm_rowcol(a8, sa.reshape(-1), b.contiguous(), sb.reshape(-1), bias)
     if pol == 4:
         return gemm_groupwise(a8, sa, b.contiguous(), sb, bias)
-    raise ValueError(f"policy {pol} is not built (0 and 4 are)")
+    if pol in (5, 7, 15, 17):
+        return gemm_intratio(a8, sa.reshape(-1), b.contiguous(), sb.reshape(-1), cw, 64 if pol % 10 == 5 else 128, bias)
+    raise ValueError(f"policy {pol} is not built (0, 4, 5, 7, 15, 17 are)")
+
+
+def gemm_intratio(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, cw: torch.Tensor, group: int,
+                  bias=None, *, a_kperm: bool = False) -> torch.Tensor:
+    """Integer weight ratios per group (the reference's policies 5/7/15/17, ``cq_gemm_intratio``): a int8-held int4
+    codes [M, K], b packed int4 [N, K/2], sa [M], sb [N] f32, cw int32 or uint8 [K/group, N]."""
+    dev = _require_cuda(a, sa, b, sb, cw, bias)
+    m, k = a.shape
+    n = b.shape[0]
+    if cw.dtype not in (torch.int32, torch.uint8) or tuple(cw.shape) != (k // group, n) or not cw.is_contiguous():
+        raise ValueError(f"cw (K/G, N): int32 (pol 5/7) or uint8 (15/17), [{k // group}, {n}]")
+    if sa.numel() != m or sb.numel() != n:
+        raise ValueError("per-row scales sa (M,), sb (N,)")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    _lib.call("cq_gemm_intratio", _ptr(a), int(bool(a_kperm)), _ptr(sa.float().contiguous()), _ptr(b),
+              _ptr(sb.float().contiguous()), _ptr(cw), int(cw.dtype == torch.uint8), int(group), _ptr(_bias_bf16(bias)),
+              _ptr(out), m, n, k, _stream(dev))
+    return out
 
 
 def w4a4_groupwise_linear(x: torch.Tensor, qweight: torch.Tensor, sb_g: torch.Tensor, bias=None,

@@ -200,6 +200,22 @@ CQ_API int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, in
                              void* stream);
 
 /*
+ * Integer weight ratios per group: the reference GEMM's policies 5, 7, 15 and 17
+ * (experiments/qwen21-kernel/kernels/g64_gemm6.cu:8-11, 93-343; called as g64_gemm6.gemm(a, b, sa, sb, ca, cw, bias,
+ * pol, cfg), g64_gemm6.cu:383-411):
+ *   acc[m, n] = sum_g cw[g, n] * sum_{k in group g} a[m, k] * b[n, k]     (int32, exact)
+ *   out[m, n] = bf16( float(acc) * sa[m] * sb[n] + bias[n] )
+ *   a        int4 values held as int8 [M, K] (a_kperm as for cq_gemm_rowcol);  b_packed packed signed int4 [N, K/2]
+ *   sa       f32 [M];  sb f32 [N] (the reference passes the row scale / 255)
+ *   cw       [K/cw_group, N] int32 (policies 5, 7) or, with cw_u8 = 1, uint8 (15, 17); values in [1, 255]
+ *   cw_group 64 (policies 5, 15) or 128 (7, 17)
+ * K < 171840 (the reference's bound on the int32 accumulator).  Runs the CTA-pair GEMM.
+ */
+CQ_API int cq_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const void* b_packed, const float* sb,
+                            const void* cw, int cw_u8, int cw_group, const void* bias, void* out, int64_t M, int64_t N,
+                            int64_t K, void* stream);
+
+/*
  * W4A8 affine linear, the headline GEMM:
  *   out[m, n] = bf16( sa[m] * sum_g ( s[g,n] * sum_{k in g} a[m,k]*(q[n,k]-8) + z[g,n] * gsum[g,m] ) + bias[n] )
  * with q the awq_w4a16 uint4 codes (packed [N, K/2]), s bf16 [K/group, N] and the zeros z passed as zt, the

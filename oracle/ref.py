@@ -367,6 +367,30 @@ def linear_groupwise(qa, sa_g, qw, sw_g, bias=None, group: int = 128) -> np.ndar
     return out
 
 
+def intratio_acc(qa, qw, cw, group: int) -> np.ndarray:
+    """Integer weight ratios per group (policies 5/7/15/17, ``g64_gemm6.cu:8-11``; ``g64_bench6.py:62-67``):
+    acc[m, n] = sum_g cw[g, n] * sum_{k in g} qa[m, k] * qw[n, k], exact (int64)."""
+    qa = np.asarray(qa, np.int64)
+    qw = np.asarray(qw, np.int64)
+    cw = np.asarray(cw, np.int64)
+    m, k = qa.shape
+    acc = np.zeros((m, qw.shape[0]), np.int64)
+    for g in range(k // group):
+        sl = slice(g * group, (g + 1) * group)
+        acc += (qa[:, sl] @ qw[:, sl].T) * cw[g][None, :]
+    return acc
+
+
+def linear_intratio(qa, sa, qw, sb, cw, group: int, bias=None) -> np.ndarray:
+    """The policies' output in the reference kernel's fp32 order (``g64_gemm6.cu:306-330``): t = fp32(fp32(acc) * sa[m]),
+    then t * sb[n] + bias[n] with one rounding (a fused multiply-add), as float32 values."""
+    acc = intratio_acc(qa, qw, cw, group)
+    t = (acc.astype(np.float32) * np.asarray(sa, np.float32).reshape(-1, 1)).astype(np.float32)
+    b = np.zeros(acc.shape[1], np.float64) if bias is None else np.asarray(bias, np.float64)
+    return (t.astype(np.float64) * np.asarray(sb, np.float32).astype(np.float64).reshape(1, -1) + b.reshape(1, -1)
+            ).astype(np.float32)
+
+
 def dequant_matmul(x_deq: np.ndarray, w_deq: np.ndarray, bias=None) -> np.ndarray:
     """F.linear in float64 of already-dequantized operands (the reference's dequantize-and-matmul path)."""
     out = np.asarray(x_deq, np.float64) @ np.asarray(w_deq, np.float64).T

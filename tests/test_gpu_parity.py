@@ -652,6 +652,70 @@ def test_groupwise_gemm_vs_oracle_with_reference_acceptance(ops, m, n, k):
     _check_status()
 
 
+# ----------------------------------------------------------------------------------------------
+# integer weight ratios per group (the reference GEMM's policies 5 / 7 / 15 / 17)
+# ----------------------------------------------------------------------------------------------
+
+def _intratio_case(m, n, k, group, seed):
+    rng = np.random.default_rng(seed)
+    a = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
+    b = rng.integers(-7, 8, size=(n, k)).astype(np.int8)
+    sa = rng.uniform(0.005, 0.015, size=m).astype(np.float32)
+    sb = (rng.uniform(0.005, 0.015, size=n) / 255).astype(np.float32)
+    cw = rng.integers(1, 256, size=(k // group, n)).astype(np.int32)
+    bias = ref.synth_bias(n, seed=seed + 1)
+    return a, b, sa, sb, cw, bias
+
+
+@pytest.mark.parametrize("pol,m,n,k", [(7, 4096, 4096, 4096), (5, 4096, 4096, 4096), (7, 512, 768, 12288),
+                                       (5, 300, 512, 12288), (7, 77, 256, 1024)])
+def test_intratio_gemm_vs_oracle_with_reference_acceptance(ops, pol, m, n, k):
+    """Policies 5 (g64) and 7 (g128), through the reference's interface ops.gemm (packed activations): the int32 sum
+    of P_g * cw[g, n] is exact, and the output follows the reference kernel's fp32 order, so it equals the oracle's
+    fp32 emulation of that order up to a rounding tie (<= 1e-4 of the outputs one bf16 step away); the reference
+    bench's acceptance rule on the first and last 256 rows; the uint8-ratio policies (15 / 17) bit-identical to
+    5 / 7; two runs bit-identical.  K = 12288 takes the path that shifts each group's sum before the ratio."""
+    group = 64 if pol == 5 else 128
+    a, b, sa, sb, cw, bias = _intratio_case(m, n, k, group, seed=m + n + k + pol)
+    ap = torch.from_numpy(ref.pack_int4(a)).cuda()
+    bp = torch.from_numpy(ref.pack_int4(b)).cuda()
+    sa_t, sb_t, cw_t = torch.from_numpy(sa).cuda(), torch.from_numpy(sb).cuda(), torch.from_numpy(cw).cuda()
+    y1 = ops.gemm(ap, bp, sa_t, sb_t, None, cw_t, bf16_dev(bias), pol=pol)
+    y2 = ops.gemm(ap, bp, sa_t, sb_t, None, cw_t, bf16_dev(bias), pol=pol)
+    y8 = ops.gemm(ap, bp, sa_t, sb_t, None, cw_t.to(torch.uint8), bf16_dev(bias), pol=pol + 10)
+    assert torch.equal(y1, y2) and torch.equal(y1, y8)
+    rows = np.r_[0:min(256, m), max(0, m - 256):m]
+    want32 = ref.linear_intratio(a[rows], sa[rows], b, sb, cw, group, ref.bf16_bits_to_f32(bias))
+    got = y1[torch.from_numpy(rows).cuda()]
+    gb = bits_of(got)
+    wb = ref.f32_to_bf16_bits(want32)
+    d = np.abs(gb.astype(np.int32) - wb.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() <= 1e-4, ((d > 0).mean(), d.max())
+    want = ref.intratio_acc(a[rows], b, cw, group).astype(np.float64) * sa[rows, None] * sb[None, :] + \
+        ref.bf16_bits_to_f32(bias)[None, :]
+    gv = f32_of(got).astype(np.float64)
+    half = len(rows) // 2
+    for sl in (slice(0, half), slice(half, len(rows))):
+        dd = gv[sl] - want[sl]
+        assert np.linalg.norm(dd) / np.linalg.norm(want[sl]) < 3e-3
+        assert np.abs(dd).max() / want[sl].std() < 0.04
+    _check_status()
+
+
+def test_intratio_gemm_rejects_bad_arguments(ops):
+    from comfy_quant_bench_b200 import _lib
+    a = torch.zeros(256, 512, dtype=torch.int8, device="cuda")
+    b = torch.zeros(256, 256, dtype=torch.int8, device="cuda")
+    s = torch.ones(256, device="cuda")
+    with pytest.raises(ValueError):      # ratios of the wrong shape
+        ops.gemm_intratio(a, s, b, s, torch.ones(3, 256, dtype=torch.int32, device="cuda"), 128)
+    with pytest.raises(ValueError):      # ratios of the wrong type
+        ops.gemm_intratio(a, s, b, s, torch.ones(4, 256, dtype=torch.int16, device="cuda"), 128)
+    with pytest.raises(_lib.CQShapeError):
+        ops.gemm_intratio(a, s, b, s, torch.ones(16, 256, dtype=torch.int32, device="cuda"), 32)   # group 32
+    _check_status()
+
+
 @pytest.mark.parametrize("swiglu", [False, True])
 def test_groupwise_linear_matches_the_node_path(ops, swiglu):
     """The node's policy-4 forward: per-group quantizer (ConvRot-256, g128, bf16-up scales), then the GEMM, against

@@ -97,3 +97,25 @@ def test_cpu_baseline_call_computes_the_affine_linear(rot):
     want = ref.linear_affine(qx.numpy().astype(np.int64), sx.numpy(), q, s, z, bias, 128)
     assert ref.rel_l2(want, got) < 1e-5
     assert len(timings) == 1 and all(t >= 0 for t in timings[0])
+
+
+def test_intratio_oracle_is_the_per_element_sum():
+    """Policies 5/7 (g64_gemm6.cu:8-11): acc[m, n] = sum_g cw[g, n] * sum_{k in g} a[m, k] * b[n, k], summed
+    element by element for a tiny case; the fp32 output order of the reference kernel on top of it."""
+    import numpy as np
+    from oracle import ref
+    rng = np.random.default_rng(0)
+    m, n, k, g = 3, 4, 256, 64
+    a = rng.integers(-7, 8, size=(m, k))
+    b = rng.integers(-7, 8, size=(n, k))
+    cw = rng.integers(1, 256, size=(k // g, n))
+    acc = ref.intratio_acc(a, b, cw, g)
+    for i in range(m):
+        for j in range(n):
+            want = sum(int(cw[kk // g, j]) * int(a[i, kk]) * int(b[j, kk]) for kk in range(k))
+            assert acc[i, j] == want
+    sa = np.full(m, 0.01, np.float32)
+    sb = np.full(n, 0.02 / 255, np.float32)
+    out = ref.linear_intratio(a, sa, b, sb, cw, g)
+    assert out.dtype == np.float32
+    assert np.allclose(out, acc * 0.01 * (0.02 / 255), rtol=1e-6)
