@@ -397,6 +397,23 @@ __device__ __forceinline__ void sts_bf16_pair(uint32_t a0, uint32_t a1, float v0
       ::"r"(a0), "r"(a1), "f"(v0), "f"(v1) : "memory");
 }
 
+// The gated residual of two tokens of one output column, in packed bf16: o_i = bf16(r_i + g * bf16(v_i)) with one
+// rounding of the exact value (fma.rn.bf16x2); r0, r1 are the residuals' bf16 bits, gate2 the gate's bits in both
+// halves.  Against torch's addcmul on bf16 tensors (an fp32 result rounded to bf16) it can differ only where the fp32
+// rounding lands on a bf16 rounding tie, about one output in 2^16.  -> shared addresses a0, a1.
+__device__ __forceinline__ void sts_gated_pair(uint32_t a0, uint32_t a1, float v0, float v1, uint32_t gate2, uint32_t r0,
+                                               uint32_t r1) {
+  asm volatile(
+      "{\n\t.reg .b32 y, r, o;\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.bf16x2.f32 y, %3, %2;\n\t"
+      "prmt.b32 r, %5, %6, 0x5410;\n\t"
+      "fma.rn.bf16x2 o, %4, y, r;\n\t"
+      "mov.b32 {lo, hi}, o;\n\t"
+      "st.shared.b16 [%0], lo;\n\t"
+      "st.shared.b16 [%1], hi;\n\t}"
+      ::"r"(a0), "r"(a1), "f"(v0), "f"(v1), "r"(gate2), "r"(r0), "r"(r1) : "memory");
+}
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
 // Smallest bf16 value >= v for v > 0 (mantissa rounded up), as the reference's per-group quantizer does.

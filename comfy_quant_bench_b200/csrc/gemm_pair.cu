@@ -472,9 +472,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
               // |P| < 2^22, so the int32 -> fp32 conversion is exact
               const float2 p = make_float2(__int2float_rn(static_cast<int>(r[2 * j])), __int2float_rn(static_cast<int>(r[2 * j + 1])));
               if constexpr (EPI == EPI_GROUP) {
-                // the reference's order: t = P * s_w rounded once, then acc += t * s_a[token] with one rounding
-                const float2 t = ffma2(s2, p, make_float2(0.0f, 0.0f));
-                const float2 a = *reinterpret_cast<const float2*>(sg_tok + 32 * ch + 2 * j);
+                // the reference's order: t = P * s_w rounded once, then acc += t * s_a[token] with one rounding; the
+                // tokens' group scales are read four at a time (one 16-byte shared load per two steps)
+                const float4 a4 = *reinterpret_cast<const float4*>(sg_tok + 32 * ch + 4 * (j >> 1));
+                const float2 a = (j & 1) ? make_float2(a4.z, a4.w) : make_float2(a4.x, a4.y);
+                const float2 t = fmul2(s2, p);
                 acc[16 * ch + j] = ffma2(t, a, acc[16 * ch + j]);
               } else {
                 acc[16 * ch + j] = ffma2(s2, p, acc[16 * ch + j]);
@@ -553,7 +555,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
               uint32_t rres[kOp == OUT_GATED ? 64 : 1];
               // the column's gate, loaded here rather than with the bias so that no register holds it across the
               // tile's group drains
-              const float gate = (kOp == OUT_GATED && n_ok) ? __bfloat162float(args.gate[n]) : 0.0f;
+              const uint32_t gate_bits =
+                  (kOp == OUT_GATED && n_ok) ? static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(args.gate) + n)) : 0u;
+              const uint32_t gate2 = gate_bits | (gate_bits << 16);
               const unsigned short* rp = nullptr;
               int rows_left = 0;
               if constexpr (kOp == OUT_GATED) {
@@ -578,12 +582,19 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
                 const float4 c2 = sa4[j4 + 2 < 16 ? j4 + 2 : 15];
                 const int t = 64 * pass + 4 * j4;
                 const int r = kOp == OUT_GATED ? 4 * j4 : 0;
-                const float v0 = out_apply<kOp>(__fmaf_rn(acc[t / 2].x, c0.x, bias), gate, rres[r]);
-                const float v1 = out_apply<kOp>(__fmaf_rn(acc[t / 2].y, c0.y, bias), gate, rres[r + (kOp == OUT_GATED)]);
-                const float v2 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].x, c0.z, bias), gate, rres[r + 2 * (kOp == OUT_GATED)]);
-                const float v3 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].y, c0.w, bias), gate, rres[r + 3 * (kOp == OUT_GATED)]);
-                sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v0, v1);
-                sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v2, v3);
+                // the linear's fp32 outputs of tokens t..t+3, two per packed fma (the same roundings as scalar fmas)
+                const float2 u01 = ffma2(acc[t / 2], make_float2(c0.x, c0.y), make_float2(bias, bias));
+                const float2 u23 = ffma2(acc[t / 2 + 1], make_float2(c0.z, c0.w), make_float2(bias, bias));
+                if constexpr (kOp == OUT_GATED) {
+                  sts_gated_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, u01.x, u01.y, gate2,
+                                 rres[r], rres[r + 1]);
+                  sts_gated_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, u23.x, u23.y, gate2,
+                                 rres[r + 2], rres[r + 3]);
+                } else {
+                  const float2 v01 = out_apply2<kOp>(u01), v23 = out_apply2<kOp>(u23);
+                  sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v01.x, v01.y);
+                  sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v23.x, v23.y);
+                }
                 c0 = c1;
                 c1 = c2;
               }

@@ -119,35 +119,6 @@ enum : int { OUT_PLAIN = 0, OUT_GELU = 1, OUT_GATED = 2 };
 constexpr int kResBatch = 8;   // gated residual: rows per batch of residual loads
 constexpr int kResAhead = 2;   //   batches in flight ahead of the one in use
 
-// gelu_tanh(y) = 0.5 y (1 + tanh(u)) with u = sqrt(2/pi) (y + 0.044715 y^3), written in its logistic form
-// y / (1 + 2^(-y (kA + kB y^2))), kA = 2 sqrt(2/pi) log2(e), kB = 0.044715 kA: no cancellation near 1 + tanh(u) = 0.
-// The hardware base-2 exponential and reciprocal (two special-function ops, eight instructions per element; for
-// large negative y the exponential overflows to inf and the reciprocal gives 0).  A variant that replaced the
-// reciprocal by Newton steps on the FMA pipe measured slower: the store pass is bound by instruction issue of the
-// epilogue warps, not by the special-function unit.
-__device__ __forceinline__ float gelu_tanh(float y) {
-  float e, r;
-  const float t = -y * __fmaf_rn(0.10294324f, y * y, 2.3022082f);
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
-  return y * r;
-}
-
-// One result through the output operation: v is the fp32 linear output (bias included) and y = bf16(v) the value
-// the plain epilogue stores; res_bits is the bf16 residual element (OUT_GATED).  The caller rounds the return
-// value to bf16.
-template <int OP>
-__device__ __forceinline__ float out_apply(float v, float gate, uint32_t res_bits) {
-  if constexpr (OP == OUT_PLAIN) {
-    return v;
-  } else {
-    const float y = bf16_round(v);
-    if constexpr (OP == OUT_GELU) return gelu_tanh(y);
-    else return __fmaf_rn(gate, y, bf16_bits_to_f32(res_bits));
-  }
-}
-
-
 __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
 }
@@ -165,6 +136,59 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
   return d;
+}
+
+// d = a * b on two fp32 lanes at once
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// d = a + b on two fp32 lanes at once
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// The output operation (plain or GELU) on two fp32 linear outputs u (bias included) of one column; the caller
+// rounds the results to bf16.  GELU acts on y = bf16(u), the value the plain epilogue stores:
+//   gelu_tanh(y) = 0.5 y (1 + tanh(w)), w = sqrt(2/pi) (y + 0.044715 y^3), in its logistic form
+//   y / (1 + 2^(-y (kA + kB y^2))), kA = 2 sqrt(2/pi) log2(e), kB = 0.044715 kA,
+// which has no cancellation near 1 + tanh(w) = 0; the hardware base-2 exponential and reciprocal (for large
+// negative y the exponential overflows to inf and the reciprocal gives 0).  The fp32 arithmetic runs in packed f32x2
+// instructions: the store pass is bound by the epilogue warps' instruction issue (a variant that replaced the
+// reciprocal by Newton steps on the FMA pipe measured slower, and so did the scalar form of this one).
+template <int OP>
+__device__ __forceinline__ float2 out_apply2(float2 u) {
+  if constexpr (OP == OUT_PLAIN) {
+    return u;
+  } else {
+    uint32_t b;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(u.y), "f"(u.x));
+    const float2 y = make_float2(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
+    // t = -y (kA + kB y^2) with the constants negated, then y / (1 + 2^t)
+    const float2 p = ffma2(make_float2(-0.10294324f, -0.10294324f), fmul2(y, y), make_float2(-2.3022082f, -2.3022082f));
+    const float2 t = fmul2(y, p);
+    float2 e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(t.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(t.y));
+    const float2 d = fadd2(e, make_float2(1.0f, 1.0f));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
+    return fmul2(y, r);
+  }
 }
 
 // Tile order.  Tiles are visited in groups of up to kRasterGroup token tiles: inside a group the token tile varies
@@ -642,7 +666,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
               uint32_t rres[kOp == OUT_GATED ? 64 : 1];
               // the column's gate, loaded here rather than with the bias so that no register holds it across the
               // tile's group drains
-              const float gate = (kOp == OUT_GATED && n_ok) ? __bfloat162float(args.gate[n]) : 0.0f;
+              const uint32_t gate_bits =
+                  (kOp == OUT_GATED && n_ok) ? static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(args.gate) + n)) : 0u;
+              const uint32_t gate2 = gate_bits | (gate_bits << 16);
               const unsigned short* rp = nullptr;
               int rows_left = 0;
               if constexpr (kOp == OUT_GATED) {
@@ -667,12 +693,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
                 const int t = 64 * pass + 4 * j4;
                 const int r = kOp == OUT_GATED ? 4 * j4 : 0;
                 const float4 c = *reinterpret_cast<const float4*>(sa_stage + t);
-                const float v0 = out_apply<kOp>(__fmaf_rn(acc[t / 2].x, c.x, bias), gate, rres[r]);
-                const float v1 = out_apply<kOp>(__fmaf_rn(acc[t / 2].y, c.y, bias), gate, rres[r + (kOp == OUT_GATED)]);
-                const float v2 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].x, c.z, bias), gate, rres[r + 2 * (kOp == OUT_GATED)]);
-                const float v3 = out_apply<kOp>(__fmaf_rn(acc[t / 2 + 1].y, c.w, bias), gate, rres[r + 3 * (kOp == OUT_GATED)]);
-                sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v0, v1);
-                sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v2, v3);
+                // the linear's fp32 outputs of tokens t..t+3, two per packed fma (the same roundings as scalar fmas)
+                const float2 u01 = ffma2(acc[t / 2], make_float2(c.x, c.y), make_float2(bias, bias));
+                const float2 u23 = ffma2(acc[t / 2 + 1], make_float2(c.z, c.w), make_float2(bias, bias));
+                if constexpr (kOp == OUT_GATED) {
+                  sts_gated_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, u01.x, u01.y, gate2,
+                                 rres[r], rres[r + 1]);
+                  sts_gated_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, u23.x, u23.y, gate2,
+                                 rres[r + 2], rres[r + 3]);
+                } else {
+                  const float2 v01 = out_apply2<kOp>(u01), v23 = out_apply2<kOp>(u23);
+                  sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v01.x, v01.y);
+                  sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v23.x, v23.y);
+                }
               }
               fence_proxy_async_smem();
               __syncwarp();

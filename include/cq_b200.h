@@ -244,7 +244,9 @@ CQ_API int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const v
  *                           (torch F.gelu(y, approximate="tanh"), the MLP-up activation; the sigmoid form of
  *                           0.5 y (1 + tanh(u)), within a few fp32 ulp of torch's value before the bf16 rounding)
  *   CQ_OUT_GATED_RESIDUAL   out = bf16(residual + gate[n] * y)  (torch.addcmul(residual, gate, y), the gated residual
- *                           after the attention-output and MLP-down linears; one fused multiply-add in fp32)
+ *                           after the attention-output and MLP-down linears; one bf16 fused multiply-add, which
+ *                           rounds the exact value once: torch's fp32-then-bf16 rounding can differ from it only
+ *                           where the fp32 value is a bf16 rounding tie, about one output in 2^16, by one step)
  * residual: bf16 [M, residual_ld] (residual_ld >= N); it may be the output buffer itself (same pointer, same row
  * stride: each element is read before it is overwritten) but must not overlap it otherwise.  gate: bf16 [N].
  * The operations other than CQ_OUT_PLAIN need N % 8 == 0 and a 16-byte aligned output.

@@ -178,9 +178,11 @@ def test_gelu_output_matches_torch_gelu_of_the_linear(ops, gemm_variant, m, n, k
 
 @pytest.mark.parametrize("m,n,k", _OP_SHAPES)
 def test_gated_residual_output_matches_addcmul(ops, gemm_variant, m, n, k):
-    """out = bf16(residual + gate * y): torch.addcmul(residual, gate, y) on the plain linear's bf16 output, the
-    same fp32 fused multiply-add, so bit for bit; also in place (out is the residual) and with a residual whose rows
-    are strided (a column slice of a wider tensor)."""
+    """out = bf16(residual + gate * y): torch.addcmul(residual, gate, y) on the plain linear's bf16 output.  The
+    epilogue rounds the exact value once (packed bf16 fused multiply-add) where torch rounds an fp32 result to bf16,
+    so the two differ only where that fp32 value lands on a bf16 rounding tie (about 2^-16 of the outputs, by one
+    step); also in place (out is the residual) and with a residual whose rows are strided (a column slice of a wider
+    tensor), both bit-identical to the plain call."""
     g = torch.Generator(device="cuda").manual_seed(m * 7 + n)
     x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
     qw, sc, z, zt, bias = _affine_layer(n, k, seed=n + 1)
@@ -197,9 +199,11 @@ def test_gated_residual_output_matches_addcmul(ops, gemm_variant, m, n, k):
     ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op="gated", residual=inplace, gate=gate, out=inplace,
                               convrot_groupsize=256)
     _status_clear()
-    assert torch.equal(got, want)
-    assert torch.equal(got_strided, want)
-    assert torch.equal(inplace, want)
+    g, w = got.float(), want.float()
+    assert bool(((g - w).abs() <= w.abs() * 2.0 ** -7 + 1e-30).all())
+    assert float((got != want).float().mean()) <= 1e-4
+    assert torch.equal(got_strided, got)
+    assert torch.equal(inplace, got)
 
 
 def test_lnmod_gelu_output_matches_composite(ops, gemm_variant):
