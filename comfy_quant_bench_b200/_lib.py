@@ -76,6 +76,7 @@ SIGNATURES = {
     "cq_gemm_affine": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_gemm_affine_op": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _opp, _vp, _i64, _i64, _i64, _int, _vp]),
     "cq_linear_workspace_bytes": (_i64, [_i64, _i64]),
+    "cq_linear_workspace_bytes_n": (_i64, [_i64, _i64, _i64]),
     "cq_linear_convrot_w4a4": (_int, [_vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "cq_linear_w4a8_affine": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64,
                                      _vp]),

@@ -306,7 +306,7 @@ int cq_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const void* 
   if (M == 0) return CQ_OK;
   if (K >= 171840) return CQ_ERR_SHAPE;          // the reference's int32 accumulator bound
   if (sa == nullptr || sb == nullptr || cw == nullptr) return CQ_ERR_ARG;
-  if (!aligned(cw, cw_u8 ? 1 : 4)) return CQ_ERR_ALIGN;
+  if (!aligned(cw, cw_u8 ? 1 : 4) || !aligned(sa, 4) || !aligned(sb, 4)) return CQ_ERR_ALIGN;
   if (int dv = check_device()) return dv;
   return cq::launch_gemm_intratio(a, a_kperm, sa, b_packed, sb, cw, cw_u8, cw_group, bias, out, static_cast<int>(M),
                                   static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream));
@@ -314,7 +314,7 @@ int cq_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const void* 
 
 static int gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                        const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
-                       int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl);
+                       int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl, float* partial = nullptr);
 
 int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                    const void* s_bf16, const void* zt_bf16, const void* bias, void* out, int64_t M, int64_t N,
@@ -350,7 +350,7 @@ int cq_gemm_affine_op(const int8_t* a, int a_kperm, const float* sa, const void*
 
 static int gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* gsplit, const void* b_packed,
                        const void* s_bf16, const void* zt_bf16, const void* bias, const cq_out_op* op, void* out,
-                       int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl) {
+                       int64_t M, int64_t N, int64_t K, int group, void* stream, bool pdl, float* partial) {
   if (group != 128) return CQ_ERR_ARG;
   if (a_kperm != 0 && a_kperm != 1) return CQ_ERR_ARG;
   if (int e = check_gemm(a, b_packed, out, M, N, K)) return e;
@@ -364,7 +364,7 @@ static int gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   if (op != nullptr) o = cq::OutOp{op->kind, op->residual, op->residual_ld, op->gate};
   return cq::launch_gemm_affine(a, a_kperm, sa, gsplit, b_packed, s_bf16, zt_bf16, bias, out, static_cast<int>(M),
                                 static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream), nullptr,
-                                0, 0, 0, &o, pdl);
+                                0, 0, 0, &o, pdl, partial);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -376,6 +376,27 @@ int64_t cq_linear_workspace_bytes(int64_t M, int64_t K) {
   if (M < 0 || K <= 0) return -1;
   const int64_t mp = ws_mpad(M);
   return round_up(mp * K, 256) + round_up(mp * 4, 256) + round_up(mp * cq_group_sum_cols(K) * 2, 256);
+}
+
+// room for the K-split partial sums of an affine GEMM with too few tiles to fill the SMs (0 when it does not split)
+static int64_t splitk_bytes(int64_t M, int64_t K, int64_t N) {
+  if (M <= 8 || M > kMaxRows || N <= 0 || N > kMaxRows || K < 128 || K % 128 != 0) return 0;
+  const int s = cq::affine_ksplit(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  return s > 1 ? round_up(static_cast<int64_t>(s) * M * N * 4, 256) : 0;
+}
+
+int64_t cq_linear_workspace_bytes_n(int64_t M, int64_t K, int64_t N) {
+  const int64_t base = cq_linear_workspace_bytes(M, K);
+  if (base < 0) return base;
+  return base + splitk_bytes(M, K, N);
+}
+
+// the partial-sum region of a workspace given with room for it, else null (the GEMM then runs unsplit)
+static float* splitk_region(void* ws, int64_t ws_bytes, int64_t M, int64_t K, int64_t N) {
+  const int64_t extra = splitk_bytes(M, K, N);
+  const int64_t base = cq_linear_workspace_bytes(M, K);
+  if (extra == 0 || ws_bytes < base + extra) return nullptr;
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + base);
 }
 
 struct Workspace {
@@ -495,7 +516,7 @@ int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N, int ro
                           stream))
     return e;
   return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, nullptr, out, M, N, K, group, stream,
-                     true);
+                     true, splitk_region(workspace, workspace_bytes, M, K, N));
 }
 
 int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
@@ -509,7 +530,7 @@ int cq_linear_w4a8_affine_lnmod(const void* x, int64_t M, int64_t K, int64_t N, 
                                 stream))
     return e;
   return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, nullptr, out, M, N, K, group, stream,
-                     true);
+                     true, splitk_region(workspace, workspace_bytes, M, K, N));
 }
 
 int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
@@ -526,7 +547,8 @@ int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_gr
                     : cq_rotquant(x, M, K, rot_group, 0, CQ_ACT_INT8_ROW, 0, w.mpad, CQ_Q_KPERM, w.xq, w.sx, w.gsplit,
                                   stream);
   if (e) return e;
-  return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, op, out, M, N, K, group, stream, true);
+  return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, op, out, M, N, K, group, stream, true,
+                     splitk_region(workspace, workspace_bytes, M, K, N));
 }
 
 int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,

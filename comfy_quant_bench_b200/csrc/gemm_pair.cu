@@ -900,6 +900,21 @@ int set_gemm_variant(int variant) {
 
 // The pair kernel's tile is 256 weight rows x 256 tokens: it pays off once there are enough tiles to fill the CTA pairs
 // (small problems keep the finer one-SM tiles, which also split a partial last wave into half tiles).
+static bool use_pair_kernel(int M, int N);
+
+// K splits for an affine GEMM on the one-SM kernel with too few tiles to fill the SMs (a DiT's text stream: one
+// 256-token tile): the largest S in {8, 6, 4, 3, 2} that divides the K blocks, leaves each split at least two of them
+// and keeps tiles x S within the SMs; 1 when the tiles already fill half the SMs
+int affine_ksplit(int M, int N, int K) {
+  const int tiles = ((M + 255) / 256) * ((N + 127) / 128);
+  const int kb = K / 128;
+  const int sms = num_sms();
+  if (sms <= 0 || 2 * tiles >= sms || N % 8 != 0 || use_pair_kernel(M, N)) return 1;
+  for (int s : {8, 6, 4, 3, 2})
+    if (kb % s == 0 && kb / s >= 2 && tiles * s <= sms) return s;
+  return 1;
+}
+
 static bool use_pair_kernel(int M, int N) {
   if (g_gemm_variant == CQ_GEMM_ONE_SM) return false;
   if (g_gemm_variant == CQ_GEMM_PAIR) return true;
@@ -943,7 +958,7 @@ int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, cons
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st, void* const* outs, int n_outs, int col0, int64_t ldo, const OutOp* op,
-                       bool pdl) {
+                       bool pdl, float* partial) {
   const bool plain = op == nullptr || op->kind == OUT_PLAIN;
   // a few tokens (adaLN modulation): read the weights once with a warp per row instead of 256-token MMA tiles
   // (plain outputs only: the output operations live in the GEMM's epilogue)
@@ -964,6 +979,14 @@ int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void
   g.bias = static_cast<const __nv_bfloat16*>(bias);
   g.out = static_cast<__nv_bfloat16*>(out);
   g.M = M; g.N = N; g.K = K;
+  // split K over more CTAs when the tiles leave most SMs idle, if the caller gave room for the partial sums
+  const bool res_pairs = plain || op->kind != OUT_GATED ||
+                         ((reinterpret_cast<uintptr_t>(op->res) & 3u) == 0 && op->res_ld % 2 == 0 &&
+                          (reinterpret_cast<uintptr_t>(op->gate) & 3u) == 0);   // the finalize reads pairs
+  if (partial != nullptr && outs == nullptr && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && res_pairs) {
+    g.ksplit = affine_ksplit(M, N, K);
+    g.partial = partial;
+  }
   const OutSpec spec{outs, n_outs, col0, ldo};
   const OutSpec* sp = outs != nullptr ? &spec : nullptr;
   auto launch = [&](auto op_c) {

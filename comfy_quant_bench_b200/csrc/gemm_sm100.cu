@@ -109,6 +109,9 @@ struct GemmArgs {
   const void* cw;        // intratio: integer weight ratios [K/cw_group, N], int32 or uint8
   int cw_u8;             // intratio: cw holds uint8 (policies 15/17) instead of int32 (5/7)
   int cw_group;          // intratio: 64 or 128 K columns per ratio
+  int ksplit;            // affine, one-SM kernel: K blocks of every tile split over this many CTAs (1: none); each
+                         // writes its fp32 partial sums to `partial`, and splitk_finalize_kernel adds them
+  float* partial;        // ksplit > 1: fp32 [ksplit, M, N] partial sums (zero-point term in split 0)
   int pdl;               // host: launch with programmatic stream serialization (the kernel's prologue - barrier
                          // set-up, TMEM allocation, descriptor prefetch - overlaps the tail of the previous kernel;
                          // every thread waits for that kernel's completion before its first read of any input)
@@ -281,12 +284,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   // and the extra control flow spills registers in the affine epilogue).
   constexpr bool kSplit = (EPI == EPI_ROWCOL);
   const int split = kSplit ? args.split : 0;
-  const int num_items = num_tiles + split;
+  // split K (affine, few tiles): item = tile * ksplit + r sums K blocks [r kps, (r + 1) kps) of the tile
+  const int ksplit = (EPI == EPI_AFFINE && args.ksplit > 1) ? args.ksplit : 1;
+  const int kps = kblocks / ksplit;
+  const int num_items = num_tiles * ksplit + split;
   auto coords = [&](int item, int& mt, int& nt, int& t0, int& width) {
     if constexpr (kSplit) {
       item_coords(item, num_tiles, split, m_tiles, n_tiles, mt, nt, t0, width);
     } else {
-      tile_coords(item, m_tiles, n_tiles, mt, nt);
+      tile_coords(item / ksplit, m_tiles, n_tiles, mt, nt);
       t0 = 0;
       width = kBT;
     }
@@ -341,18 +347,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         coords(item, mt, nt, t0, width);
         const int m0 = mt * kBT + t0;    // a half tile loads 256 rows from its first token; the MMA reads 128
         const int n0 = nt * kBW;
+        const int r_split = item % ksplit;
         if (EPI == EPI_AFFINE) {
-          // zero-point operand: the tokens' split group sums (bf16, 64 columns per block) into the X slot
+          // zero-point operand: the tokens' split group sums (bf16, 64 columns per block) into the X slot.  Only
+          // the first K split adds the zero-point term: the others load rows past M, which the copy fills with 0.
           for (int p = 0; p < args.nz; ++p) {
             if (!mbar_wait(&empty_tma[stage], phase ^ 1u, abort_flag, 10)) break;
             uint8_t* st = sm_tma + stage * P::kTmaStageBytes;
             mbar_arrive_expect_tx(&full_tma[stage], kXBytes);
-            tma_load_2d(st, &tm_r, &full_tma[stage], p * 128, m0);
+            tma_load_2d(st, &tm_r, &full_tma[stage], p * 128, r_split == 0 ? m0 : M);
             ++issued;
             if (++stage == kTmaStages) { stage = 0; phase ^= 1u; }
           }
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = r_split * kps; kb < (r_split + 1) * kps; ++kb) {
           if (!mbar_wait(&empty_tma[stage], phase ^ 1u, abort_flag, 1)) break;
           uint8_t* st = sm_tma + stage * P::kTmaStageBytes;
           mbar_arrive_expect_tx(&full_tma[stage], P::kTmaStageBytes);
@@ -406,7 +414,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (width != kBT) mbar_arrive_cnt(&tmem_empty[buf], 4);   // the idle second-half epilogue warps
           if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
-        for (int kb = 0; kb < kblocks && ok; ++kb) {
+        for (int kb = 0; kb < kps && ok; ++kb) {
           if (EPI == EPI_AFFINE) {
             if (!(ok = mbar_wait(&tmem_empty[buf], buf_phase, abort_flag, 3))) break;
             tc_fence_after();
@@ -452,7 +460,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       const int pair = (warp - 2) >> 1;               // 0..kConvStages-1: this pair's converter stage
       const int pt = threadIdx.x - 64 * (1 + pair);   // 0..63
       const int nzb = (EPI == EPI_AFFINE) ? args.nz : 0;
-      const int bpt = nzb + kblocks;                  // operand blocks per tile
+      const int bpt = nzb + kps;                      // operand blocks per item (tile, or K split of a tile)
       uint8_t* dst = sm_conv + pair * kWuBytes;
       // the thread's items are it = pt + 64 i (i = 0..7): row (pt >> 2) + 16 i, 16-byte column c4 = pt & 3.  Row
       // steps of 16 keep (row & 7), so both swizzled destination chunks sit at fixed offsets from the row start
@@ -526,7 +534,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       if (half * kWarpTok >= width) {
         // a half tile holds tokens for the first half's warps only; the MMA issuer arrives on this warp's behalf on
         // each of the item's accumulator buffers, so the warp only steps its buffer position past the item
-        const int uses = (EPI == EPI_AFFINE) ? 1 + kblocks : 1;
+        const int uses = (EPI == EPI_AFFINE) ? 1 + kps : 1;
         for (int u = 0; u < uses; ++u)
           if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         continue;
@@ -577,11 +585,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         }
         // the weight scale of the next group is loaded one group ahead as raw bf16 bits and converted only when it
         // is used, so its latency hides behind a drain instead of stalling the warp at the load
-        const unsigned short* ws_bits = reinterpret_cast<const unsigned short*>(args.ws) + n;
+        const int r_split = item % ksplit;
+        const unsigned short* ws_bits =
+            reinterpret_cast<const unsigned short*>(args.ws) + static_cast<int64_t>(r_split * kps) * N + n;
         unsigned short s_bits_next = n_ok ? __ldg(ws_bits) : static_cast<unsigned short>(0);
-        for (int g = 0; g < kblocks; ++g) {
+        for (int g = 0; g < kps; ++g) {
           const unsigned short s_bits = s_bits_next;
-          if (g + 1 < kblocks && n_ok) s_bits_next = __ldg(ws_bits + static_cast<int64_t>(g + 1) * N);
+          if (g + 1 < kps && n_ok) s_bits_next = __ldg(ws_bits + static_cast<int64_t>(g + 1) * N);
           if (!(ok = mbar_wait(&tmem_full[buf], buf_phase, abort_flag, 7))) break;
           tc_fence_after();
           const float s = bf16_bits_to_f32(s_bits) * wscale_fold;
@@ -629,6 +639,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           if (++buf == kNumBufs) { buf = 0; buf_phase ^= 1u; }
         }
         if (!ok) break;
+        if (ksplit > 1) {
+          // one K split of the tile: its fp32 sums (the zero-point term in split 0) into the partial array, 32
+          // consecutive columns per token row; splitk_finalize_kernel adds the splits in order and applies the token
+          // scale, the bias and the output operation
+          if (n_ok) {
+            float* prow = args.partial + (static_cast<int64_t>(r_split) * M + m0) * N + n;
+#pragma unroll
+            for (int j = 0; j < kWarpTok / 2; ++j) {
+              if (m_full || m0 + 2 * j < M) prow[static_cast<int64_t>(2 * j) * N] = acc[j].x;
+              if (m_full || m0 + 2 * j + 1 < M) prow[static_cast<int64_t>(2 * j + 1) * N] = acc[j].y;
+            }
+          }
+          continue;
+        }
         stage_sa();
         if (args.tma_out) {
           // two passes of 64 tokens: bf16 results into a staging buffer ([token][columns]), then one TMA tensor store
@@ -841,6 +865,50 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   }
 }
 
+// The K splits of the affine GEMM added up: out[m, n0..n0+7] = op(bf16(fma(sum_r partial[r, m, n], sa[m], bias[n])))
+// with the splits summed in order r = 0, 1, ... (deterministic), and the output operation as in the GEMM's epilogue.
+// One thread per 8 consecutive columns of a row (N % 8 == 0).
+template <int OP>
+__global__ void splitk_finalize_kernel(const GemmArgs args) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int N = args.N, M = args.M;
+  const int n8 = N / 8;
+  if (i >= static_cast<int64_t>(M) * n8) return;
+  const int m = static_cast<int>(i / n8), n0 = 8 * static_cast<int>(i % n8);
+  float v[8];
+  const float* p = args.partial + static_cast<int64_t>(m) * N + n0;
+  {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  for (int r = 1; r < args.ksplit; ++r) {
+    const float* q = p + static_cast<int64_t>(r) * M * N;
+    const float4 a = *reinterpret_cast<const float4*>(q), b = *reinterpret_cast<const float4*>(q + 4);
+    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  }
+  const float sa = args.sa[m];
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float b0 = args.bias != nullptr ? __bfloat162float(args.bias[n0 + 2 * k]) : 0.0f;
+    const float b1 = args.bias != nullptr ? __bfloat162float(args.bias[n0 + 2 * k + 1]) : 0.0f;
+    const float2 u = make_float2(__fmaf_rn(v[2 * k], sa, b0), __fmaf_rn(v[2 * k + 1], sa, b1));
+    if constexpr (OP == OUT_GATED) {
+      // one bf16x2 fused multiply-add: res + gate * bf16(u), as the epilogue's gated store
+      const uint32_t g2 = *reinterpret_cast<const uint32_t*>(args.gate + n0 + 2 * k);
+      const uint32_t r2 = *reinterpret_cast<const uint32_t*>(args.res + static_cast<int64_t>(m) * args.res_ld + n0 + 2 * k);
+      uint32_t y, o;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(y) : "f"(u.y), "f"(u.x));
+      asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(o) : "r"(g2), "r"(y), "r"(r2));
+      w[k] = o;
+    } else {
+      const float2 o = out_apply2<OP>(u);
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w[k]) : "f"(o.y), "f"(o.x));
+    }
+  }
+  *reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(m) * N + n0) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // Zt[n, j] = z[j mod G, n] for j < 2G, 0 for 2G <= j < cols (the affine GEMM's zero-point weight operand)
 __global__ void prep_zt_kernel(const __nv_bfloat16* __restrict__ z, __nv_bfloat16* __restrict__ zt, int N, int G,
                                int cols) {
@@ -923,6 +991,16 @@ static bool make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64
 
 static int g_num_sms = 0;
 
+// the current device's SM count (queried once)
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_num_sms;
+}
+
 // Output destinations of an affine launch: n buffers of [M, ldo] bf16, this launch's columns starting at col0.
 struct OutSpec {
   void* const* ptrs;
@@ -949,12 +1027,7 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     configured = true;
   }
   if (!regs_ok) return CQ_ERR_CUDA;
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) return CQ_ERR_CUDA;
-  }
+  if (num_sms() <= 0) return CQ_ERR_CUDA;
   CUtensorMap tm_x, tm_w, tm_r, tm_z;
   OutMaps tm_out;
   if (!make_map_u8(&tm_x, a, args.M, args.K, kBK, kBT, true)) return CQ_ERR_CUDA;
@@ -1002,7 +1075,8 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     else if (2 * (tiles % g_num_sms) <= g_num_sms) split = tiles % g_num_sms;
   }
   ga.split = split;
-  const int items = tiles + split;
+  if (EPI != EPI_AFFINE) ga.ksplit = 1;
+  const int items = tiles * (ga.ksplit > 1 ? ga.ksplit : 1) + split;
   const int grid = items < g_num_sms ? items : g_num_sms;
   if (grid == 0) return CQ_OK;
   if (ga.pdl) {
@@ -1019,6 +1093,10 @@ static int launch_gemm_t(const int8_t* a, const void* b, const void* rsplit, con
     if (cudaLaunchKernelEx(&cfg, kern, tm_x, tm_w, tm_r, tm_z, tm_out, ga) != cudaSuccess) return CQ_ERR_CUDA;
   } else {
     kern<<<grid, kThreads, smem_bytes, st>>>(tm_x, tm_w, tm_r, tm_z, tm_out, ga);
+  }
+  if (EPI == EPI_AFFINE && ga.ksplit > 1) {
+    const int64_t threads = static_cast<int64_t>(ga.M) * (ga.N / 8);
+    splitk_finalize_kernel<OP><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(ga);
   }
   return cudaGetLastError() == cudaSuccess ? CQ_OK : CQ_ERR_CUDA;
 }

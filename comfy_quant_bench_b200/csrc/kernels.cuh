@@ -86,7 +86,9 @@ struct OutOp {
 int launch_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const void* rsplit, const void* b,
                        const void* s, const void* zt, const void* bias, void* out, int M, int N, int K,
                        cudaStream_t st, void* const* outs = nullptr, int n_outs = 0, int col0 = 0, int64_t ldo = 0,
-                       const OutOp* op = nullptr, bool pdl = false);
+                       const OutOp* op = nullptr, bool pdl = false, float* partial = nullptr);
+// K splits the affine GEMM takes for a shape when given room for fp32 partial sums [S, M, N] (1: no split)
+int affine_ksplit(int M, int N, int K);
 cudaError_t launch_prep_zt(const void* z, int N, int K, void* zt, cudaStream_t st);
 // per-group scales on both sides (policy 4): sag f32 [K/128, sag_ld], sbg f32 [K/128, N]; CTA-pair kernel
 int launch_gemm_group(const int8_t* a, int a_kperm, const float* sag, int64_t sag_ld, const void* b, const float* sbg,

@@ -350,8 +350,11 @@ def w4a4_groupwise_linear(x: torch.Tensor, qweight: torch.Tensor, sb_g: torch.Te
     return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
-def _workspace(m: int, k: int, dev) -> torch.Tensor:
-    nbytes = int(_lib.load().cq_linear_workspace_bytes(m, k))
+def _workspace(m: int, k: int, dev, n: int | None = None) -> torch.Tensor:
+    """Scratch for a fused linear; with ``n`` (W4A8 affine linears) also room for the K-split partial sums the GEMM
+    takes when its tiles leave most SMs idle."""
+    lib = _lib.load()
+    nbytes = int(lib.cq_linear_workspace_bytes_n(m, k, n) if n is not None else lib.cq_linear_workspace_bytes(m, k))
     return torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
 
 
@@ -453,7 +456,7 @@ def w4a8_affine_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     x2 = _as2d(x)
     m = x2.shape[0]
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-    ws = _workspace(m, k, dev)
+    ws = _workspace(m, k, dev, n)
     wp, wn = _ws_ptr(ws)
     bias = _bias_bf16(bias)
     zt = zeros_prepared if zeros_prepared is not None else prepare_affine_zeros(zeros, group_size)
@@ -559,7 +562,7 @@ def w4a8_affine_linear_lnmod(x: torch.Tensor, shift: torch.Tensor, scale1p: torc
     x2 = _as2d(x)
     m = x2.shape[0]
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-    ws = _workspace(m, k, dev)
+    ws = _workspace(m, k, dev, n)
     wp, wn = _ws_ptr(ws)
     sh, sc = _vec_bf16(shift, k, "shift"), _vec_bf16(scale1p, k, "scale1p")
     _lib.call("cq_linear_w4a8_affine_lnmod", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc),
@@ -614,7 +617,7 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     elif out.dtype != torch.bfloat16 or out.numel() != m * n or not out.is_contiguous():
         raise ValueError(f"out must be contiguous bf16 with {m} x {n} elements")
-    ws = _workspace(m, k, dev)
+    ws = _workspace(m, k, dev, n)
     wp, wn = _ws_ptr(ws)
     sh = _vec_bf16(shift, k, "shift") if shift is not None else None
     sc = _vec_bf16(scale, k, "scale") if scale is not None else None

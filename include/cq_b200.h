@@ -283,6 +283,13 @@ CQ_API int cq_gemm_affine_op(const int8_t* a, int a_kperm, const float* sa, cons
  *   input_act) (tools/_native_probe.py:234-255).
  */
 CQ_API int64_t cq_linear_workspace_bytes(int64_t M, int64_t K);
+/* The workspace for the W4A8 affine linears (cq_linear_w4a8_affine, _lnmod, cq_linear_w4a8_op) of an N-output
+ * linear, with room for the K-split partial sums the GEMM uses when its tiles leave most SMs idle (few tokens, e.g.
+ * a DiT's 256-token text stream): fp32 [S, M, N] after the cq_linear_workspace_bytes(M, K) bytes, S <= 8 chosen by
+ * shape.  Given at least this much, those linears split K over more CTAs and add the S partial sums in a fixed
+ * order (deterministic) in a second kernel; given only cq_linear_workspace_bytes(M, K), they run unsplit.  The two
+ * results agree to fp32 rounding, not bit for bit. */
+CQ_API int64_t cq_linear_workspace_bytes_n(int64_t M, int64_t K, int64_t N);
 CQ_API int cq_linear_convrot_w4a4(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, int act_bits,
                            const void* qweight, const float* wscale, const void* bias, void* out, void* workspace,
                            int64_t workspace_bytes, void* stream);

@@ -249,3 +249,40 @@ def test_output_op_rejects_bad_arguments(ops):
                                         ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
     assert st == _lib.CQ_ERR_ARG
     _status_clear()
+
+
+# ----------------------------------------------------------------------------------------------
+# few-token-tile affine GEMMs split over K (a DiT's text stream: one 256-token tile)
+# ----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,n,k,out_op", [(256, 3072, 12288, "gated"), (256, 3072, 3072, "plain"), (300, 3072, 3072, "gelu"),
+                                          (256, 9216, 3072, "plain")])
+def test_split_k_linear_matches_the_unsplit_gemm(ops, m, n, k, out_op):
+    """With room for the partial sums (the workspace the ops allocate), the linear splits K over more CTAs and adds the
+    partial tiles in a fixed order: deterministic, equal to the unsplit GEMM (the standalone cq_gemm_affine on the
+    same codes) up to fp32 summation order (within one bf16 step, a small fraction off), and to the oracle-free
+    composite for the output operations."""
+    from comfy_quant_bench_b200 import _lib
+    lib = _lib.load()
+    assert lib.cq_linear_workspace_bytes_n(m, k, n) > lib.cq_linear_workspace_bytes(m, k)   # this shape splits
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    qw, sc, z, zt, bias = _affine_layer(n, k, seed=n + k)
+    res = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    gate = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
+    kw = {"residual": res, "gate": gate} if out_op == "gated" else {}
+    y1 = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op=out_op, convrot_groupsize=256, **kw)
+    y2 = ops.w4a8_affine_linear_op(x, qw, sc, zt, bias, out_op=out_op, convrot_groupsize=256, **kw)
+    q, s, gs = ops.rotquant(x, 256, _lib.CQ_ACT_INT8_ROW, m_pad=(m + 15) // 16 * 16, group_sums=True, kperm=True)
+    unsplit = ops.gemm_affine(q[:m], s[:m], gs, qw, sc, z, bias, a_kperm=True, zeros_prepared=zt)
+    if out_op == "gelu":
+        want = F.gelu(unsplit, approximate="tanh")
+    elif out_op == "gated":
+        want = torch.addcmul(res, gate, unsplit)
+    else:
+        want = unsplit
+    _status_clear()
+    assert torch.equal(y1, y2)
+    a, b = y1.float(), want.float()
+    assert bool(((a - b).abs() <= b.abs() * 2.0 ** -7 + 1e-6).all()), float(((a - b).abs() - b.abs() * 2.0 ** -7).max())
+    assert float((y1 != want).float().mean()) <= 0.02

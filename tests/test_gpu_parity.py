@@ -548,12 +548,16 @@ def test_w4a8_affine_linear_few_tokens_vs_oracle(ops, m, n, k):
                                             (130, 96, 1024, 32, 256), (77, 128, 512, 40, 256)])
 def test_affine_linear_into_several_buffers_at_an_offset(ops, gemm_variant, m, n, k, col0, ldo):
     """The column-parallel form writes this shard's columns into every output buffer at col0; the rest stays."""
+    from comfy_quant_bench_b200 import _lib
     x = bf16_dev(ref.synth_activations(m, k, seed=11))
     w = torch.from_numpy(ref.synth_weight(n, k, seed=12)).cuda()
     qw, s, z = ops.quantize_affine_w4_weight(w, 128, 256)
     zt = ops.prepare_affine_zeros(z, 128)
     bias = bf16_dev(ref.synth_bias(n, seed=13))
-    want = ops.w4a8_affine_linear(x, qw, s, z, bias, 128, 256, zeros_prepared=zt)
+    # the same codes through the unsplit GEMM (the fused linear may split K for this few-tile shape, which changes
+    # the fp32 summation order; the column-parallel form never splits)
+    q, sx, gs = ops.rotquant(x, 256, _lib.CQ_ACT_INT8_ROW, m_pad=(m + 15) // 16 * 16, group_sums=True, kperm=True)
+    want = ops.gemm_affine(q[:m], sx[:m], gs, qw, s, z, bias, a_kperm=True, zeros_prepared=zt)
     outs = [torch.full((m, ldo), 7.0, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
     ops.w4a8_affine_linear_into(x, qw, s, zt, bias, outs, col0, ldo, convrot_groupsize=256)
     torch.cuda.synchronize()
