@@ -86,8 +86,9 @@ int cq_linear_w4a8_affine_noalloc(const void* x, int64_t M, int64_t K, int64_t N
   if (need > cq::kNoallocScratchBytes) return CQ_ERR_CAPACITY;   // problem larger than the fixed scratch array
   void* scratch = nullptr;
   if (int e = cq::noalloc_scratch_ptr(&scratch)) return e;
-  return cq_linear_w4a8_affine(x, M, K, N, rot_group, swiglu, qweight, s_bf16, zt_bf16, group, bias, out, scratch,
-                               cq::kNoallocScratchBytes, stream);
+  // exactly the base workspace: the GEMM runs unsplit, as cq_linear_w4a8_affine does with that workspace
+  return cq_linear_w4a8_affine(x, M, K, N, rot_group, swiglu, qweight, s_bf16, zt_bf16, group, bias, out, scratch, need,
+                               stream);
 }
 
 }  // extern "C"

@@ -344,7 +344,8 @@ CQ_API int cq_linear_w4a8_affine_peers(const void* x, int64_t M, int64_t K, int6
  * CQ_ERR_CAPACITY.  All calls share the array: calls that overlap on the GPU race, so serialize them on one
  * stream.  The first call on each device looks up the array's device address, and so does the first call after
  * the device's context was reset (cudaDeviceReset); make those calls before any stream capture.  It calls no
- * cudaMalloc / cudaFree.
+ * cudaMalloc / cudaFree, and its GEMM never splits K (its results equal cq_linear_w4a8_affine's given the
+ * cq_linear_workspace_bytes(M, K) workspace).
  */
 CQ_API int cq_linear_w4a8_affine_noalloc(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu,
                                          const void* qweight, const void* s_bf16, const void* zt_bf16, int group,
