@@ -94,6 +94,8 @@ SIGNATURES = {
     "cq_rotquant_absmax": (_int, [_vp, _i64, _i64, _int, _i64, _vp, _vp]),
     "cq_rotquant_scaled": (_int, [_vp, _i64, _i64, _int, _vp, _i64, _int, _vp, _vp, _vp, _vp]),
     "cq_qkv_rmsnorm_rope": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "cq_qkv_rmsnorm_rope_layout": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _int,
+                                          _vp]),
     "cq_heads_to_rows": (_int, [_vp, _i64, _int, _int, _vp, _int, _i64, _i64, _vp]),
     "cq_gemm_rowcol_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "cq_linear_convrot_w4a4_swiglu": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),

@@ -175,6 +175,13 @@ int cq_rotquant_scaled(const void* x, int64_t M, int64_t K, int rot_group, const
 
 int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm, float eps,
                         const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0, void* stream) {
+  return cq_qkv_rmsnorm_rope_layout(y, S, H, D, q_norm, k_norm, eps, rope, q, k, v, s_all, s0, 0, stream);
+}
+
+int cq_qkv_rmsnorm_rope_layout(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm,
+                               float eps, const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0,
+                               int token_major, void* stream) {
+  if (token_major != 0 && token_major != 1) return CQ_ERR_ARG;
   if (S < 0 || S > kMaxRows || H < 1 || H > 4096 || (D != 64 && D != 128)) return CQ_ERR_SHAPE;
   if (s0 < 0 || s_all < s0 + S || s_all > kMaxRows) return CQ_ERR_SHAPE;
   if (!(eps >= 0.0f)) return CQ_ERR_ARG;
@@ -188,7 +195,8 @@ int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_no
   if (int dv = check_device()) return dv;
   cq::QkvRopeArgs a{static_cast<const __nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(q_norm),
                     static_cast<const __nv_bfloat16*>(k_norm), rope, static_cast<__nv_bfloat16*>(q),
-                    static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), S, s_all, s0, H, D, eps};
+                    static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), S, s_all, s0, H, D, eps,
+                    token_major ? static_cast<int64_t>(H) * D : D, token_major ? D : s_all * D};
   return cuda_status(cq::launch_qkv_rmsnorm_rope(a, static_cast<cudaStream_t>(stream)));
 }
 

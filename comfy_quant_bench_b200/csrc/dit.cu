@@ -3,7 +3,8 @@
 //
 // qkv_rmsnorm_rope_kernel: one token's QKV linear output y [3, H, D] (bf16) ->
 //   q = rope(rmsnorm(y[0]) * w_q), k = rope(rmsnorm(y[1]) * w_k), v = y[2], each written at token s0 + s of the
-//   joint attention layout [H, S_all, D] (batch 1).  RMSNorm per head in fp32 (x * rsqrt(mean(x^2) + eps) * w,
+//   joint attention layout, head-major [H, S_all, D] or token-major [S_all, H, D] (batch 1; the token-major form is
+//   the [tokens, hidden] layout an attention kernel given strided views reads and writes back in place).  RMSNorm per head in fp32 (x * rsqrt(mean(x^2) + eps) * w,
 //   rounded once to bf16, as torch's fused rms_norm does); the rotary rotation acts on interleaved pairs
 //   (x[2p], x[2p+1]) with (cos, sin) of the token's position, in fp32 on the bf16 normalized values, rounded to
 //   bf16.  It replaces, per stream and block, rms_norm + float copy + complex multiply + bf16 copy + the
@@ -21,8 +22,8 @@ __global__ void __launch_bounds__(256) qkv_rmsnorm_rope_kernel(const QkvRopeArgs
   const int part = blockIdx.y;                    // 0: q, 1: k, 2: v
   const int H = a.H;
   const __nv_bfloat16* src = a.y + (s * 3 + part) * static_cast<int64_t>(H) * D + lane * E;
-  __nv_bfloat16* dst = (part == 0 ? a.q : part == 1 ? a.k : a.v) + (a.s0 + s) * D + lane * E;
-  const int64_t head_stride = a.s_all * D;
+  __nv_bfloat16* dst = (part == 0 ? a.q : part == 1 ? a.k : a.v) + (a.s0 + s) * a.tok_stride + lane * E;
+  const int64_t head_stride = a.head_stride;
 
   float w[E], cs[E / 2], sn[E / 2];
   if (part < 2) {

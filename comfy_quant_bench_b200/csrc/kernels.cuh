@@ -43,12 +43,14 @@ struct QkvRopeArgs {
   const __nv_bfloat16* qw;    // [D] RMSNorm weight of q
   const __nv_bfloat16* kw;    // [D] RMSNorm weight of k
   const float* rope;          // [S, D/2, 2]: (cos, sin) of each token's position
-  __nv_bfloat16* q;           // [H, s_all, D]
+  __nv_bfloat16* q;           // [H, s_all, D] (head-major) or [s_all, H, D] (token-major)
   __nv_bfloat16* k;
   __nv_bfloat16* v;
   int64_t S, s_all, s0;       // tokens of this stream, tokens of the joint sequence, this stream's first token
   int H, D;
   float eps;
+  int64_t tok_stride;         // elements between tokens: D (head-major) or H*D (token-major)
+  int64_t head_stride;        // elements between heads: s_all*D (head-major) or D (token-major)
 };
 cudaError_t launch_qkv_rmsnorm_rope(const QkvRopeArgs& a, cudaStream_t st);
 

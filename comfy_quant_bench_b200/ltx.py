@@ -229,8 +229,11 @@ class LTXDiT:
         return self._bufs[name][0][: x.shape[0]]
 
     def _heads_local(self, o: torch.Tensor) -> torch.Tensor:
-        """o [1, H/P, S, D] -> this rank's heads as [S, H/P * D] rows (the row-parallel projections' input)."""
+        """o [1, H/P, S, D] -> this rank's heads as [S, H/P * D] rows (the row-parallel projections' input): a view
+        when o is token-major in memory (attention over token-major q), else a copy."""
         _, hp, s, d = o.shape
+        if o.transpose(1, 2).is_contiguous():
+            return o.transpose(1, 2).reshape(s, hp * d)
         a = torch.empty(s, hp * d, dtype=torch.bfloat16, device=o.device)
         ops.heads_to_rows(o, [a], 0, hp * d)
         return a
@@ -244,10 +247,12 @@ class LTXDiT:
         return self._step_gather(x, ctx)
 
     def _attn_inputs(self, s: int, device):
+        """q, k, v of this rank's heads as [1, H/P, S, D] views of token-major [1, S, H/P, D] memory, so that the
+        attention's output is token-major too and reaches the output projection as rows without a copy."""
         c = self.cfg
         hp = c.heads // self.world
-        q = torch.empty(1, hp, s, c.head_dim, dtype=torch.bfloat16, device=device)
-        return q, torch.empty_like(q), torch.empty_like(q)
+        return tuple(torch.empty(1, s, hp, c.head_dim, dtype=torch.bfloat16, device=device).transpose(1, 2)
+                     for _ in range(3))
 
     def _cross_attention(self, b, x, ctx, s: int):
         c = self.cfg

@@ -16,8 +16,9 @@ Attention is a torch op (scaled_dot_product_attention).  On the kernel path the 
 library's kernels: the layer norm + modulation before the QKV and MLP-up linears in the activation kernel
 (``ops.w4a8_affine_linear_lnmod`` / ``ops.w4a8_affine_linear_op``), the GELU after MLP-up and the two gated residuals
 in the GEMM epilogues (``ops.w4a8_affine_linear_op``), the q/k RMSNorm + rotary embedding + joint attention layout as
-one kernel (``ops.qkv_rmsnorm_rope``), and the attention output to the [tokens, hidden] layout through
-``ops.heads_to_rows``; ``fused_glue=False`` runs them as torch ops instead.  Weights are drawn N(0, 0.02) per linear from a
+one kernel (``ops.qkv_rmsnorm_rope``), writing q, k, v token-major so that the attention's output is already the
+[tokens, hidden] rows of the output projection (``ops.heads_to_rows`` copies it when the attention returns head-major
+memory); ``fused_glue=False`` runs them as torch ops instead.  Weights are drawn N(0, 0.02) per linear from a
 seeded generator, quantized on the device with the library's weight kernel, and only the packed form is kept.
 
 ``MMDiT.step(..., reference=True)`` runs the same step with every linear replaced by a torch fp32 product of the
@@ -51,6 +52,9 @@ class MMDiTConfig:
     epilogue_gated: bool = True        # with fused_glue: the gated residuals in the GEMM epilogues of the
                                        # attention-output and MLP-down linears (False: torch addcmul)
     epilogue_gelu: bool = True         # with fused_glue: GELU in the MLP-up GEMM's epilogue (False: torch gelu)
+    token_major_qkv: bool = True       # with fused_glue: q, k, v in [tokens, heads, D] memory, passed to the attention
+                                       # as strided views, whose output then is the [tokens, hidden] rows of the output
+                                       # projection (False: head-major q, k, v and the head-to-rows copy)
 
     @property
     def head_dim(self) -> int:
@@ -221,9 +225,13 @@ class MMDiT:
         fused = c.fused_glue and not reference
         st_txt, st_img = txt.shape[0], img.shape[0]
         s_all = st_txt + st_img
-        q = torch.empty(1, nh, s_all, d, dtype=torch.bfloat16, device=img.device)
-        k = torch.empty_like(q)
-        v = torch.empty_like(q)
+        if fused and c.token_major_qkv:
+            q, k, v = (torch.empty(1, s_all, nh, d, dtype=torch.bfloat16, device=img.device).transpose(1, 2)
+                       for _ in range(3))
+        else:
+            q = torch.empty(1, nh, s_all, d, dtype=torch.bfloat16, device=img.device)
+            k = torch.empty_like(q)
+            v = torch.empty_like(q)
         si, st = blk
         mi = self._mod(si, temb_act, reference).chunk(6, dim=-1)
         mt = self._mod(st, temb_act, reference).chunk(6, dim=-1)
@@ -239,8 +247,12 @@ class MMDiT:
             k[0, :, lo:hi] = _apply_rope(F.rms_norm(y[:, 1], (d,), s.k_norm, eps=1e-6), rot).transpose(0, 1)
             v[0, :, lo:hi] = y[:, 2].transpose(0, 1)
         if fused:
-            a = torch.empty(s_all, h, dtype=torch.bfloat16, device=img.device)
-            ops.heads_to_rows(F.scaled_dot_product_attention(q, k, v), [a], 0, h)
+            o = F.scaled_dot_product_attention(q, k, v)
+            if o.transpose(1, 2).is_contiguous():
+                a = o.transpose(1, 2).reshape(s_all, h)   # token-major output: already the [tokens, hidden] rows
+            else:
+                a = torch.empty(s_all, h, dtype=torch.bfloat16, device=img.device)
+                ops.heads_to_rows(o, [a], 0, h)
         else:
             a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).reshape(s_all, h)
         new = []

@@ -631,13 +631,24 @@ def qkv_rmsnorm_rope(y: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor
                      q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s0: int, eps: float = 1e-6) -> None:
     """One stream's QKV output y [S, 3*H*D] (bf16) into the joint attention layout q, k, v [1, H, S_all, D] at
     tokens [s0, s0 + S): q and k RMS-normalized per head (weights q_norm / k_norm [D]) and rotated by ``rope``
-    ([S, D/2] complex64, or its real view [S, D/2, 2] of (cos, sin)); v copied."""
+    ([S, D/2] complex64, or its real view [S, D/2, 2] of (cos, sin)); v copied.
+
+    q, k, v are either contiguous (head-major memory) or all three ``transpose(1, 2)`` views of contiguous
+    [1, S_all, H, D] tensors (token-major memory: the [tokens, hidden] rows, which an attention kernel reads as
+    strided views and mirrors in its output)."""
     dev = _require_cuda(y, q_norm, k_norm, rope, q, k, v)
-    if q.dim() != 4 or q.shape[0] != 1 or not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
-        raise ValueError("q, k, v must be contiguous [1, H, S_all, D]")
+    if q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError("q, k, v must be [1, H, S_all, D]")
     _, h, s_all, d = q.shape
-    if k.shape != q.shape or v.shape != q.shape or q.dtype != torch.bfloat16:
+    if k.shape != q.shape or v.shape != q.shape or q.dtype != torch.bfloat16 or k.dtype != q.dtype or v.dtype != q.dtype:
         raise ValueError("q, k, v must be bf16 of one shape")
+    if all(t.is_contiguous() for t in (q, k, v)):
+        token_major = 0
+    elif all(t.transpose(1, 2).is_contiguous() for t in (q, k, v)):
+        token_major = 1
+    else:
+        raise ValueError("q, k, v must all be contiguous [1, H, S_all, D] or all transposed views of contiguous "
+                         "[1, S_all, H, D]")
     y2 = _as2d(y)
     s = y2.shape[0]
     if y2.shape[1] != 3 * h * d:
@@ -648,8 +659,8 @@ def qkv_rmsnorm_rope(y: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor
     if tuple(rope.shape) != (s, d // 2, 2):
         raise ValueError(f"rope must be [{s}, {d // 2}] complex (or [{s}, {d // 2}, 2] real)")
     qn, kn = q_norm.to(torch.bfloat16).contiguous(), k_norm.to(torch.bfloat16).contiguous()
-    _lib.call("cq_qkv_rmsnorm_rope", _ptr(y2), s, h, d, _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(q), _ptr(k),
-              _ptr(v), s_all, int(s0), _stream(dev))
+    _lib.call("cq_qkv_rmsnorm_rope_layout", _ptr(y2), s, h, d, _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(q),
+              _ptr(k), _ptr(v), s_all, int(s0), token_major, _stream(dev))
 
 
 def _out_ptrs(outs, rows: int, ldo: int):

@@ -368,6 +368,9 @@ CQ_API int cq_linear_w4a8_affine_noalloc(const void* x, int64_t M, int64_t K, in
  * with q, k, v bf16 [H, s_all, D] (the joint attention layout, batch 1), rmsnorm(x) = x * rsqrt(mean(x^2) + eps)
  * in fp32, and rope rotating the interleaved pairs (x[2p], x[2p+1]) by rope[s, p] = (cos, sin) (f32 [S, D/2, 2]),
  * in fp32, rounded to bf16.  D = 64 or 128.
+ * cq_qkv_rmsnorm_rope_layout: the same with token_major = 1 writing q, k, v as bf16 [s_all, H, D] (the [tokens,
+ *   hidden] layout: an attention kernel given these as strided [1, H, s_all, D] views writes its output in the same
+ *   token-major layout, which the output projection reads as it is); token_major = 0 is cq_qkv_rmsnorm_rope.
  */
 CQ_API int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift,
                              const void* scale1p, float eps, int64_t M_pad, int flags, void* q, float* scale,
@@ -417,6 +420,9 @@ CQ_API int cq_heads_to_rows(const void* o, int64_t S, int Hp, int D, void* const
 CQ_API int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm,
                                float eps, const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0,
                                void* stream);
+CQ_API int cq_qkv_rmsnorm_rope_layout(const void* y, int64_t S, int H, int D, const void* q_norm,
+                                      const void* k_norm, float eps, const float* rope, void* q, void* k, void* v,
+                                      int64_t s_all, int64_t s0, int token_major, void* stream);
 
 #ifdef __cplusplus
 }

@@ -128,6 +128,8 @@ def test_dit_glue_argument_checks_need_no_device(lib):
     assert lib.cq_qkv_rmsnorm_rope(vp, 8, 4, 96, vp, vp, f, vp, vp, vp, vp, 8, 0, None) == _lib.CQ_ERR_SHAPE
     assert lib.cq_qkv_rmsnorm_rope(vp, 8, 4, 128, vp, vp, f, vp, vp, vp, vp, 10, 4, None) == _lib.CQ_ERR_SHAPE
     assert lib.cq_qkv_rmsnorm_rope(vp, 0, 4, 128, None, None, f, None, None, None, None, 10, 4, None) == _lib.CQ_OK
+    assert lib.cq_qkv_rmsnorm_rope_layout(vp, 8, 4, 128, vp, vp, f, vp, vp, vp, vp, 8, 0, 2, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_qkv_rmsnorm_rope_layout(vp, 8, 4, 96, vp, vp, f, vp, vp, vp, vp, 8, 0, 1, None) == _lib.CQ_ERR_SHAPE
     # head gather: 1..8 buffers, 16-byte aligned, columns inside the rows
     outs = (ctypes.c_void_p * 2)(16, 32)
     assert lib.cq_heads_to_rows(vp, 8, 4, 128, outs, 0, 0, 512, None) == _lib.CQ_ERR_ARG

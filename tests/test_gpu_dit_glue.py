@@ -48,14 +48,22 @@ def _within_one_rounding(got, want):
     assert float((g != w).float().mean()) <= 0.02
 
 
+def _qkv_buffers(h, s_all, d, token_major):
+    if token_major:   # [1, S_all, H, D] memory seen as [1, H, S_all, D]
+        return tuple(torch.full((1, s_all, h, d), 3.0, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+                     for _ in range(3))
+    return tuple(torch.full((1, h, s_all, d), 3.0, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+
+
+@pytest.mark.parametrize("token_major", [False, True])
 @pytest.mark.parametrize("s,h,d,s0,s_all", [(300, 24, 128, 40, 345), (17, 4, 64, 0, 17)])
-def test_qkv_rmsnorm_rope_matches_torch(ops, s, h, d, s0, s_all):
+def test_qkv_rmsnorm_rope_matches_torch(ops, s, h, d, s0, s_all, token_major):
     g = torch.Generator(device="cuda").manual_seed(s + h)
     y = torch.randn(s, 3 * h * d, generator=g, device="cuda").to(torch.bfloat16)
     qn = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
     kn = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
     rot = _rope_table(s, d, s0, "cuda")
-    q, k, v = (torch.full((1, h, s_all, d), 3.0, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    q, k, v = _qkv_buffers(h, s_all, d, token_major)
     ops.qkv_rmsnorm_rope(y, qn, kn, rot, q, k, v, s0, eps=1e-6)
     yv = y.view(s, 3, h, d)
     want_q = _torch_rope(F.rms_norm(yv[:, 0], (d,), qn, eps=1e-6), rot).transpose(0, 1)
@@ -66,6 +74,41 @@ def test_qkv_rmsnorm_rope_matches_torch(ops, s, h, d, s0, s_all):
     _within_one_rounding(k[0, :, s0:s0 + s], want_k)
     for t in (q, k, v):   # tokens of the other stream are untouched
         assert bool((t[0, :, :s0] == 3.0).all()) and bool((t[0, :, s0 + s:] == 3.0).all())
+
+
+def test_qkv_token_major_equals_head_major_and_attention_output_is_rows(ops):
+    """The token-major layout holds the same values as the head-major one, and the attention over strided
+    token-major views returns [tokens, hidden] rows equal to the head-major attention's output transposed."""
+    s, h, d = 272, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(7)
+    y = torch.randn(s, 3 * h * d, generator=g, device="cuda").to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
+    rot = _rope_table(s, d, 0, "cuda")
+    hm = _qkv_buffers(h, s, d, False)
+    tm = _qkv_buffers(h, s, d, True)
+    ops.qkv_rmsnorm_rope(y, qn, kn, rot, *hm, 0, eps=1e-6)
+    ops.qkv_rmsnorm_rope(y, qn, kn, rot, *tm, 0, eps=1e-6)
+    _status_clear()
+    for a, b in zip(hm, tm):
+        assert torch.equal(a, b)
+    o_hm = F.scaled_dot_product_attention(*hm)
+    o_tm = F.scaled_dot_product_attention(*tm)
+    rows = torch.empty(s, h * d, dtype=torch.bfloat16, device="cuda")
+    ops.heads_to_rows(o_hm, [rows], 0, h * d)
+    _status_clear()
+    got = o_tm.transpose(1, 2).reshape(s, h * d)
+    assert (got - rows).abs().max().item() <= 2.0 ** -6 * rows.abs().max().item()
+
+
+def test_qkv_rejects_mixed_layouts(ops):
+    s, h, d = 16, 2, 64
+    y = torch.zeros(s, 3 * h * d, dtype=torch.bfloat16, device="cuda")
+    w = torch.ones(d, dtype=torch.bfloat16, device="cuda")
+    rot = _rope_table(s, d, 0, "cuda")
+    (q, _, _), (_, k, v) = _qkv_buffers(h, s, d, False), _qkv_buffers(h, s, d, True)
+    with pytest.raises(ValueError):
+        ops.qkv_rmsnorm_rope(y, w, w, rot, q, k, v, 0)
 
 
 def _lnmod_inputs(m, k, seed):
