@@ -693,7 +693,7 @@ def run_mmdit(args, world, rank, local):
     cfg = mm.MMDiTConfig(blocks=args.mmdit_blocks, quantize_modulation=not args.mmdit_bf16_modulation)
     model = mm.MMDiT(cfg, device=dev, seed=0)
     img, txt, temb = model.inputs(seed=1 + rank)
-    launches = 2 * len(model.linears()) + (3 * cfg.blocks if cfg.fused_glue else 0)   # + qkv glue x2, head gather
+    launches = model.launches_per_step()
     linears = ("every linear W4A8 affine g128, ConvRot g256 (modulation included)" if cfg.quantize_modulation else
                "every linear but the adaLN modulation W4A8 affine g128, ConvRot g256; modulation bf16 (torch), as "
                "the reference's quantization profiles leave it")
@@ -802,7 +802,7 @@ def run_ltx(args, world, rank, local):
         "e2e": {"value": e2e_ms, "unit": "ms", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": (x.numel() + ctx.numel()) * 2, "d2h_bytes_per_step": out.numel() * 2,
                 "path": "LTXDiT.step with pinned-host input/output copies"},
-        "gpu_launches": (2 * len(model.linears()) + 3 * cfg.blocks) * args.steps,
+        "gpu_launches": (2 * len(model.linears()) + cfg.blocks) * args.steps,   # linears + the qkv glue per block
         "clocks": clk.summary(),
     }
     if world > 1 and not args.no_reference_check:

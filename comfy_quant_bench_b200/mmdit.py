@@ -52,6 +52,9 @@ class MMDiTConfig:
     epilogue_gated: bool = True        # with fused_glue: the gated residuals in the GEMM epilogues of the
                                        # attention-output and MLP-down linears (False: torch addcmul)
     epilogue_gelu: bool = True         # with fused_glue: GELU in the MLP-up GEMM's epilogue (False: torch gelu)
+    batched_modulation: bool = True    # with fused_glue and quantize_modulation: the adaLN modulation linears of every
+                                       # block and stream, which all read the same timestep embedding, as one
+                                       # few-token product over their joined weights at the start of the step
     token_major_qkv: bool = True       # with fused_glue: q, k, v in [tokens, heads, D] memory, passed to the attention
                                        # as strided views, whose output then is the [tokens, hidden] rows of the output
                                        # projection (False: head-major q, k, v and the head-to-rows copy)
@@ -91,6 +94,27 @@ class QLinear:
                                          residual=residual, gate=gate, shift=shift, scale=scale,
                                          group_size=self.cfg.group_size, convrot_groupsize=self.cfg.convrot_groupsize,
                                          eps=1e-6)
+
+    @classmethod
+    def joined(cls, parts: list["QLinear"]) -> "QLinear":
+        """One linear with the parts' output features in order (the same input; every output row is the same
+        product as in its part).  The parts' packed weights, zero operands and biases become views of the joined
+        tensors, so the packed weights are held once."""
+        lin = cls.__new__(cls)
+        lin.cfg, lin.in_f = parts[0].cfg, parts[0].in_f
+        lin.out_f = sum(p.out_f for p in parts)
+        lin.qweight = torch.cat([p.qweight for p in parts])
+        lin.scale = torch.cat([p.scale for p in parts], dim=1)
+        lin.zeros = torch.cat([p.zeros for p in parts], dim=1)
+        lin.zt = torch.cat([p.zt for p in parts])
+        lin.bias = torch.cat([p.bias for p in parts]) if parts[0].bias is not None else None
+        off = 0
+        for p in parts:
+            p.qweight, p.zt = lin.qweight[off:off + p.out_f], lin.zt[off:off + p.out_f]
+            if lin.bias is not None:
+                p.bias = lin.bias[off:off + p.out_f]
+            off += p.out_f
+        return lin
 
     def dequantized_weight(self) -> torch.Tensor:
         """W in the rotated basis, fp32 [N, K]: (q - 8) * scale + zeros per 128-wide group."""
@@ -152,6 +176,8 @@ class MMDiT:
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed)
         self.blocks = [(_Stream(gen, self.device, cfg), _Stream(gen, self.device, cfg)) for _ in range(cfg.blocks)]
+        # every block's image- and text-stream modulation linear, joined (block order, image stream first)
+        self.mod_all = QLinear.joined([st.mod for blk in self.blocks for st in blk]) if cfg.quantize_modulation else None
         d = cfg.head_dim
         self.rope_txt = _rope_table(cfg.txt_tokens, d, self.device)
         self.rope_img = _rope_table(cfg.img_tokens, d, self.device, offset=cfg.txt_tokens)
@@ -173,6 +199,22 @@ class MMDiT:
             for st in (img, txt):
                 out += [l for l in (st.mod, st.qkv, st.out, st.fc1, st.fc2) if l is not None]
         return out
+
+    def launches_per_step(self) -> int:
+        """The library's kernel launches in one kernel-path step (attention and the timestep embedding's torch ops
+        not counted)."""
+        c = self.cfg
+        n = 0
+        for m in (c.img_tokens, c.txt_tokens):
+            n += sum(ops.affine_linear_launches(m, nn, kk) for nn, kk in
+                     ((3 * c.hidden, c.hidden), (c.hidden, c.hidden), (c.mlp, c.hidden), (c.hidden, c.mlp)))
+            n += 1 if c.fused_glue else 0                                        # q/k norm + rotary + layout
+        n *= c.blocks
+        if c.fused_glue and not c.token_major_qkv:
+            n += c.blocks                                                        # head-major output to rows
+        if self.mod_all is not None:
+            n += 2 if (c.batched_modulation and c.fused_glue) else 2 * 2 * c.blocks
+        return n
 
     def weight_bytes(self) -> int:
         return sum(l.qweight.numel() + 2 * l.scale.numel() * 2 + l.zt.numel() * 2 for l in self.linears())
@@ -203,8 +245,13 @@ class MMDiT:
         only) the layer norm + modulation run inside the activation kernel of the QKV and MLP-up linears and the
         q/k RMSNorm + rotary + layout copies are one kernel; the reference path always runs the torch ops."""
         temb_act = F.silu(temb.float()).to(torch.bfloat16)
-        for blk in self.blocks:
-            img, txt = self._block(blk, img, txt, temb_act, reference)
+        c = self.cfg
+        mods = None
+        if c.batched_modulation and c.fused_glue and self.mod_all is not None and not reference:
+            # [1, 2 * blocks * 6 * hidden]: one activation kernel and one weight stream for all modulation linears
+            mods = self.mod_all(temb_act).split(6 * c.hidden, dim=-1)
+        for i, blk in enumerate(self.blocks):
+            img, txt = self._block(blk, img, txt, temb_act, reference, None if mods is None else mods[2 * i:2 * i + 2])
         return img, txt
 
     def block_errors(self, img: torch.Tensor, txt: torch.Tensor, temb: torch.Tensor) -> list[float]:
@@ -218,8 +265,9 @@ class MMDiT:
             errs.append(rel_l2(img, ref_img))
         return errs
 
-    def _block(self, blk, img: torch.Tensor, txt: torch.Tensor, temb_act: torch.Tensor, reference: bool):
-        """One dual-stream block on (img, txt); returns the new (img, txt)."""
+    def _block(self, blk, img: torch.Tensor, txt: torch.Tensor, temb_act: torch.Tensor, reference: bool, mods=None):
+        """One dual-stream block on (img, txt); returns the new (img, txt).  ``mods``: the block's (image, text)
+        modulation outputs when computed ahead for the whole step."""
         c = self.cfg
         h, nh, d = c.hidden, c.heads, c.head_dim
         fused = c.fused_glue and not reference
@@ -233,8 +281,8 @@ class MMDiT:
             k = torch.empty_like(q)
             v = torch.empty_like(q)
         si, st = blk
-        mi = self._mod(si, temb_act, reference).chunk(6, dim=-1)
-        mt = self._mod(st, temb_act, reference).chunk(6, dim=-1)
+        mi = (mods[0] if mods is not None else self._mod(si, temb_act, reference)).chunk(6, dim=-1)
+        mt = (mods[1] if mods is not None else self._mod(st, temb_act, reference)).chunk(6, dim=-1)
         for x, s, m, rot, lo, hi in ((txt, st, mt, self.rope_txt, 0, st_txt),
                                      (img, si, mi, self.rope_img, st_txt, s_all)):
             if fused:

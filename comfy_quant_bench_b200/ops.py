@@ -419,6 +419,13 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     return out if dt == torch.bfloat16 else out.to(dt)
 
 
+def affine_linear_launches(m: int, n: int, k: int) -> int:
+    """Kernels one fused W4A8 affine linear of [m, k] x [k, n] launches: the activation kernel and the product, plus
+    the split-K finalize kernel when the GEMM splits K (the workspace then holds fp32 partial sums)."""
+    lib = _lib.load()
+    return 3 if m > 8 and lib.cq_linear_workspace_bytes_n(m, k, n) > lib.cq_linear_workspace_bytes(m, k) else 2
+
+
 def prepare_affine_zeros(zeros: torch.Tensor, group_size: int = 128) -> torch.Tensor:
     """The zero-point operand of the W4A8 GEMM, built once per weight from the awq-layout zeros [K/G, N]:
     zt [N, cq_group_sum_cols(K)] bf16 with zt[n, j] = zeros[j mod G, n] for j < 2G, else 0."""

@@ -55,6 +55,27 @@ def test_mmdit_step_is_deterministic_and_graph_capturable(mmdit):
     assert torch.equal(model.step(img, txt, temb)[0], eager)
 
 
+def test_mmdit_layout_and_modulation_forms_are_bit_identical(mmdit):
+    """The joined modulation product (one activation kernel and one weight stream for every block's modulation
+    linears) and the token-major attention layout change only how the work is launched: the step output equals the
+    per-stream, head-major form bit for bit."""
+    from dataclasses import replace
+    cfg = mmdit.MMDiTConfig(blocks=3, hidden=512, heads=4, mlp=1024, img_tokens=300, txt_tokens=40)
+    model = mmdit.MMDiT(cfg, device="cuda", seed=9)
+    img, txt, temb = model.inputs(seed=10)
+    base = model.step(img, txt, temb)
+    outs = []
+    for batched, token_major in ((False, True), (True, False), (False, False)):
+        model.cfg = replace(cfg, batched_modulation=batched, token_major_qkv=token_major)
+        outs.append(model.step(img, txt, temb))
+    model.cfg = cfg
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o[0], base[0]) and torch.equal(o[1], base[1])
+    from comfy_quant_bench_b200 import _lib
+    assert _lib.take_device_status() == (0, 0)
+
+
 def test_wan_step_matches_reference():
     """Wan-like block stack on the mixed plan (W4A4 ConvRot g64 and W8A8 linears) against the fp32-linear
     reference of the same step (the same rel-L2 bound as the MMDiT step)."""
