@@ -719,7 +719,9 @@ def run_wan(args, world, rank, local):
               "batch": 1,
               "linears": f"{plan['w4a4']} ConvRot W4A4 (Hadamard g{cfg.w4a4_rot}, per-row int4 weights, per-token "
                          f"int4 acts) + {plan['w8a8']} W8A8 int8_tensorwise (per-token int8 acts), seeded choice",
-              "glue": "torch ops"}
+              "glue": ("modulated layer norms in the QKV / MLP-up activation kernels, q/k RMSNorm + rotary in one "
+                       "kernel, GELU and the residual updates in the GEMM epilogues; affine layer norm and attention "
+                       "torch" if cfg.fused_glue else "torch ops")}
     def block_check():
         errs = model.block_errors(x, ctx)
         return {"max_block_rel_l2": max(errs), "mean_block_rel_l2": sum(errs) / len(errs),
@@ -728,7 +730,7 @@ def run_wan(args, world, rank, local):
                         "a one-rounding difference in a linear's input into a code flip of 1/7 of the token scale"}
 
     _run_dit(args, world, rank, local, model, (x, ctx), lambda o: o, "Wan DiT denoise steps/s", config,
-             2 * len(model.linears()), block_check)
+             model.launches_per_step(), block_check)
 
 
 def run_ltx(args, world, rank, local):

@@ -81,6 +81,10 @@ SIGNATURES = {
     "cq_linear_w4a8_affine": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64,
                                      _vp]),
     "cq_linear_w8a8": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "cq_linear_convrot_w4a4_op": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _opp,
+                                         _vp, _vp, _i64, _vp]),
+    "cq_linear_w8a8_op": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _f32, _vp, _vp, _vp, _opp, _vp, _vp, _i64,
+                                 _vp]),
     "cq_linear_w4a8_affine_noalloc": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp]),
     "cq_gemm_affine_peers": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64,
                                     _int, _vp]),
@@ -94,6 +98,7 @@ SIGNATURES = {
     "cq_rotquant_absmax": (_int, [_vp, _i64, _i64, _int, _i64, _vp, _vp]),
     "cq_rotquant_scaled": (_int, [_vp, _i64, _i64, _int, _vp, _i64, _int, _vp, _vp, _vp, _vp]),
     "cq_qkv_rmsnorm_rope": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "cq_rmsnorm_rope_rows": (_int, [_vp, _i64, _int, _vp, _f32, _vp, _int, _vp, _vp]),
     "cq_qkv_rmsnorm_rope_layout": (_int, [_vp, _i64, _int, _int, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _i64, _i64, _int,
                                           _vp]),
     "cq_heads_to_rows": (_int, [_vp, _i64, _int, _int, _vp, _int, _i64, _i64, _vp]),

@@ -107,17 +107,18 @@ int cq_rotquant(const void* x, int64_t M, int64_t K, int rot_group, int swiglu, 
 
 static int rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
                           float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream,
-                          bool scale_plus_one);
+                          bool scale_plus_one, int mode = CQ_ACT_INT8_ROW);
 
 int cq_rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
                       float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream) {
   return rotquant_lnmod(x, M, K, rot_group, shift, scale1p, eps, M_pad, flags, q, scale, group_sums, stream, false);
 }
 
-// scale_plus_one: `scale1p` holds the modulation scale; the kernel forms bf16(1 + scale) itself
+// scale_plus_one: `scale1p` holds the modulation scale; the kernel forms bf16(1 + scale) itself.  mode
+// CQ_ACT_INT4_ROW: per-token int4 values held as int8 codes (the W4A4 GEMM's operand), no group sums.
 static int rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, const void* shift, const void* scale1p,
                           float eps, int64_t M_pad, int flags, void* q, float* scale, void* group_sums, void* stream,
-                          bool scale_plus_one) {
+                          bool scale_plus_one, int mode) {
   if (M < 0 || M_pad < M || M_pad > kMaxRows) return CQ_ERR_SHAPE;
   if (K < 256 || K % 256 != 0 || K > kMaxLnModK) return CQ_ERR_SHAPE;
   if (!valid_rot(rot_group)) return CQ_ERR_ARG;
@@ -130,11 +131,12 @@ static int rotquant_lnmod(const void* x, int64_t M, int64_t K, int rot_group, co
       !aligned(scale1p, 16))
     return CQ_ERR_ALIGN;
   if (int dv = check_device()) return dv;
-  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), 0, 0, (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
+  cq::RotQuantArgs a{x, M, M_pad, static_cast<int>(K), 0, mode == CQ_ACT_INT4_ROW ? 1 : 0,
+                     (flags & CQ_Q_KPERM) ? 1 : 0, q, scale, nullptr,
                      static_cast<__nv_bfloat16*>(group_sums), cq::rsplit_cols(static_cast<int>(K)),
                      static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale1p), eps,
                      scale_plus_one ? 1 : 0};
-  return cuda_status(cq::launch_act_rotquant(rot_group, false, CQ_ACT_INT8_ROW, a, static_cast<cudaStream_t>(stream)));
+  return cuda_status(cq::launch_act_rotquant(rot_group, false, mode, a, static_cast<cudaStream_t>(stream)));
 }
 
 // the two phases of per-token int8 activations for a row-parallel linear (K split over ranks)
@@ -198,6 +200,21 @@ int cq_qkv_rmsnorm_rope_layout(const void* y, int64_t S, int H, int D, const voi
                     static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), S, s_all, s0, H, D, eps,
                     token_major ? static_cast<int64_t>(H) * D : D, token_major ? D : s_all * D};
   return cuda_status(cq::launch_qkv_rmsnorm_rope(a, static_cast<cudaStream_t>(stream)));
+}
+
+int cq_rmsnorm_rope_rows(const void* x, int64_t S, int C, const void* w, float eps, const float* rope, int D,
+                         void* out, void* stream) {
+  if (S < 0 || S > kMaxRows || C < 8 || C % 8 != 0 || C > 16384) return CQ_ERR_SHAPE;
+  if (rope != nullptr && ((D != 64 && D != 128) || C % D != 0)) return CQ_ERR_SHAPE;
+  if (!(eps >= 0.0f)) return CQ_ERR_ARG;
+  if (S == 0) return CQ_OK;
+  if (x == nullptr || w == nullptr || out == nullptr) return CQ_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || (rope != nullptr && !aligned(rope, 8)))
+    return CQ_ERR_ALIGN;
+  if (int dv = check_device()) return dv;
+  cq::RmsRopeArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), rope,
+                    static_cast<__nv_bfloat16*>(out), S, C, rope != nullptr ? D : 0, eps, 1};
+  return cuda_status(cq::launch_rmsnorm_rope_rows(a, static_cast<cudaStream_t>(stream)));
 }
 
 int cq_heads_to_rows(const void* o, int64_t S, int Hp, int D, void* const* outs, int n_outs, int64_t col0,
@@ -268,7 +285,8 @@ static int check_gemm(const void* a, const void* b, const void* out, int64_t M, 
 }
 
 static int gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl);
+                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl,
+                       const cq::OutOp* op = nullptr);
 
 int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
                    const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
@@ -277,7 +295,8 @@ int cq_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b,
 
 // pdl: the fused linears launch the GEMM as a programmatic dependent of their activation kernel
 static int gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl) {
+                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream, bool pdl,
+                       const cq::OutOp* op) {
   if (b_format != CQ_B_INT4_SIGNED && b_format != CQ_B_INT8) return CQ_ERR_ARG;
   if (a_kperm != 0 && (a_kperm != 1 || b_format == CQ_B_INT8)) return CQ_ERR_ARG;
   if (int e = check_gemm(a, b, out, M, N, K)) return e;
@@ -285,7 +304,7 @@ static int gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void
   if (sa == nullptr || sb == nullptr) return CQ_ERR_ARG;
   if (int dv = check_device()) return dv;
   return cq::launch_gemm_rowcol(a, a_kperm, sa, b, b_format, sb, bias, out, static_cast<int>(M), static_cast<int>(N),
-                                static_cast<int>(K), static_cast<cudaStream_t>(stream), pdl);
+                                static_cast<int>(K), static_cast<cudaStream_t>(stream), pdl, op);
 }
 
 int cq_gemm_groupwise(const int8_t* a, int a_kperm, const float* sa_g, int64_t sa_ld, const void* b_packed,
@@ -557,6 +576,51 @@ int cq_linear_w4a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_gr
   if (e) return e;
   return gemm_affine(w.xq, 1, w.sx, w.gsplit, qweight, s_bf16, zt_bf16, bias, op, out, M, N, K, group, stream, true,
                      splitk_region(workspace, workspace_bytes, M, K, N));
+}
+
+// the library's epilogue operation from the public one (the same kind codes; null: plain output)
+static const cq::OutOp* to_out_op(const cq_out_op* op, cq::OutOp* buf) {
+  if (op == nullptr || op->kind == CQ_OUT_PLAIN) return nullptr;
+  *buf = cq::OutOp{op->kind, op->residual, op->residual_ld, op->gate};
+  return buf;
+}
+
+// the fused row/col linears with an epilogue operation: activations (optionally of the modulated layer norm), then
+// the GEMM as a programmatic dependent with `op` in its epilogue
+static int linear_rowcol_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int mode,
+                            const void* shift, const void* mod_scale, float eps, const void* weight, int b_format,
+                            const float* wscale, const void* bias, const cq_out_op* op, void* out, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+  if (M == 0) return CQ_OK;
+  if (int e = check_out_op(op, out, M, N)) return e;
+  Workspace w;
+  if (int e = carve(workspace, workspace_bytes, M, K, &w)) return e;
+  const int kperm = b_format == CQ_B_INT4_SIGNED ? CQ_Q_KPERM : 0;
+  const int codes = mode == CQ_ACT_INT4_ROW ? CQ_Q_INT8_CODES : 0;
+  const int e = shift != nullptr
+                    ? rotquant_lnmod(x, M, K, rot_group, shift, mod_scale, eps, w.mpad, kperm, w.xq, w.sx, nullptr,
+                                     stream, true, mode)
+                    : cq_rotquant(x, M, K, rot_group, 0, mode, 0, w.mpad, codes | kperm, w.xq, w.sx, nullptr, stream);
+  if (e) return e;
+  cq::OutOp buf;
+  return gemm_rowcol(w.xq, kperm ? 1 : 0, w.sx, weight, b_format, wscale, bias, out, M, N, K, stream, true,
+                     to_out_op(op, &buf));
+}
+
+int cq_linear_convrot_w4a4_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int act_bits,
+                              const void* shift, const void* mod_scale, float eps, const void* qweight,
+                              const float* wscale, const void* bias, const cq_out_op* op, void* out, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
+  if (act_bits != 4 && act_bits != 8) return CQ_ERR_ARG;
+  return linear_rowcol_op(x, M, K, N, rot_group, act_bits == 4 ? CQ_ACT_INT4_ROW : CQ_ACT_INT8_ROW, shift, mod_scale,
+                          eps, qweight, CQ_B_INT4_SIGNED, wscale, bias, op, out, workspace, workspace_bytes, stream);
+}
+
+int cq_linear_w8a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
+                      const void* mod_scale, float eps, const int8_t* weight, const float* wscale, const void* bias,
+                      const cq_out_op* op, void* out, void* workspace, int64_t workspace_bytes, void* stream) {
+  return linear_rowcol_op(x, M, K, N, rot_group, CQ_ACT_INT8_ROW, shift, mod_scale, eps, weight, CQ_B_INT8, wscale,
+                          bias, op, out, workspace, workspace_bytes, stream);
 }
 
 int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,

@@ -414,6 +414,24 @@ __device__ __forceinline__ void sts_gated_pair(uint32_t a0, uint32_t a1, float v
       ::"r"(a0), "r"(a1), "f"(v0), "f"(v1), "r"(gate2), "r"(r0), "r"(r1) : "memory");
 }
 
+// v0 (low half) and v1 (high half) as a bf16 pair (round to nearest even)
+__device__ __forceinline__ uint32_t bf16_pair_bits(float v0, float v1) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v1), "f"(v0));
+  return d;
+}
+
+// sts_gated_pair's value in a register: bf16(r_i + g * bf16(v_i)) for i = 0 (low half), 1 (high half)
+__device__ __forceinline__ uint32_t gated_pair_bits(float v0, float v1, uint32_t gate2, uint32_t r0, uint32_t r1) {
+  uint32_t o;
+  asm("{\n\t.reg .b32 y, r;\n\t"
+      "cvt.rn.bf16x2.f32 y, %2, %1;\n\t"
+      "prmt.b32 r, %4, %5, 0x5410;\n\t"
+      "fma.rn.bf16x2 %0, %3, y, r;\n\t}"
+      : "=r"(o) : "f"(v0), "f"(v1), "r"(gate2), "r"(r0), "r"(r1));
+  return o;
+}
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
 // Smallest bf16 value >= v for v > 0 (mantissa rounded up), as the reference's per-group quantizer does.

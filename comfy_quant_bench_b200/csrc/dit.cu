@@ -99,4 +99,75 @@ cudaError_t launch_heads_to_rows(const HeadsToRowsArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// rmsnorm_rope_rows_kernel: one token's row x [C] (bf16) -> out = rope(bf16(x * rsqrt(mean(x^2) + eps) * w)), the
+// RMSNorm over the whole row in fp32 with one bf16 rounding (torch's fused rms_norm on a bf16 row), then, with a
+// rope table, each D-wide head's interleaved pairs (x[2p], x[2p+1]) rotated by (cos, sin) of the token's position in
+// fp32 and rounded to bf16 (the float copy + complex multiply + bf16 copy it replaces).  One CTA per token; each
+// thread holds `chunks` 16-byte chunks of the row in registers across the CTA's sum, so out may be x.
+__global__ void __launch_bounds__(512) rmsnorm_rope_rows_kernel(const RmsRopeArgs a) {
+  constexpr int kMaxChunks = 4;
+  __shared__ float red[16];
+  const int64_t s = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  const int nchunk = a.C >> 3;
+  const __nv_bfloat16* xr = a.x + s * a.C;
+  uint4 raw[kMaxChunks];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    raw[i] = make_uint4(0, 0, 0, 0);
+    if (i < a.chunks && c < nchunk) raw[i] = *reinterpret_cast<const uint4*>(xr + 8 * c);
+    const uint32_t wv[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = bf16_bits_to_f32(wv[j] & 0xFFFFu), hi = bf16_bits_to_f32(wv[j] >> 16);
+      ss = fmaf(lo, lo, ss);
+      ss = fmaf(hi, hi, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int w = 0; w < nwarps; ++w) tot += red[w];
+  const float r = rsqrtf(tot / static_cast<float>(a.C) + a.eps);
+  const float* rp = a.rope != nullptr ? a.rope + s * (a.D / 2) * 2 : nullptr;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (i >= a.chunks || c >= nchunk) break;
+    const uint4 wq = *reinterpret_cast<const uint4*>(a.w + 8 * c);
+    const uint32_t xv[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+    uint32_t ov[4];
+    const int p0 = ((8 * c) % a.D) >> 1;   // first rotary pair of the chunk inside its head
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float x0 = bf16_round(bf16_bits_to_f32(xv[j] & 0xFFFFu) * r * bf16_bits_to_f32(wv[j] & 0xFFFFu));
+      float x1 = bf16_round(bf16_bits_to_f32(xv[j] >> 16) * r * bf16_bits_to_f32(wv[j] >> 16));
+      if (rp != nullptr) {
+        const float2 cs = *reinterpret_cast<const float2*>(rp + 2 * (p0 + j));
+        const float y0 = x0 * cs.x - x1 * cs.y, y1 = x0 * cs.y + x1 * cs.x;
+        x0 = y0;
+        x1 = y1;
+      }
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(x0, x1);
+      ov[j] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    *reinterpret_cast<uint4*>(a.out + s * a.C + 8 * c) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+  }
+}
+
+cudaError_t launch_rmsnorm_rope_rows(const RmsRopeArgs& a, cudaStream_t st) {
+  if (a.S == 0) return cudaSuccess;
+  const int nchunk = a.C / 8;
+  RmsRopeArgs b = a;
+  b.chunks = (nchunk + 511) / 512;
+  const int threads = ((nchunk + b.chunks - 1) / b.chunks + 31) / 32 * 32;
+  rmsnorm_rope_rows_kernel<<<static_cast<unsigned>(a.S), threads, 0, st>>>(b);
+  return cudaGetLastError();
+}
+
 }  // namespace cq

@@ -87,7 +87,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
   using P = Plan<EPI>;
   static_assert(BFMT == BF_U4 || BFMT == BF_S4, "the pair kernel converts packed int4 weights");
   static_assert(!GLU || EPI == EPI_ROWCOL, "the SwiGLU output is a row/col epilogue");
-  static_assert(OP == OUT_PLAIN || EPI == EPI_AFFINE, "output operations are affine-epilogue variants");
+  static_assert(OP == OUT_PLAIN || EPI == EPI_AFFINE || (EPI == EPI_ROWCOL && !GLU),
+                "output operations are affine or plain row/col epilogue variants");
   constexpr int kXS = P::kXStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -737,6 +738,15 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
               if (m < M && j < ncols) args.out[static_cast<int64_t>(m) * ncols + j] = __float2bfloat16_rn(__fmul_rn(silu, u));
             }
           }
+        } else if constexpr (OP != OUT_PLAIN) {
+          const uint32_t gate2 = load_gate2<OP>(args, n, n_ok);
+#pragma unroll 1
+          for (int ch = 0; ch < kChunks; ++ch) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr + 32 * ch, r);
+            tmem_wait_ld_dep(r);
+            if (n_ok && m0 + 32 * ch < M) rowcol_op_chunk<OP>(args, r, sa_stage + 32 * ch, sb, bias, m0 + 32 * ch, n, gate2);
+          }
         } else {
           __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;
 #pragma unroll 1
@@ -923,7 +933,7 @@ static bool use_pair_kernel(int M, int N) {
 }
 
 int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl) {
+                       const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl, const OutOp* op) {
   GemmArgs g{};
   g.pdl = pdl;
   g.sa = sa;
@@ -931,13 +941,25 @@ int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void
   g.bias = static_cast<const __nv_bfloat16*>(bias);
   g.out = static_cast<__nv_bfloat16*>(out);
   g.M = M; g.N = N; g.K = K;
-  if (b_format == CQ_B_INT8) return launch_gemm_t<EPI_ROWCOL, BF_S8, false>(a, b, nullptr, g, st);
-  if (use_pair_kernel(M, N)) {
-    if (a_kperm) return launch_gemm_pair_t<EPI_ROWCOL, BF_S4, true>(a, b, nullptr, g, st);
-    return launch_gemm_pair_t<EPI_ROWCOL, BF_S4, false>(a, b, nullptr, g, st);
+  if (op != nullptr && op->kind != OUT_PLAIN) {
+    g.out_op = op->kind;
+    g.res = static_cast<const __nv_bfloat16*>(op->res);
+    g.res_ld = op->res_ld;
+    g.gate = static_cast<const __nv_bfloat16*>(op->gate);
   }
-  if (a_kperm) return launch_gemm_t<EPI_ROWCOL, BF_S4, true>(a, b, nullptr, g, st);
-  return launch_gemm_t<EPI_ROWCOL, BF_S4, false>(a, b, nullptr, g, st);
+  auto launch = [&](auto op_c) {
+    constexpr int kOp = decltype(op_c)::value;
+    if (b_format == CQ_B_INT8) return launch_gemm_t<EPI_ROWCOL, BF_S8, false, false, kOp>(a, b, nullptr, g, st);
+    if (use_pair_kernel(M, N)) {
+      if (a_kperm) return launch_gemm_pair_t<EPI_ROWCOL, BF_S4, true, false, kOp>(a, b, nullptr, g, st);
+      return launch_gemm_pair_t<EPI_ROWCOL, BF_S4, false, false, kOp>(a, b, nullptr, g, st);
+    }
+    if (a_kperm) return launch_gemm_t<EPI_ROWCOL, BF_S4, true, false, kOp>(a, b, nullptr, g, st);
+    return launch_gemm_t<EPI_ROWCOL, BF_S4, false, false, kOp>(a, b, nullptr, g, st);
+  };
+  if (g.out_op == OUT_GELU) return launch(std::integral_constant<int, OUT_GELU>{});
+  if (g.out_op == OUT_GATED) return launch(std::integral_constant<int, OUT_GATED>{});
+  return launch(std::integral_constant<int, OUT_PLAIN>{});
 }
 
 // W4A4 row/col GEMM with the SwiGLU output: b holds the weight rows interleaved in groups of 32 (16 gate rows, then

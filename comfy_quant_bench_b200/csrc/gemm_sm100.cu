@@ -194,6 +194,50 @@ __device__ __forceinline__ float2 out_apply2(float2 u) {
   }
 }
 
+// Row/col epilogue with an output operation: one 32-token chunk (tokens m_c + [0, 32)) of column n from the chunk's
+// int32 sums r.  v = fma(float(P) * sb, sa[m], bias), the plain epilogue's value; then GELU-tanh of bf16(v), or the
+// gated residual bf16(res[m, n] + gate[n] * bf16(v)) in one packed bf16 fma (gate2: the gate's bits in both halves);
+// stored as bf16.  Rows past M are neither read nor written.  Each (m, n) is read and written by one thread, so the
+// residual may be the output itself.
+template <int OP>
+__device__ __forceinline__ void rowcol_op_chunk(const GemmArgs& args, const uint32_t (&r)[32], const float* sa_c,
+                                                float sb, float bias, int m_c, int n, uint32_t gate2) {
+  const int N = args.N;
+  const int rows = min(32, args.M - m_c);
+  uint32_t res[OP == OUT_GATED ? 32 : 1];
+  if constexpr (OP == OUT_GATED) {
+    const unsigned short* rp =
+        reinterpret_cast<const unsigned short*>(args.res) + static_cast<int64_t>(m_c) * args.res_ld + n;
+#pragma unroll
+    for (int t = 0; t < 32; ++t) res[t] = t < rows ? __ldg(rp + static_cast<int64_t>(t) * args.res_ld) : 0u;
+  }
+  __nv_bfloat16* orow = args.out + static_cast<int64_t>(m_c) * N + n;
+#pragma unroll
+  for (int t = 0; t < 32; t += 2) {
+    const float2 c = *reinterpret_cast<const float2*>(sa_c + t);
+    const float v0 = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t])), sb), c.x, bias);
+    const float v1 = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[t + 1])), sb), c.y, bias);
+    uint32_t o;
+    if constexpr (OP == OUT_GATED) {
+      o = gated_pair_bits(v0, v1, gate2, res[t], res[t + 1]);
+    } else {
+      const float2 g = out_apply2<OP>(make_float2(v0, v1));
+      o = bf16_pair_bits(g.x, g.y);
+    }
+    if (t < rows) *reinterpret_cast<unsigned short*>(orow) = static_cast<unsigned short>(o & 0xFFFFu);
+    if (t + 1 < rows) *reinterpret_cast<unsigned short*>(orow + N) = static_cast<unsigned short>(o >> 16);
+    orow += 2 * static_cast<int64_t>(N);
+  }
+}
+
+// the gate of column n in both halves of a word (gated residual output), else 0
+template <int OP>
+__device__ __forceinline__ uint32_t load_gate2(const GemmArgs& args, int n, bool n_ok) {
+  if constexpr (OP != OUT_GATED) return 0u;
+  const uint32_t g = n_ok ? static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(args.gate) + n)) : 0u;
+  return g | (g << 16);
+}
+
 // Tile order.  Tiles are visited in groups of up to kRasterGroup token tiles: inside a group the token tile varies
 // fastest and the weight tile next, so one wave of CTAs (consecutive tile indices) covers a few token tiles by many
 // weight tiles.  Both operands of a wave then stay in L2, where a plain token-fastest order would stream a
@@ -248,7 +292,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             const __grid_constant__ OutMaps tm_out, const GemmArgs args) {
   using P = SmemPlan<EPI, BFMT, GLU>;
   static_assert(!GLU || (EPI == EPI_ROWCOL && BFMT == BF_S4), "the SwiGLU output is a row/col W4A4 epilogue");
-  static_assert(OP == OUT_PLAIN || EPI == EPI_AFFINE, "output operations are affine-epilogue variants");
+  static_assert(OP == OUT_PLAIN || EPI == EPI_AFFINE || (EPI == EPI_ROWCOL && !GLU),
+                "output operations are affine or plain row/col epilogue variants");
   constexpr int kTmaStages = P::kStages;
   constexpr bool kConv = BFMT != BF_S8;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -813,6 +858,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
               const int m = m0 + 32 * ch + tb + k;
               if (m < M) args.out[static_cast<int64_t>(m) * ncols + j] = __float2bfloat16_rn(__fmul_rn(silu, u));
             }
+          }
+        } else if constexpr (OP != OUT_PLAIN) {
+          stage_sa();
+          const uint32_t gate2 = load_gate2<OP>(args, n, n_ok);
+#pragma unroll 1
+          for (int ch = 0; ch < kChunks; ++ch) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr + 32 * ch, r);
+            tmem_wait_ld_dep(r);
+            if (n_ok && m0 + 32 * ch < M) rowcol_op_chunk<OP>(args, r, sa_stage + 32 * ch, sb, bias, m0 + 32 * ch, n, gate2);
           }
         } else {
         __nv_bfloat16* orow = args.out + static_cast<int64_t>(m0) * N + n;

@@ -65,13 +65,30 @@ struct HeadsToRowsArgs {
 };
 cudaError_t launch_heads_to_rows(const HeadsToRowsArgs& a, cudaStream_t st);
 
+// DiT glue: RMSNorm over whole rows (a Wan-style q/k norm over the hidden dim), then optionally the rotary rotation of
+// each D-wide head's interleaved pairs
+struct RmsRopeArgs {
+  const __nv_bfloat16* x;     // [S, C]
+  const __nv_bfloat16* w;     // [C] norm weight
+  const float* rope;          // [S, D/2, 2] (cos, sin) or null: no rotation
+  __nv_bfloat16* out;         // [S, C]; may be x
+  int64_t S;
+  int C, D;
+  float eps;
+  int chunks;                 // 8-column chunks per thread
+};
+cudaError_t launch_rmsnorm_rope_rows(const RmsRopeArgs& a, cudaStream_t st);
+
 cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_weight_rotquant(int rot, bool w_bf16, int mode, const RotQuantArgs& a, cudaStream_t st);
 cudaError_t launch_unpack_int4(const void* src, int64_t n_bytes, void* dst, cudaStream_t st);
 // pdl: launch with programmatic stream serialization (the fused linears, whose previous kernel in the stream is
 // their own activation kernel): the GEMM's prologue overlaps that kernel's tail
+struct OutOp;
+// op: an output operation (GELU-tanh, gated residual) in the epilogue, or null / OUT_PLAIN for the plain output
 int launch_gemm_rowcol(const int8_t* a, int a_kperm, const float* sa, const void* b, int b_format, const float* sb,
-                       const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl = false);
+                       const void* bias, void* out, int M, int N, int K, cudaStream_t st, bool pdl = false,
+                       const OutOp* op = nullptr);
 int launch_gemm_rowcol_glu(const int8_t* a, const float* sa, const void* b, const float* sb, const void* bias,
                            void* out, int M, int N, int K, cudaStream_t st, bool pdl = false);
 constexpr int kMaxOutBuffers = 8;   // output buffers of one column-parallel affine launch

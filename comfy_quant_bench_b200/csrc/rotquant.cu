@@ -902,6 +902,15 @@ cudaError_t launch_act_rotquant(int rot, bool swiglu, int mode, const RotQuantAr
   }
   if (mode == MODE_ACT_INT4_ROW) {
     if (a.rows_pad == 0) return cudaSuccess;
+    if (a.ln_shift != nullptr) {                    // modulated layer norm prologue (callers check act8_fits)
+      if (!act8_fits(a)) return cudaErrorInvalidValue;
+      switch (rot) {
+        case 0: return launch_act8<0, true, 7>(a, st);
+        case 16: return launch_act8<16, true, 7>(a, st);
+        case 64: return launch_act8<64, true, 7>(a, st);
+        default: return launch_act8<256, true, 7>(a, st);
+      }
+    }
     // int4 values as int8 codes (the W4A4 GEMM's operand) or as packed nibbles (the reference's format)
     if (act8_fits(a)) return launch_act8_rot<7, false>(rot, a, st);
     return launch_rq_rot<__nv_bfloat16, false, MODE_ACT_INT4_ROW>(rot, a, st);

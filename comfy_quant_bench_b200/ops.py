@@ -597,11 +597,6 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
     (an in-place residual update)."""
     if group_size != 128:
         raise ValueError("the W4A8 affine kernel supports group_size 128")
-    kinds = {"plain": _lib.CQ_OUT_PLAIN, "gelu": _lib.CQ_OUT_GELU_TANH, "gated": _lib.CQ_OUT_GATED_RESIDUAL}
-    if out_op not in kinds:
-        raise ValueError(f"out_op must be one of {sorted(kinds)}")
-    if (shift is None) != (scale is None):
-        raise ValueError("shift and scale go together")
     k = x.shape[-1]
     if k != qweight.shape[-1] * 2:
         raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
@@ -609,7 +604,25 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
     dev = _require_cuda(x, qweight, wscale, zeros_prepared, bias, shift, scale, residual, gate, out)
     x2 = _as2d(x)
     m = x2.shape[0]
+    op, keep, out, sh, sc = _op_args(out_op, residual, gate, shift, scale, out, m, n, k, dev)
+    ws = _workspace(m, k, dev, n)
+    wp, wn = _ws_ptr(ws)
+    _lib.call("cq_linear_w4a8_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc), float(eps),
+              _ptr(qweight.contiguous()), _ptr(wscale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
+              int(group_size), _ptr(_bias_bf16(bias)), ctypes.byref(op), _ptr(out), wp, wn, _stream(dev))
+    return out.reshape(*x.shape[:-1], n)
+
+
+def _op_args(out_op, residual, gate, shift, scale, out, m: int, n: int, k: int, dev):
+    """The output operation struct of the op linears (and the tensors its pointers refer to, kept alive by the
+    caller), the output buffer, and the modulation vectors as bf16 [K]."""
+    kinds = {"plain": _lib.CQ_OUT_PLAIN, "gelu": _lib.CQ_OUT_GELU_TANH, "gated": _lib.CQ_OUT_GATED_RESIDUAL}
+    if out_op not in kinds:
+        raise ValueError(f"out_op must be one of {sorted(kinds)}")
+    if (shift is None) != (scale is None):
+        raise ValueError("shift and scale go together")
     op = _lib.CQOutOp(kinds[out_op], None, 0, None)
+    keep = []
     if out_op == "gated":
         if residual is None or gate is None:
             raise ValueError("the gated residual needs residual and gate")
@@ -619,18 +632,64 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
         if r2.stride(1) != 1:
             raise ValueError("residual rows must be contiguous")
         g = _vec_bf16(gate, n, "gate")
+        keep += [r2, g]
         op.residual, op.residual_ld, op.gate = _ptr(r2), r2.stride(0), _ptr(g)
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     elif out.dtype != torch.bfloat16 or out.numel() != m * n or not out.is_contiguous():
         raise ValueError(f"out must be contiguous bf16 with {m} x {n} elements")
-    ws = _workspace(m, k, dev, n)
-    wp, wn = _ws_ptr(ws)
     sh = _vec_bf16(shift, k, "shift") if shift is not None else None
     sc = _vec_bf16(scale, k, "scale") if scale is not None else None
-    _lib.call("cq_linear_w4a8_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc), float(eps),
-              _ptr(qweight.contiguous()), _ptr(wscale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),
-              int(group_size), _ptr(_bias_bf16(bias)), ctypes.byref(op), _ptr(out), wp, wn, _stream(dev))
+    return op, keep, out, sh, sc
+
+
+def convrot_w4a4_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor,
+                           bias: torch.Tensor | None = None, *, out_op: str = "plain",
+                           residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                           shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+                           convrot_groupsize: int = 256, linear_dtype: str = "int4", eps: float = 1e-6,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``convrot_w4a4_linear`` with the elementwise step after it in the GEMM's epilogue and, with ``shift`` and
+    the modulation ``scale``, the modulated layer norm bf16(shift + bf16(layer_norm(x)) * bf16(1 + scale)) formed in
+    the activation kernel; ``out_op``, ``residual``, ``gate`` and ``out`` as in ``w4a8_affine_linear_op``."""
+    if linear_dtype not in {"int4", "int8"}:
+        raise ValueError(f"ConvRot W4A4 linear_dtype must be 'int4' or 'int8', got {linear_dtype!r}")
+    k = x.shape[-1]
+    if k != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={k} does not match qweight K={qweight.shape[-1] * 2}")
+    n = qweight.shape[0]
+    dev = _require_cuda(x, qweight, wscales, bias, shift, scale, residual, gate, out)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    op, keep, out, sh, sc = _op_args(out_op, residual, gate, shift, scale, out, m, n, k, dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    _lib.call("cq_linear_convrot_w4a4_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize),
+              4 if linear_dtype == "int4" else 8, _ptr(sh), _ptr(sc), float(eps), _ptr(qweight.contiguous()),
+              _ptr(wscales.float().reshape(-1).contiguous()), _ptr(_bias_bf16(bias)), ctypes.byref(op), _ptr(out),
+              wp, wn, _stream(dev))
+    return out.reshape(*x.shape[:-1], n)
+
+
+def int8_linear_op(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                   *, out_op: str = "plain", residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                   shift: torch.Tensor | None = None, scale: torch.Tensor | None = None, convrot: bool = False,
+                   convrot_groupsize: int = 256, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``int8_linear`` with the elementwise step after it in the GEMM's epilogue and the optional modulated layer
+    norm in the activation kernel (as ``convrot_w4a4_linear_op``)."""
+    k = x.shape[-1]
+    if weight.dtype != torch.int8 or weight.shape[-1] != k:
+        raise ValueError(f"weight must be int8 [N, {k}]")
+    n = weight.shape[0]
+    dev = _require_cuda(x, weight, weight_scale, bias, shift, scale, residual, gate, out)
+    x2 = _as2d(x)
+    m = x2.shape[0]
+    op, keep, out, sh, sc = _op_args(out_op, residual, gate, shift, scale, out, m, n, k, dev)
+    ws = _workspace(m, k, dev)
+    wp, wn = _ws_ptr(ws)
+    _lib.call("cq_linear_w8a8_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize if convrot else 0), _ptr(sh),
+              _ptr(sc), float(eps), _ptr(weight.contiguous()), _ptr(weight_scale.float().reshape(-1).contiguous()),
+              _ptr(_bias_bf16(bias)), ctypes.byref(op), _ptr(out), wp, wn, _stream(dev))
     return out.reshape(*x.shape[:-1], n)
 
 
@@ -668,6 +727,36 @@ def qkv_rmsnorm_rope(y: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor
     qn, kn = q_norm.to(torch.bfloat16).contiguous(), k_norm.to(torch.bfloat16).contiguous()
     _lib.call("cq_qkv_rmsnorm_rope_layout", _ptr(y2), s, h, d, _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(q),
               _ptr(k), _ptr(v), s_all, int(s0), token_major, _stream(dev))
+
+
+def rmsnorm_rope_rows(x: torch.Tensor, weight: torch.Tensor, rope: torch.Tensor | None = None, head_dim: int = 128,
+                      eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over whole rows of x [S, C] (bf16; a Wan-style q/k norm over the hidden dim), weight [C], one bf16
+    rounding, then with ``rope`` ([S, D/2] complex64 or its real view [S, D/2, 2]) each head_dim-wide head's
+    interleaved pairs rotated, as torch's rms_norm followed by the complex-multiply rotary embedding.  ``out`` may
+    be x."""
+    dev = _require_cuda(x, weight, rope, out)
+    x2 = _as2d(x)
+    if x2.dtype != torch.bfloat16 or not x2.is_contiguous():
+        raise ValueError("x must be contiguous bf16")
+    s, c = x2.shape
+    w = weight.to(torch.bfloat16).contiguous()
+    if w.numel() != c:
+        raise ValueError(f"weight must have {c} elements")
+    rp = None
+    if rope is not None:
+        if rope.is_complex():
+            rope = torch.view_as_real(rope)
+        rp = rope.to(torch.float32).contiguous()
+        if tuple(rp.shape) != (s, head_dim // 2, 2):
+            raise ValueError(f"rope must be [{s}, {head_dim // 2}] complex (or [{s}, {head_dim // 2}, 2] real)")
+    if out is None:
+        out = torch.empty_like(x2)
+    elif out.shape != x2.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be contiguous bf16 of x's shape")
+    _lib.call("cq_rmsnorm_rope_rows", _ptr(x2), s, c, _ptr(w), float(eps), _ptr(rp), int(head_dim), _ptr(out),
+              _stream(dev))
+    return out.reshape(x.shape)
 
 
 def _out_ptrs(outs, rows: int, ldo: int):

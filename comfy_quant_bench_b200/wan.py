@@ -14,7 +14,10 @@ int8 activations).  The block follows the public Wan 2.x layout:
     x = x + gate_ff * W2 gelu_tanh(W1 (LayerNorm(x) * (1 + scale_ff) + shift_ff))
 
 The per-block modulation vectors (shift/scale/gate) are drawn at random, standing in for the model's time
-embedding.  Norms, rotary embedding, attention and GELU are torch ops.  ``step(..., reference=True)`` replaces
+embedding.  On the kernel path (``fused_glue``) the q/k RMSNorm and the rotary embedding run as one library
+kernel per tensor (``ops.rmsnorm_rope_rows``), the modulated layer norms inside the activation kernels of the QKV
+and MLP-up linears, and GELU and the residual updates in the GEMM epilogues (``ops.convrot_w4a4_linear_op`` /
+``ops.int8_linear_op``); the affine layer norm before the cross-attention and the attention itself stay torch ops.  ``step(..., reference=True)`` replaces
 every linear by a torch fp32 product of its dequantized weight and the dequantized activation codes the library's
 own activation kernel produced.
 """
@@ -43,6 +46,9 @@ class WanConfig:
     w4a4_fraction: float = 0.35
     w4a4_rot: int = 64          # Hadamard group of the W4A4 linears
     w8a8_rot: int = 0           # int8_tensorwise without rotation
+    fused_glue: bool = True     # kernel path: q/k RMSNorm (+ rotary) as one library kernel per tensor, the
+                                # modulated layer norms in the activation kernels of the QKV and MLP-up linears, GELU
+                                # and the (gated) residual updates in the GEMM epilogues
 
     @property
     def tokens(self) -> int:
@@ -75,6 +81,11 @@ class W4A4Linear:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return ops.convrot_w4a4_linear(x, self.qweight, self.wscale, self.bias, convrot_groupsize=self.rot)
 
+    def op(self, x: torch.Tensor, out_op: str, **kw) -> torch.Tensor:
+        """This linear with the step after it in the GEMM's epilogue (``ops.convrot_w4a4_linear_op``)."""
+        return ops.convrot_w4a4_linear_op(x, self.qweight, self.wscale, self.bias, out_op=out_op,
+                                          convrot_groupsize=self.rot, **kw)
+
     def reference(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
         q, sx, _ = ops.rotquant(x2, self.rot, _lib.CQ_ACT_INT4_ROW, int4_as_int8=True)
@@ -101,6 +112,11 @@ class W8A8Linear:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return ops.int8_linear(x, self.qweight, self.wscale, self.bias, convrot=self.rot > 0,
                                convrot_groupsize=max(self.rot, 16))
+
+    def op(self, x: torch.Tensor, out_op: str, **kw) -> torch.Tensor:
+        """This linear with the step after it in the GEMM's epilogue (``ops.int8_linear_op``)."""
+        return ops.int8_linear_op(x, self.qweight, self.wscale, self.bias, out_op=out_op, convrot=self.rot > 0,
+                                  convrot_groupsize=max(self.rot, 16), **kw)
 
     def reference(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
@@ -168,6 +184,7 @@ class WanDiT:
         nb = len(_Block.NAMES)
         self.blocks = [_Block(gen, self.device, cfg, kinds[b * nb:(b + 1) * nb]) for b in range(cfg.blocks)]
         self.rope = _rope3d(cfg, self.device)
+        self.one = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=self.device)
 
     def linears(self):
         return [l for b in self.blocks for l in b.lin.values()]
@@ -178,6 +195,11 @@ class WanDiT:
     def plan(self) -> dict:
         ls = self.linears()
         return {"w4a4": sum(l.kind == "w4a4" for l in ls), "w8a8": sum(l.kind == "w8a8" for l in ls)}
+
+    def launches_per_step(self) -> int:
+        """The library's kernel launches in one kernel-path step: an activation kernel and a GEMM per linear, and
+        with the fused glue the q/k norm kernel for q, k and the cross-attention's q, k."""
+        return 2 * len(self.linears()) + (4 * self.cfg.blocks if self.cfg.fused_glue else 0)
 
     def linear_int_ops(self) -> float:
         c = self.cfg
@@ -216,18 +238,29 @@ class WanDiT:
         def lin(l, t):
             return l.reference(t) if reference else l(t)
 
+        fused = c.fused_glue and not reference
+
+        def norm(t, w, rope):
+            """RMSNorm over the hidden dim (then the rotary embedding): one library kernel, in place, on the kernel
+            path; torch rms_norm and the complex multiply on the reference path."""
+            if fused:
+                return ops.rmsnorm_rope_rows(t, w, rope, d, eps=1e-6, out=t).view(-1, nh, d)
+            t = F.rms_norm(t, (h,), w, eps=1e-6).view(-1, nh, d)
+            return _rope(t, rope) if rope is not None else t
+
         m = b.mod
+        if fused:
+            return self._block_fused(b, x, ctx, norm)
         y = torch.addcmul(m[0], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[1])
-        q = F.rms_norm(lin(b.lin["q"], y), (h,), b.norm_q, eps=1e-6).view(s, nh, d)
-        k = F.rms_norm(lin(b.lin["k"], y), (h,), b.norm_k, eps=1e-6).view(s, nh, d)
+        q = norm(lin(b.lin["q"], y), b.norm_q, self.rope)
+        k = norm(lin(b.lin["k"], y), b.norm_k, self.rope)
         v = lin(b.lin["v"], y).view(s, nh, d)
-        q, k = _rope(q, self.rope), _rope(k, self.rope)
         a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
                                            v.transpose(0, 1)[None])[0].transpose(0, 1).reshape(s, h)
         x = torch.addcmul(x, m[2], lin(b.lin["o"], a))
         y = F.layer_norm(x, (h,), b.norm3_w, b.norm3_b, eps=1e-6)
-        cq = F.rms_norm(lin(b.lin["cq"], y), (h,), b.norm_cq, eps=1e-6).view(s, nh, d)
-        ck = F.rms_norm(lin(b.lin["ck"], ctx), (h,), b.norm_ck, eps=1e-6).view(-1, nh, d)
+        cq = norm(lin(b.lin["cq"], y), b.norm_cq, None)
+        ck = norm(lin(b.lin["ck"], ctx), b.norm_ck, None)
         cv = lin(b.lin["cv"], ctx).view(-1, nh, d)
         a = F.scaled_dot_product_attention(cq.transpose(0, 1)[None], ck.transpose(0, 1)[None],
                                            cv.transpose(0, 1)[None])[0].transpose(0, 1).reshape(s, h)
@@ -235,6 +268,31 @@ class WanDiT:
         y = torch.addcmul(m[3], F.layer_norm(x, (h,), eps=1e-6), 1.0 + m[4])
         x = torch.addcmul(x, m[5], lin(b.lin["ff2"], F.gelu(lin(b.lin["ff1"], y), approximate="tanh")))
         return x
+
+    def _block_fused(self, b: "_Block", x: torch.Tensor, ctx: torch.Tensor, norm) -> torch.Tensor:
+        """The kernel path's block: the modulated layer norms inside the QKV and MLP-up activation kernels, the q/k
+        norm + rotary kernel, GELU and the residual updates in the GEMM epilogues (the cross-attention residual as a
+        gated residual with gate 1: bf16(x + y), torch's bf16 add)."""
+        c = self.cfg
+        h, nh, d = c.hidden, c.heads, c.head_dim
+        s = x.shape[0]
+        m = b.mod
+        L = b.lin
+        q = norm(L["q"].op(x, "plain", shift=m[0], scale=m[1]), b.norm_q, self.rope)
+        k = norm(L["k"].op(x, "plain", shift=m[0], scale=m[1]), b.norm_k, self.rope)
+        v = L["v"].op(x, "plain", shift=m[0], scale=m[1]).view(s, nh, d)
+        a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                           v.transpose(0, 1)[None])[0].transpose(0, 1).reshape(s, h)
+        x = L["o"].op(a, "gated", residual=x, gate=m[2])
+        y = F.layer_norm(x, (h,), b.norm3_w, b.norm3_b, eps=1e-6)
+        cq = norm(L["cq"](y), b.norm_cq, None)
+        ck = norm(L["ck"](ctx), b.norm_ck, None)
+        cv = L["cv"](ctx).view(-1, nh, d)
+        a = F.scaled_dot_product_attention(cq.transpose(0, 1)[None], ck.transpose(0, 1)[None],
+                                           cv.transpose(0, 1)[None])[0].transpose(0, 1).reshape(s, h)
+        x = L["co"].op(a, "gated", residual=x, gate=self.one)
+        g = L["ff1"].op(x, "gelu", shift=m[3], scale=m[4])
+        return L["ff2"].op(g, "gated", residual=x, gate=m[5])
 
     def inputs(self, seed: int = 1):
         c = self.cfg

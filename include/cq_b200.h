@@ -237,8 +237,9 @@ CQ_API int cq_gemm_affine(const int8_t* a, int a_kperm, const float* sa, const v
                           int64_t K, int group, void* stream);
 
 /*
- * The elementwise step that follows a DiT block's linear, applied by the W4A8 affine GEMM to its bf16 result
- * before the store.  y = the bf16 output cq_gemm_affine writes for the same inputs; then
+ * The elementwise step that follows a DiT block's linear, applied by the W4A8 affine GEMM (and the row/col GEMM of
+ * cq_linear_convrot_w4a4_op / cq_linear_w8a8_op) to its bf16 result before the store.  y = the bf16 output the plain
+ * GEMM writes for the same inputs; then
  *   CQ_OUT_PLAIN            out = y
  *   CQ_OUT_GELU_TANH        out = bf16(gelu_tanh(y)),  gelu_tanh(y) = y / (1 + exp(-2 sqrt(2/pi) (y + 0.044715 y^3)))
  *                           (torch F.gelu(y, approximate="tanh"), the MLP-up activation; the sigmoid form of
@@ -299,6 +300,24 @@ CQ_API int cq_linear_w4a8_affine(const void* x, int64_t M, int64_t K, int64_t N,
 CQ_API int cq_linear_w8a8(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int swiglu, const int8_t* weight,
                    const float* wscale, const void* bias, void* out, void* workspace, int64_t workspace_bytes,
                    void* stream);
+/*
+ * cq_linear_convrot_w4a4_op / cq_linear_w8a8_op: the same linears (no SwiGLU input) with the output operation `op`
+ * (cq_out_op, NULL: CQ_OUT_PLAIN) applied in the row/col GEMM's epilogue to its bf16 result, and, when shift is not
+ * NULL, the activation stage quantizing the modulated layer norm
+ *   xn = bf16( shift + bf16( (x - mean) * rsqrt(var + eps) ) * bf16(1 + mod_scale) )
+ * per token over its K columns (shift, mod_scale bf16 [K], 16-byte aligned; K % 256 == 0, K <= 24576) instead of
+ * x: a Wan-style DiT block's norm + modulation before its QKV and MLP-up linears, its GELU after MLP-up and its
+ * gated residuals after the attention-output and MLP-down linears.  The operations need N % 8 == 0 and a 16-byte
+ * aligned output.  No counterpart in the reference, whose model code runs these as torch ops.
+ */
+CQ_API int cq_linear_convrot_w4a4_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, int act_bits,
+                                     const void* shift, const void* mod_scale, float eps, const void* qweight,
+                                     const float* wscale, const void* bias, const cq_out_op* op, void* out,
+                                     void* workspace, int64_t workspace_bytes, void* stream);
+CQ_API int cq_linear_w8a8_op(const void* x, int64_t M, int64_t K, int64_t N, int rot_group, const void* shift,
+                             const void* mod_scale, float eps, const int8_t* weight, const float* wscale,
+                             const void* bias, const cq_out_op* op, void* out, void* workspace,
+                             int64_t workspace_bytes, void* stream);
 
 /*
  * W4A4 row/col GEMM / ConvRot W4A4 linear with the SwiGLU output fused into the epilogue
@@ -420,6 +439,16 @@ CQ_API int cq_heads_to_rows(const void* o, int64_t S, int Hp, int D, void* const
 CQ_API int cq_qkv_rmsnorm_rope(const void* y, int64_t S, int H, int D, const void* q_norm, const void* k_norm,
                                float eps, const float* rope, void* q, void* k, void* v, int64_t s_all, int64_t s0,
                                void* stream);
+/*
+ * cq_rmsnorm_rope_rows: out[s, :] = rope(bf16(x[s, :] * rsqrt(mean(x[s, :]^2) + eps) * w)) for bf16 rows x [S, C]:
+ * RMSNorm over the whole row (a Wan-style q/k norm over the hidden dim) in fp32, one bf16 rounding; then, when rope
+ * is not null, each D-wide head's interleaved pairs (x[2p], x[2p+1]) rotated by rope[s, p] = (cos, sin) (f32
+ * [S, D/2, 2]) in fp32 and rounded to bf16.  w bf16 [C].  out may be x.  C % 8 == 0, C <= 16384; with rope,
+ * D = 64 or 128 and C % D == 0.  x, w, out 16-byte aligned.  No counterpart in the reference (its model code runs
+ * rms_norm, a float copy, a complex multiply and a bf16 copy).
+ */
+CQ_API int cq_rmsnorm_rope_rows(const void* x, int64_t S, int C, const void* w, float eps, const float* rope, int D,
+                                void* out, void* stream);
 CQ_API int cq_qkv_rmsnorm_rope_layout(const void* y, int64_t S, int H, int D, const void* q_norm,
                                       const void* k_norm, float eps, const float* rope, void* q, void* k, void* v,
                                       int64_t s_all, int64_t s0, int token_major, void* stream);

@@ -130,6 +130,14 @@ def test_dit_glue_argument_checks_need_no_device(lib):
     assert lib.cq_qkv_rmsnorm_rope(vp, 0, 4, 128, None, None, f, None, None, None, None, 10, 4, None) == _lib.CQ_OK
     assert lib.cq_qkv_rmsnorm_rope_layout(vp, 8, 4, 128, vp, vp, f, vp, vp, vp, vp, 8, 0, 2, None) == _lib.CQ_ERR_ARG
     assert lib.cq_qkv_rmsnorm_rope_layout(vp, 8, 4, 96, vp, vp, f, vp, vp, vp, vp, 8, 0, 1, None) == _lib.CQ_ERR_SHAPE
+    # row RMSNorm + rotary: C a multiple of 8 up to 16384; with a rope table, head dim 64 or 128 dividing C
+    assert lib.cq_rmsnorm_rope_rows(vp, 4, 1004, vp, f, None, 128, vp, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_rmsnorm_rope_rows(vp, 4, 32768, vp, f, None, 128, vp, None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_rmsnorm_rope_rows(vp, 4, 3072, vp, f, ctypes.cast(vp, ctypes.POINTER(ctypes.c_float)), 96, vp,
+                                    None) == _lib.CQ_ERR_SHAPE
+    assert lib.cq_rmsnorm_rope_rows(vp, 4, 3072, vp, ctypes.c_float(-1.0), None, 128, vp, None) == _lib.CQ_ERR_ARG
+    assert lib.cq_rmsnorm_rope_rows(ctypes.c_void_p(24), 4, 3072, vp, f, None, 128, vp, None) == _lib.CQ_ERR_ALIGN
+    assert lib.cq_rmsnorm_rope_rows(None, 0, 3072, None, f, None, 128, None, None) == _lib.CQ_OK
     # head gather: 1..8 buffers, 16-byte aligned, columns inside the rows
     outs = (ctypes.c_void_p * 2)(16, 32)
     assert lib.cq_heads_to_rows(vp, 8, 4, 128, outs, 0, 0, 512, None) == _lib.CQ_ERR_ARG

@@ -101,6 +101,40 @@ def test_qkv_token_major_equals_head_major_and_attention_output_is_rows(ops):
     assert (got - rows).abs().max().item() <= 2.0 ** -6 * rows.abs().max().item()
 
 
+@pytest.mark.parametrize("s,c,d,with_rope,in_place", [(300, 3072, 128, True, False), (300, 3072, 128, False, True),
+                                                        (37, 5120, 128, True, True), (9, 512, 64, True, False),
+                                                        (5, 16384, 128, False, False)])
+def test_rmsnorm_rope_rows_matches_torch(ops, s, c, d, with_rope, in_place):
+    """RMSNorm over whole rows (Wan's q/k norm over the hidden dim) then the rotary embedding, against torch's
+    rms_norm and the complex multiply: within one bf16 rounding."""
+    g = torch.Generator(device="cuda").manual_seed(s + c)
+    x = (torch.randn(s, c, generator=g, device="cuda") * 3.0).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(c, generator=g, device="cuda")).to(torch.bfloat16)
+    rot = _rope_table(s, d, 5, "cuda") if with_rope else None
+    want = F.rms_norm(x, (c,), w, eps=1e-6)
+    if with_rope:
+        want = _torch_rope(want.view(s, c // d, d), rot).view(s, c)
+    src = x.clone()
+    got = ops.rmsnorm_rope_rows(src, w, rot, d, eps=1e-6, out=src if in_place else None)
+    _status_clear()
+    if in_place:
+        assert got.data_ptr() == src.data_ptr()
+    _within_one_rounding(got, want)
+
+
+def test_rmsnorm_rope_rows_rejects_bad_arguments(ops):
+    from comfy_quant_bench_b200 import _lib
+    w = torch.ones(1004, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.CQShapeError):          # C not a multiple of 8
+        ops.rmsnorm_rope_rows(torch.zeros(4, 1004, dtype=torch.bfloat16, device="cuda"), w)
+    w = torch.ones(3072, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):                  # rope table of the wrong length
+        ops.rmsnorm_rope_rows(torch.zeros(4, 3072, dtype=torch.bfloat16, device="cuda"), w,
+                              torch.zeros(5, 64, 2, device="cuda"), 128)
+    with pytest.raises(ValueError):                  # weight length
+        ops.rmsnorm_rope_rows(torch.zeros(4, 3072, dtype=torch.bfloat16, device="cuda"), w[:100])
+
+
 def test_qkv_rejects_mixed_layouts(ops):
     s, h, d = 16, 2, 64
     y = torch.zeros(s, 3 * h * d, dtype=torch.bfloat16, device="cuda")
@@ -329,3 +363,82 @@ def test_split_k_linear_matches_the_unsplit_gemm(ops, m, n, k, out_op):
     a, b = y1.float(), want.float()
     assert bool(((a - b).abs() <= b.abs() * 2.0 ** -7 + 1e-6).all()), float(((a - b).abs() - b.abs() * 2.0 ** -7).max())
     assert float((y1 != want).float().mean()) <= 0.02
+
+
+# ----------------------------------------------------------------------------------------------
+# output operations and the modulated layer norm on the row/col linears (ConvRot W4A4, W8A8)
+# ----------------------------------------------------------------------------------------------
+
+def _rowcol_layer(ops, kind, n, k, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn(n, k, device="cuda", generator=g) * 0.02
+    bias = (0.01 * torch.randn(n, device="cuda", generator=g)).to(torch.bfloat16)
+    if kind == "w8a8":
+        qw, ws = ops.quantize_int8_convrot_weight(w, 0)
+        return (lambda x: ops.int8_linear(x, qw, ws, bias),
+                lambda x, out_op, **kw: ops.int8_linear_op(x, qw, ws, bias, out_op=out_op, **kw))
+    qw, ws = ops.quantize_convrot_w4a4_weight(w, 64)
+    dt = "int4" if kind == "w4a4" else "int8"
+    return (lambda x: ops.convrot_w4a4_linear(x, qw, ws, bias, convrot_groupsize=64, linear_dtype=dt),
+            lambda x, out_op, **kw: ops.convrot_w4a4_linear_op(x, qw, ws, bias, out_op=out_op, convrot_groupsize=64,
+                                                               linear_dtype=dt, **kw))
+
+
+_ROWCOL_SHAPES = [(4096, 3072, 3072), (300, 384, 1024), (77, 416, 1024), (33, 264, 512)]
+
+
+@pytest.mark.parametrize("kind", ["w4a4", "w4a4_int8act", "w8a8"])
+@pytest.mark.parametrize("m,n,k", _ROWCOL_SHAPES)
+def test_rowcol_output_ops_match_torch(ops, gemm_variant, kind, m, n, k):
+    """The row/col linears' epilogue operations on y, the plain linear's bf16 output: plain is y bit for bit, GELU
+    is F.gelu(y, approximate="tanh") within one bf16 rounding, the gated residual is torch.addcmul(residual, gate, y)
+    but at bf16 rounding ties (also in place, bit-identical)."""
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    plain, op = _rowcol_layer(ops, kind, n, k, seed=n + 3)
+    y = plain(x)
+    assert torch.equal(op(x, "plain"), y)
+    got = op(x, "gelu")
+    res = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    gate = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
+    gated = op(x, "gated", residual=res, gate=gate)
+    inplace = res.clone()
+    op(x, "gated", residual=inplace, gate=gate, out=inplace)
+    _status_clear()
+    want_gelu = F.gelu(y, approximate="tanh")
+    _within_one_rounding(got, want_gelu)
+    assert float((got != want_gelu).float().mean()) <= 2e-3
+    want = torch.addcmul(res, gate, y)
+    gf, wf = gated.float(), want.float()
+    assert bool(((gf - wf).abs() <= wf.abs() * 2.0 ** -7 + 1e-30).all())
+    assert float((gated != want).float().mean()) <= 1e-4
+    assert torch.equal(inplace, gated)
+
+
+@pytest.mark.parametrize("kind", ["w4a4", "w8a8"])
+def test_rowcol_lnmod_prologue_matches_composite(ops, gemm_variant, kind):
+    """The modulated layer norm formed in the activation kernel of a row/col linear, against the plain linear of
+    torch's composite bf16(shift + bf16(layer_norm(x)) * bf16(1 + scale)): the activation codes may differ by one
+    where the composite's two bf16 roundings land differently, so the outputs agree to rel-L2 1e-3."""
+    m, k, n = 1024, 3072, 3072
+    x, shift, _ = _lnmod_inputs(m, k, seed=21)
+    scale = (0.3 * torch.randn(k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(22))).to(torch.bfloat16)
+    plain, op = _rowcol_layer(ops, kind, n, k, seed=23)
+    want = plain(_torch_lnmod(x, shift, 1.0 + scale))
+    got = op(x, "plain", shift=shift, scale=scale)
+    got_gelu = op(x, "gelu", shift=shift, scale=scale)
+    _status_clear()
+    from comfy_quant_bench_b200.mmdit import rel_l2
+    assert rel_l2(got, want) <= 1e-3
+    _within_one_rounding(got_gelu, F.gelu(got, approximate="tanh"))
+
+
+def test_rowcol_op_rejects_bad_arguments(ops):
+    plain, op = _rowcol_layer(ops, "w8a8", 264, 512, seed=1)
+    x = torch.zeros(8, 512, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        op(x, "gated")                                   # no residual / gate
+    with pytest.raises(ValueError):
+        op(x, "relu")
+    with pytest.raises(ValueError):
+        op(x, "plain", shift=torch.zeros(512, dtype=torch.bfloat16, device="cuda"))   # shift without scale
