@@ -39,9 +39,6 @@ CQ_B_INT8 = 1
 CQ_GEMM_AUTO = 0
 CQ_GEMM_ONE_SM = 1
 CQ_GEMM_PAIR = 2
-CQ_ACT_AUTO = 0
-CQ_ACT_WAVES = 1
-CQ_ACT_STAGED = 2
 
 CQ_OUT_PLAIN = 0
 CQ_OUT_GELU_TANH = 1
@@ -66,7 +63,6 @@ SIGNATURES = {
     "cq_version": (ctypes.c_char_p, []),
     "cq_status_string": (ctypes.c_char_p, [_int]),
     "cq_set_gemm_variant": (_int, [_int]),
-    "cq_set_act_variant": (_int, [_int]),
     "cq_take_device_status": (_int, [ctypes.POINTER(_int), _vp]),
     "cq_selftest_bounded_wait": (_int, [_vp]),
     "cq_rotquant": (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _i64, _int, _vp, _vp, _vp, _vp]),
@@ -170,11 +166,6 @@ def exported_symbols() -> list[str]:
 def set_gemm_variant(variant: int) -> None:
     """Process-wide kernel form of the packed-int4-weight GEMMs (CQ_GEMM_AUTO, CQ_GEMM_ONE_SM, CQ_GEMM_PAIR)."""
     call("cq_set_gemm_variant", int(variant))
-
-
-def set_act_variant(variant: int) -> None:
-    """Process-wide kernel form of the per-token activation kernels (CQ_ACT_AUTO, CQ_ACT_WAVES, CQ_ACT_STAGED)."""
-    call("cq_set_act_variant", int(variant))
 
 
 def take_device_status(stream=None) -> tuple[int, int]:

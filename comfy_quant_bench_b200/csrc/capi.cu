@@ -67,8 +67,6 @@ int cq_take_device_status(int* status, void* stream) {
 
 int cq_set_gemm_variant(int variant) { return cq::set_gemm_variant(variant); }
 
-int cq_set_act_variant(int variant) { return cq::set_act_variant(variant); }
-
 int cq_selftest_bounded_wait(void* stream) {
   if (int dv = check_device()) return dv;
   return cuda_status(cq::launch_selftest_wait(static_cast<cudaStream_t>(stream)));

@@ -198,13 +198,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory into this CTA's
-// shared memory, completing on the mbarrier at `bar` (shared-memory addresses).  No multicast.
-__device__ __forceinline__ void bulk_load_g2s(uint32_t smem_dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(smem_dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar) : "memory");
-}
-
 // TMA tensor store (2-D) from shared memory into global memory, tracked by this thread's bulk-async groups.
 // Coordinates are element indices into the tensor map (never negative here); out-of-range parts are clipped.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {

@@ -117,8 +117,6 @@ int launch_gemm_intratio(const int8_t* a, int a_kperm, const float* sa, const vo
                          int cw_u8, int cw_group, const void* bias, void* out, int M, int N, int K, cudaStream_t st);
 // process-wide kernel choice for the packed-int4-weight GEMMs (cq_gemm_variant values)
 int set_gemm_variant(int variant);
-// process-wide kernel choice for the per-token activation kernels (cq_act_variant values)
-int set_act_variant(int variant);
 // failure-path self-test: two waits on mbarriers nothing arrives on; sites kSelftestSite and kSelftestSite + 1
 constexpr int kSelftestSite = 90;
 cudaError_t launch_selftest_wait(cudaStream_t st);

@@ -12,11 +12,6 @@
 //     shared-memory tile (conflict-free 16-byte and 4-byte phases), runs the two stages in registers and
 //     transposes back.
 // Quantization then runs in the load layout, so every store is a contiguous 16-, 8- or 4-byte vector.
-#include <algorithm>
-#include <map>
-#include <mutex>
-#include <tuple>
-
 #include "kernels.cuh"
 
 namespace cq {
@@ -371,7 +366,6 @@ constexpr int kStageRow = 48;           // bytes per staged 16-column chunk (32 
 constexpr int kStageBlock = 16 * kStageRow + 32;   // second 256-column block: banks shifted by 8
 constexpr int kMaxTeamWarps = 16;
 constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
-constexpr unsigned long long kDrainNs = 50000000ull;   // wait for a copy in flight while unwinding (50 ms)
 }  // namespace act8
 
 __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
@@ -600,30 +594,27 @@ __device__ __forceinline__ float2 bf16x2_round(float2 v) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
 }
 
-// 16 bytes of input at p: a read-only global load, or a shared-memory load when the pair was staged there
-template <bool SMEM>
-__device__ __forceinline__ uint4 act8_ld16(const __nv_bfloat16* p) {
-  if constexpr (SMEM) return *reinterpret_cast<const uint4*>(p);
-  else return __ldg(reinterpret_cast<const uint4*>(p));
-}
-
-// One token pair (rows rA, rA + 1) of the per-token activation kernels: xa, xb point at the two rows, in global
-// memory or (SMEM) in a shared-memory stage that holds them.  Every thread of the CTA calls it (it holds CTA
-// barriers); `tile` is the warp's transpose tile.  after_load() runs, on every thread, once the pair is in
-// registers.
-template <int ROT, int PASSES, bool LNMOD, int QMAX, bool SWIGLU, bool SMEM, typename AfterLoad>
-__device__ __forceinline__ void act8_pair(const RotQuantArgs& args, int64_t rA, const __nv_bfloat16* xa,
-                                          const __nv_bfloat16* xb, unsigned char* tile,
-                                          float (&red)[2][act8::kMaxTeamWarps],
-                                          float (&red_ln)[2][2][act8::kMaxTeamWarps], AfterLoad after_load) {
+template <int ROT, int PASSES, bool LNMOD, int QMAX, bool SWIGLU>
+__global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
   static_assert(!(LNMOD && SWIGLU), "one prologue at a time");
+  // the GEMM that consumes these codes may be scheduled as soon as every CTA of this grid runs (its prologue then
+  // overlaps this kernel's tail; it waits for this grid's completion before reading anything)
+  grid_dep_launch();
+  extern __shared__ __align__(16) unsigned char act8_smem[];
+  __shared__ float red[2][act8::kMaxTeamWarps];
+  __shared__ float red_ln[2][2][act8::kMaxTeamWarps];   // layer-norm prologue: sums, then centered squares
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int K = args.K;
   const int nchunks = (K + 511) >> 9;
+  const int64_t rA = 2 * static_cast<int64_t>(blockIdx.x);
   const bool liveA = rA < args.rows, liveB = rA + 1 < args.rows, storeB = rA + 1 < args.rows_pad;
+  unsigned char* tile = act8_smem + warp * act8::kTileBytes;
   const int h = lane >> 4;
 
   float2 v[PASSES][16];
+  const int64_t ld = SWIGLU ? 2 * static_cast<int64_t>(K) : K;   // SwiGLU rows are [gate | up], 2K wide
+  const __nv_bfloat16* xa = static_cast<const __nv_bfloat16*>(args.x) + rA * ld;
+  const __nv_bfloat16* xb = xa + ld;
 #pragma unroll
   for (int s = 0; s < PASSES; ++s) {
     const int j = warp + s * nwarps;
@@ -635,12 +626,12 @@ __device__ __forceinline__ void act8_pair(const RotQuantArgs& args, int64_t rA, 
 #pragma unroll
       for (int i = 0; i < 8; ++i) r[i] = make_uint4(0, 0, 0, 0);
       if (valid && liveA) {
-        r[0] = act8_ld16<SMEM>(xa + e); r[1] = act8_ld16<SMEM>(xa + e + 8);
-        r[2] = act8_ld16<SMEM>(xa + K + e); r[3] = act8_ld16<SMEM>(xa + K + e + 8);
+        r[0] = __ldg(reinterpret_cast<const uint4*>(xa + e)); r[1] = __ldg(reinterpret_cast<const uint4*>(xa + e + 8));
+        r[2] = __ldg(reinterpret_cast<const uint4*>(xa + K + e)); r[3] = __ldg(reinterpret_cast<const uint4*>(xa + K + e + 8));
       }
       if (valid && liveB) {
-        r[4] = act8_ld16<SMEM>(xb + e); r[5] = act8_ld16<SMEM>(xb + e + 8);
-        r[6] = act8_ld16<SMEM>(xb + K + e); r[7] = act8_ld16<SMEM>(xb + K + e + 8);
+        r[4] = __ldg(reinterpret_cast<const uint4*>(xb + e)); r[5] = __ldg(reinterpret_cast<const uint4*>(xb + e + 8));
+        r[6] = __ldg(reinterpret_cast<const uint4*>(xb + K + e)); r[7] = __ldg(reinterpret_cast<const uint4*>(xb + K + e + 8));
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -656,8 +647,8 @@ __device__ __forceinline__ void act8_pair(const RotQuantArgs& args, int64_t rA, 
       continue;
     }
     uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
-    if (valid && liveA) { a0 = act8_ld16<SMEM>(xa + e); a1 = act8_ld16<SMEM>(xa + e + 8); }
-    if (valid && liveB) { b0 = act8_ld16<SMEM>(xb + e); b1 = act8_ld16<SMEM>(xb + e + 8); }
+    if (valid && liveA) { a0 = __ldg(reinterpret_cast<const uint4*>(xa + e)); a1 = __ldg(reinterpret_cast<const uint4*>(xa + e + 8)); }
+    if (valid && liveB) { b0 = __ldg(reinterpret_cast<const uint4*>(xb + e)); b1 = __ldg(reinterpret_cast<const uint4*>(xb + e + 8)); }
     const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
@@ -666,7 +657,6 @@ __device__ __forceinline__ void act8_pair(const RotQuantArgs& args, int64_t rA, 
       v[s][2 * k + 1] = make_float2(__uint_as_float(wa[k] & 0xFFFF0000u), __uint_as_float(wb[k] & 0xFFFF0000u));
     }
   }
-  after_load();
 
   if constexpr (LNMOD) {
     // layer norm over the K columns of each token (two passes over the registers: mean, then centered squares),
@@ -827,140 +817,18 @@ __device__ __forceinline__ void act8_pair(const RotQuantArgs& args, int64_t rA, 
   else act8_quant_store<ROT, PASSES, true>(args, v, inv, rA, storeB, warp, nwarps, nchunks, lane, tile, pack);
 }
 
-// One token pair per CTA, read straight from global memory.
-template <int ROT, int PASSES, bool LNMOD, int QMAX, bool SWIGLU>
-__global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_kernel(const RotQuantArgs args) {
-  // the GEMM that consumes these codes may be scheduled as soon as every CTA of this grid runs (its prologue then
-  // overlaps this kernel's tail; it waits for this grid's completion before reading anything)
-  grid_dep_launch();
-  extern __shared__ __align__(16) unsigned char act8_smem[];
-  __shared__ float red[2][act8::kMaxTeamWarps];
-  __shared__ float red_ln[2][2][act8::kMaxTeamWarps];   // layer-norm prologue: sums, then centered squares
-  const int64_t rA = 2 * static_cast<int64_t>(blockIdx.x);
-  const int64_t ld = SWIGLU ? 2 * static_cast<int64_t>(args.K) : args.K;   // SwiGLU rows are [gate | up], 2K wide
-  const __nv_bfloat16* xa = static_cast<const __nv_bfloat16*>(args.x) + rA * ld;
-  act8_pair<ROT, PASSES, LNMOD, QMAX, SWIGLU, false>(args, rA, xa, xa + ld, act8_smem + (threadIdx.x >> 5) * act8::kTileBytes,
-                                                     red, red_ln, [] {});
-}
-
-// Persistent form: CTA b walks the token pairs b, b + gridDim.x, ...  Each pair's two rows arrive in a shared-memory
-// stage by one bulk copy per row (cp.async.bulk, no multicast), tracked by an mbarrier; once every thread holds the
-// pair in registers the stage is refilled with the CTA's next pair, so that pair's load overlaps this pair's
-// rotation, quantization and stores.  The per-pair arithmetic is act8_pair's, so the outputs are the same bits as
-// act8_kernel's.  The stage wait is bounded (CQ_ERR_TIMEOUT, site 40); after a timeout the CTA waits a bounded time
-// for its copy in flight and returns.
-template <int ROT, int PASSES, bool LNMOD, int QMAX>
-__global__ void __launch_bounds__(act8::kMaxTeamWarps * 32) act8_staged_kernel(const RotQuantArgs args) {
-  grid_dep_launch();
-  extern __shared__ __align__(128) unsigned char act8_stage_smem[];
-  __shared__ float red[2][act8::kMaxTeamWarps];
-  __shared__ float red_ln[2][2][act8::kMaxTeamWarps];
-  __shared__ __align__(8) uint64_t stage_full;
-  __shared__ int abort_flag;
-  const int nwarps = blockDim.x >> 5;
-  const int64_t K = args.K;
-  const uint32_t row_bytes = static_cast<uint32_t>(2 * K);
-  unsigned char* stage = act8_stage_smem + nwarps * act8::kTileBytes;   // kTileBytes is a multiple of 128
-  const __nv_bfloat16* stage_a = reinterpret_cast<const __nv_bfloat16*>(stage);
-  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(args.x);
-  const int64_t npairs = (args.rows_pad + 1) / 2;
-  if (threadIdx.x == 0) {
-    mbar_init(&stage_full, 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-  // thread 0: the rows of pair p that exist (padding rows are not read) into the stage
-  auto fill = [&](int64_t p) {
-    const int64_t r = 2 * p;
-    const int live = (r < args.rows ? 1 : 0) + (r + 1 < args.rows ? 1 : 0);
-    fence_proxy_async_smem();   // the generic-proxy reads of the stage's previous pair come first
-    mbar_arrive_expect_tx(&stage_full, static_cast<uint32_t>(live) * row_bytes);
-    for (int i = 0; i < live; ++i)
-      bulk_load_g2s(smem_u32(stage + i * row_bytes), x + (r + i) * K, row_bytes, smem_u32(&stage_full));
-  };
-  if (threadIdx.x == 0 && blockIdx.x < npairs) fill(blockIdx.x);
-  uint32_t phase = 0;
-  for (int64_t p = blockIdx.x; p < npairs; p += gridDim.x) {
-    mbar_wait(&stage_full, phase, &abort_flag, 40);
-    __syncthreads();
-    if (abort_flag) {
-      if (threadIdx.x == 0) mbar_wait_drain(&stage_full, phase, act8::kDrainNs);
-      return;
-    }
-    phase ^= 1u;
-    // every thread loads its part of the pair from the stage into registers inside act8_pair; the barrier that
-    // frees the stage for the next pair sits between those loads and the pair's arithmetic
-    act8_pair<ROT, PASSES, LNMOD, QMAX, false, true>(
-        args, 2 * p, stage_a, stage_a + K, act8_stage_smem + (threadIdx.x >> 5) * act8::kTileBytes, red, red_ln,
-        [&]() {
-          __syncthreads();
-          if (threadIdx.x == 0 && p + gridDim.x < npairs) fill(p + gridDim.x);
-        });
-  }
-}
-
-// Kernel form of the per-token activation kernels for every later call in this process (cq_act_variant).
-static int g_act_variant = CQ_ACT_AUTO;
-
-int set_act_variant(int variant) {
-  if (variant != CQ_ACT_AUTO && variant != CQ_ACT_WAVES && variant != CQ_ACT_STAGED) return CQ_ERR_ARG;
-  g_act_variant = variant;
-  return CQ_OK;
-}
-
-// The staged form needs 16-byte aligned rows (bulk copies), plain bf16 rows (no SwiGLU pair of halves) and a stage
-// of at most 48 KB (K <= 12288), so that register-bound occupancy, not shared memory, limits its CTAs per SM.
-static bool act8_staged_ok(const RotQuantArgs& a, bool swiglu) {
-  if (g_act_variant != CQ_ACT_STAGED || swiglu) return false;
-  return a.K <= 12288 && (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 && (2 * static_cast<int64_t>(a.K)) % 16 == 0;
-}
-
-// CTAs of a persistent kernel that fit on the current device at once (SMs x resident CTAs per SM), looked up once
-// per (device, kernel, block size, shared memory)
-static int64_t act8_resident_ctas(const void* kernel, int threads, size_t smem) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int, size_t>, int64_t> cache;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, kernel, threads, smem);
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    const auto it = cache.find(key);
-    if (it != cache.end()) return it->second;
-  }
-  int sms = 0, per_sm = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
-  const int64_t n = static_cast<int64_t>(std::max(per_sm, 1)) * std::max(sms, 1);
-  std::lock_guard<std::mutex> lock(mu);
-  cache[key] = n;
-  return n;
-}
-
 template <int ROT, bool LNMOD = false, int QMAX = 127, bool SWIGLU = false>
 static cudaError_t launch_act8(const RotQuantArgs& a, cudaStream_t st) {
   // Three chunks per warp.  Measured on B200 at K = 3072 and 12288, M = 4096-65536: one or two chunks per warp
   // (more, smaller warps) were slower or equal, and so was a persistent variant that prefetched the next token
-  // pair into shared memory with per-lane cp.async copies while working on the current one.
+  // pair into shared memory (cp.async) while working on the current one.
   constexpr int kPasses = 3;
   const int nchunks = (a.K + 511) / 512;
   const int warps = (nchunks + kPasses - 1) / kPasses;
-  const size_t tiles = static_cast<size_t>(warps) * act8::kTileBytes;
-  if constexpr (!SWIGLU) {
-    if (act8_staged_ok(a, SWIGLU)) {
-      auto k = act8_staged_kernel<ROT, kPasses, LNMOD, QMAX>;
-      const size_t smem = tiles + 2 * 2 * static_cast<size_t>(a.K);
-      if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      const int64_t npairs = (a.rows_pad + 1) / 2;
-      const int64_t grid = std::min<int64_t>(npairs, act8_resident_ctas(reinterpret_cast<const void*>(k), warps * 32, smem));
-      k<<<static_cast<unsigned>(grid), warps * 32, smem, st>>>(a);
-      return cudaGetLastError();
-    }
-  }
+  const size_t smem = static_cast<size_t>(warps) * act8::kTileBytes;
   auto k = act8_kernel<ROT, kPasses, LNMOD, QMAX, SWIGLU>;
-  if (tiles > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tiles));
-  k<<<static_cast<unsigned>((a.rows_pad + 1) / 2), warps * 32, tiles, st>>>(a);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  k<<<static_cast<unsigned>((a.rows_pad + 1) / 2), warps * 32, smem, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -80,15 +80,6 @@ typedef enum {
                           operand's shared-memory traffic per SM and a deeper load ring                              */
 } cq_gemm_variant;
 
-/* Kernel forms of the per-token activation kernels (cq_rotquant CQ_ACT_INT8_ROW / CQ_ACT_INT4_ROW without SwiGLU,
- * and the activation step of the fused linears). */
-typedef enum {
-  CQ_ACT_AUTO = 0,    /* the library's choice (currently waves)                                                    */
-  CQ_ACT_WAVES = 1,   /* one CTA per token pair, reading its rows from global memory                               */
-  CQ_ACT_STAGED = 2   /* persistent CTAs; each token pair's rows arrive in shared memory by bulk copies issued while
-                         the CTA works on its previous pair (falls back to waves where its conditions do not hold)   */
-} cq_act_variant;
-
 /* Library version string, e.g. "cq_b200 0.1.0 sm_100a". */
 CQ_API const char* cq_version(void);
 /* Human-readable name of a cq_status code. */
@@ -99,12 +90,6 @@ CQ_API const char* cq_status_string(int status);
  * testing switch with no counterpart in the reference; it is process-wide and not synchronized with calls running
  * on other host threads.  Returns CQ_OK or CQ_ERR_ARG. */
 CQ_API int cq_set_gemm_variant(int variant);
-
-/* Select the kernel form of the per-token activation kernels for every later call in this process
- * (cq_act_variant; the default is CQ_ACT_AUTO).  Both forms run the same per-pair arithmetic, so codes, scales and
- * group sums agree to the last bit.  A tuning and testing switch with no counterpart in the reference; process-wide
- * and not synchronized with calls running on other host threads.  Returns CQ_OK or CQ_ERR_ARG. */
-CQ_API int cq_set_act_variant(int variant);
 
 /* Copy the device status word of the current device into status[0..1] (code, site) and clear it.
  * Synchronizes `stream`.  Returns CQ_OK or CQ_ERR_CUDA. */
