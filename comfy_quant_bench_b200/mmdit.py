@@ -18,7 +18,9 @@ library's kernels: the layer norm + modulation before the QKV and MLP-up linears
 in the GEMM epilogues (``ops.w4a8_affine_linear_op``), the q/k RMSNorm + rotary embedding + joint attention layout as
 one kernel (``ops.qkv_rmsnorm_rope``), writing q, k, v token-major so that the attention's output is already the
 [tokens, hidden] rows of the output projection (``ops.heads_to_rows`` copies it when the attention returns head-major
-memory); ``fused_glue=False`` runs them as torch ops instead.  Weights are drawn N(0, 0.02) per linear from a
+memory); ``fused_glue=False`` runs them as torch ops instead.  The text stream's linears (256 tokens: few output
+tiles, latency-bound) run on a second CUDA stream that joins the main one only at the joint attention, so they
+overlap the image stream's GEMMs (``text_side_stream``).  Weights are drawn N(0, 0.02) per linear from a
 seeded generator, quantized on the device with the library's weight kernel, and only the packed form is kept.
 
 ``MMDiT.step(..., reference=True)`` runs the same step with every linear replaced by a torch fp32 product of the
@@ -58,6 +60,9 @@ class MMDiTConfig:
     token_major_qkv: bool = True       # with fused_glue: q, k, v in [tokens, heads, D] memory, passed to the attention
                                        # as strided views, whose output then is the [tokens, hidden] rows of the output
                                        # projection (False: head-major q, k, v and the head-to-rows copy)
+    text_side_stream: bool = True      # with fused_glue and token_major_qkv: the text stream's linears on a second CUDA
+                                       # stream, joined only at the attention, so its few-tile 256-token GEMMs can run
+                                       # beside the image stream's GEMMs instead of after them
 
     @property
     def head_dim(self) -> int:
@@ -181,6 +186,8 @@ class MMDiT:
         d = cfg.head_dim
         self.rope_txt = _rope_table(cfg.txt_tokens, d, self.device)
         self.rope_img = _rope_table(cfg.img_tokens, d, self.device, offset=cfg.txt_tokens)
+        self._side = None     # the text stream's CUDA stream (text_side_stream)
+        self._qkv_bufs = None # two token-major q, k, v sets, alternating by block (text_side_stream)
 
     # ---- per-linear dispatch (kernel path or torch reference) ----
     @staticmethod
@@ -250,8 +257,67 @@ class MMDiT:
         if c.batched_modulation and c.fused_glue and self.mod_all is not None and not reference:
             # [1, 2 * blocks * 6 * hidden]: one activation kernel and one weight stream for all modulation linears
             mods = self.mod_all(temb_act).split(6 * c.hidden, dim=-1)
+        if self._two_streams(reference):
+            return self._step_two_streams(img, txt, temb_act, mods)
         for i, blk in enumerate(self.blocks):
             img, txt = self._block(blk, img, txt, temb_act, reference, None if mods is None else mods[2 * i:2 * i + 2])
+        return img, txt
+
+    def _two_streams(self, reference: bool) -> bool:
+        c = self.cfg
+        return c.text_side_stream and c.fused_glue and c.token_major_qkv and c.epilogue_gated and c.epilogue_gelu \
+            and not reference
+
+    def _step_two_streams(self, img: torch.Tensor, txt: torch.Tensor, temb_act: torch.Tensor, mods):
+        """The fused step with the text stream's work on a second stream.  Per block the text stream waits for the
+        main stream once (the joint attention's output) and the main stream waits for the text stream once (the
+        text q, k, v before the attention).  q, k, v live in two persistent buffer sets used by alternate blocks:
+        block i + 2 rewrites block i's set only after the attention of block i, which both streams are ordered
+        after.  The attention output is marked as used by the text stream, so the allocator does not hand its
+        memory out again before the text stream has read it.  The step ends with the main stream waiting for the
+        text stream."""
+        c = self.cfg
+        h, nh, d = c.hidden, c.heads, c.head_dim
+        main = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        side = self._side
+        st_txt, st_img = txt.shape[0], img.shape[0]
+        s_all = st_txt + st_img
+        if self._qkv_bufs is None or self._qkv_bufs[0][0].shape[2] != s_all:
+            self._qkv_bufs = [tuple(torch.empty(1, s_all, nh, d, dtype=torch.bfloat16, device=self.device).transpose(1, 2)
+                                    for _ in range(3)) for _ in range(2)]
+        if mods is None:
+            mods = []
+            for si, st in self.blocks:
+                mods += [self._mod(si, temb_act, False), self._mod(st, temb_act, False)]
+        side.wait_stream(main)              # the step's inputs and the modulation outputs
+        for i, (si, st) in enumerate(self.blocks):
+            q, k, v = self._qkv_bufs[i % 2]
+            mi, mt = mods[2 * i].chunk(6, dim=-1), mods[2 * i + 1].chunk(6, dim=-1)
+            with torch.cuda.stream(side):
+                y = st.qkv.op(txt, "plain", shift=mt[0], scale=mt[1])
+                ops.qkv_rmsnorm_rope(y, st.q_norm, st.k_norm, self.rope_txt, q, k, v, 0, eps=1e-6)
+            y = si.qkv.op(img, "plain", shift=mi[0], scale=mi[1])
+            ops.qkv_rmsnorm_rope(y, si.q_norm, si.k_norm, self.rope_img, q, k, v, st_txt, eps=1e-6)
+            main.wait_stream(side)
+            o = F.scaled_dot_product_attention(q, k, v)
+            if o.transpose(1, 2).is_contiguous():
+                a = o.transpose(1, 2).reshape(s_all, h)
+            else:
+                a = torch.empty(s_all, h, dtype=torch.bfloat16, device=self.device)
+                ops.heads_to_rows(o, [a], 0, h)
+            a.record_stream(side)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                x = st.out.op(a[:st_txt], "gated", residual=txt, gate=mt[2])
+                f = st.fc1.op(x, "gelu", shift=mt[3], scale=mt[4])
+                txt = st.fc2.op(f, "gated", residual=x, gate=mt[5])
+            x = si.out.op(a[st_txt:], "gated", residual=img, gate=mi[2])
+            f = si.fc1.op(x, "gelu", shift=mi[3], scale=mi[4])
+            img = si.fc2.op(f, "gated", residual=x, gate=mi[5])
+        main.wait_stream(side)
+        txt.record_stream(main)
         return img, txt
 
     def block_errors(self, img: torch.Tensor, txt: torch.Tensor, temb: torch.Tensor) -> list[float]:

@@ -57,16 +57,18 @@ def test_mmdit_step_is_deterministic_and_graph_capturable(mmdit):
 
 def test_mmdit_layout_and_modulation_forms_are_bit_identical(mmdit):
     """The joined modulation product (one activation kernel and one weight stream for every block's modulation
-    linears) and the token-major attention layout change only how the work is launched: the step output equals the
-    per-stream, head-major form bit for bit."""
+    linears), the token-major attention layout and the text stream's work on a second CUDA stream change only how
+    the work is launched: the step output equals the per-stream, head-major, one-stream form bit for bit."""
     from dataclasses import replace
     cfg = mmdit.MMDiTConfig(blocks=3, hidden=512, heads=4, mlp=1024, img_tokens=300, txt_tokens=40)
     model = mmdit.MMDiT(cfg, device="cuda", seed=9)
     img, txt, temb = model.inputs(seed=10)
     base = model.step(img, txt, temb)
     outs = []
-    for batched, token_major in ((False, True), (True, False), (False, False)):
-        model.cfg = replace(cfg, batched_modulation=batched, token_major_qkv=token_major)
+    assert cfg.text_side_stream
+    for batched, token_major, side in ((False, True, True), (True, True, False), (True, False, False),
+                                       (False, False, False)):
+        model.cfg = replace(cfg, batched_modulation=batched, token_major_qkv=token_major, text_side_stream=side)
         outs.append(model.step(img, txt, temb))
     model.cfg = cfg
     torch.cuda.synchronize()
