@@ -583,7 +583,7 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
                           residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
                           shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
                           group_size: int = 128, convrot_groupsize: int = 0, eps: float = 1e-6,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
+                          out: torch.Tensor | None = None, split_k: bool = True) -> torch.Tensor:
     """A DiT-block linear with the elementwise step after it done in the GEMM's epilogue.
 
     With y the bf16 output of ``w4a8_affine_linear`` (or, when ``shift`` and the modulation ``scale`` are given, of
@@ -594,7 +594,9 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
       ``out_op="gated"``:  ``torch.addcmul(residual, gate, y)``         (the gated residual after the attention
                            output and MLP-down linears; ``gate`` [N] or [1, N], ``residual`` [..., N] bf16)
     ``out`` (bf16, contiguous, the output's shape) receives the result if given; it may be ``residual`` itself
-    (an in-place residual update)."""
+    (an in-place residual update).  ``split_k=False`` gives the call only the base workspace, so a GEMM with few
+    output tiles keeps one CTA per tile instead of splitting K over more CTAs (for a linear that runs beside other
+    work on another stream, where the idle SMs are not idle)."""
     if group_size != 128:
         raise ValueError("the W4A8 affine kernel supports group_size 128")
     k = x.shape[-1]
@@ -605,7 +607,7 @@ def w4a8_affine_linear_op(x: torch.Tensor, qweight: torch.Tensor, wscale: torch.
     x2 = _as2d(x)
     m = x2.shape[0]
     op, keep, out, sh, sc = _op_args(out_op, residual, gate, shift, scale, out, m, n, k, dev)
-    ws = _workspace(m, k, dev, n)
+    ws = _workspace(m, k, dev, n if split_k else None)
     wp, wn = _ws_ptr(ws)
     _lib.call("cq_linear_w4a8_op", _ptr(x2), m, k, n, _check_rot(convrot_groupsize), _ptr(sh), _ptr(sc), float(eps),
               _ptr(qweight.contiguous()), _ptr(wscale.to(torch.bfloat16).contiguous()), _ptr(zeros_prepared),

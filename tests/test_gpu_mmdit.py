@@ -58,9 +58,16 @@ def test_mmdit_step_is_deterministic_and_graph_capturable(mmdit):
 def test_mmdit_layout_and_modulation_forms_are_bit_identical(mmdit):
     """The joined modulation product (one activation kernel and one weight stream for every block's modulation
     linears), the token-major attention layout and the text stream's work on a second CUDA stream change only how
-    the work is launched: the step output equals the per-stream, head-major, one-stream form bit for bit."""
+    the work is launched: with the text linears' K split fixed, the step output equals the per-stream, head-major,
+    one-stream form bit for bit."""
     from dataclasses import replace
-    cfg = mmdit.MMDiTConfig(blocks=3, hidden=512, heads=4, mlp=1024, img_tokens=300, txt_tokens=40)
+    for text_split_k in (False, True):
+        _check_launch_forms(mmdit, replace, text_split_k)
+
+
+def _check_launch_forms(mmdit, replace, text_split_k):
+    cfg = mmdit.MMDiTConfig(blocks=3, hidden=512, heads=4, mlp=1024, img_tokens=300, txt_tokens=40,
+                            text_split_k=text_split_k)
     model = mmdit.MMDiT(cfg, device="cuda", seed=9)
     img, txt, temb = model.inputs(seed=10)
     base = model.step(img, txt, temb)
