@@ -397,6 +397,17 @@ __device__ __forceinline__ void sts_bf16_pair(uint32_t a0, uint32_t a1, float v0
       ::"r"(a0), "r"(a1), "f"(v0), "f"(v1) : "memory");
 }
 
+// bf16 bits of lo (low half) and hi (high half), each rounded to nearest even
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+__device__ __forceinline__ void sts_b32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // The gated residual of two tokens of one output column, in packed bf16: o_i = bf16(r_i + g * bf16(v_i)) with one
 // rounding of the exact value (fma.rn.bf16x2); r0, r1 are the residuals' bf16 bits, gate2 the gate's bits in both
 // halves.  Against torch's addcmul on bf16 tensors (an fp32 result rounded to bf16) it can differ only where the fp32
