@@ -386,17 +386,6 @@ __device__ __forceinline__ void st_bf16_pair_ordered(__nv_bfloat16* p0, __nv_bfl
       ::"l"(p0), "l"(p1), "f"(v0), "f"(v1) : "memory");
 }
 
-// v0 -> shared address a0 and v1 -> a1 as bf16 (round to nearest even), one paired conversion
-__device__ __forceinline__ void sts_bf16_pair(uint32_t a0, uint32_t a1, float v0, float v1) {
-  asm volatile(
-      "{\n\t.reg .b32 d;\n\t.reg .b16 lo, hi;\n\t"
-      "cvt.rn.bf16x2.f32 d, %3, %2;\n\t"
-      "mov.b32 {lo, hi}, d;\n\t"
-      "st.shared.b16 [%0], lo;\n\t"
-      "st.shared.b16 [%1], hi;\n\t}"
-      ::"r"(a0), "r"(a1), "f"(v0), "f"(v1) : "memory");
-}
-
 // bf16 bits of lo (low half) and hi (high half), each rounded to nearest even
 __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
   uint32_t d;

@@ -713,6 +713,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             const int owner = kPair ? (e & ~1) : e;
             unsigned short* ost = reinterpret_cast<unsigned short*>(smem + P::kOutStage + owner * P::kOutWarpBytes);
             const uint32_t ost_lane = smem_u32(ost) + (kPair ? 64u * (e & 1) : 0u) + 2u * lane;
+            // plain and GELU outputs leave as 32-bit stores of two adjacent columns: lanes 2i and 2i + 1 swap one
+            // packed token pair, then the even lane writes both columns of the first token and the odd lane both
+            // columns of the second (half the shared-memory store instructions of one 16-bit store per element)
+            const uint32_t odd = lane & 1u;
+            const uint32_t pair_sel = odd ? 0x3276u : 0x5410u;
+            const uint32_t ost_pair = ost_lane - 2u * odd + odd * kRow;
             const bool issuer = !kPair || (e & 1) == 0;
             const int x0 = nt * kBW + (kPair ? (quad & 2) : quad) * 32;
             const int pr = e >> 1;
@@ -772,8 +778,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
                                  rres[r + 2], rres[r + 3]);
                 } else {
                   const float2 v01 = out_apply2<kOp>(u01), v23 = out_apply2<kOp>(u23);
-                  sts_bf16_pair(ost_lane + (4 * j4) * kRow, ost_lane + (4 * j4 + 1) * kRow, v01.x, v01.y);
-                  sts_bf16_pair(ost_lane + (4 * j4 + 2) * kRow, ost_lane + (4 * j4 + 3) * kRow, v23.x, v23.y);
+                  const uint32_t b01 = bf16x2_bits(v01.x, v01.y), b23 = bf16x2_bits(v23.x, v23.y);
+                  const uint32_t r01 = __shfl_xor_sync(0xffffffffu, b01, 1), r23 = __shfl_xor_sync(0xffffffffu, b23, 1);
+                  sts_b32(ost_pair + (4 * j4) * kRow, prmt(b01, r01, pair_sel));
+                  sts_b32(ost_pair + (4 * j4 + 2) * kRow, prmt(b23, r23, pair_sel));
                 }
               }
               fence_proxy_async_smem();
